@@ -1,0 +1,290 @@
+/*
+ * kvm.h -- C ABI of libkvm, a B200-native (sm_100a) implementation of
+ * KVMem's per-step KV reselection path:
+ *
+ *     score every stored 128-token block against the captured query
+ *  -> select the top-k blocks within the budget (sinks pinned, mandatory
+ *     blocks newest-first, ties to the higher block id)
+ *  -> diff the selection against the resident window (KvMemPlan) and lay the
+ *     window out chronologically (slot i = i-th selected block)
+ *  -> move retained blocks in place and gather + quantize the newly selected
+ *     F16 K/V blocks into ggml q8_0 / q4_0 / q5_0 rows of the window.
+ *
+ * Plain C types only; every pointer is a host pointer unless its name starts
+ * with `d_` (device) or the comment says "host or device".  All calls return
+ * a kvm_status and never throw.  Calls that take a `stream` are
+ * stream-ordered and do not block the host, except where noted.  One session
+ * serves one sequence on one device; sessions are independent and may be
+ * used from different threads; one session is single-threaded.
+ *
+ * Reference interfaces this ABI replaces (paths in CrKcel/kvmem-llama.cpp):
+ *   - llama_memory_kvmem::score_retrieval        src/adapter/llama-memory-kvmem.cpp:2869-2916
+ *   - KvMemStore::pick_topk_blocks(mandatory)    kvmem/src/host/kvmem_store.cpp:357-359, :482-623
+ *   - KvMemStore::set_selection -> KvMemPlan     kvmem/src/host/kvmem_store.cpp:758-882
+ *   - layout_gpu_slots_by_orig_pos               src/adapter/llama-memory-kvmem.cpp:931-1254
+ *   - write_block_to_gpu / kvmem_stagein_*       src/adapter/llama-memory-kvmem.cpp:2726-2791,
+ *                                                src/adapter/llama-kvmem-stagein.h:12-62
+ *   - RawKvStore mean-K summaries                kvmem/src/host/raw_kv_store.cpp:204-223, :674-720, :976-1043
+ */
+#ifndef KVM_H
+#define KVM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVM_ABI_VERSION 1
+
+typedef struct kvm_session kvm_session;
+/* A cudaStream_t passed as an opaque handle (NULL = legacy default stream). */
+typedef void *kvm_stream;
+
+typedef enum kvm_status {
+    KVM_OK = 0,
+    KVM_EINVAL = 1,    /* bad argument or configuration (std::invalid_argument) */
+    KVM_ENOMEM = 2,    /* device or pinned allocation failed */
+    KVM_ECUDA = 3,     /* CUDA runtime error; see kvm_last_error */
+    KVM_ETIMEOUT = 4,  /* bounded host wait or device wait ran out */
+    KVM_ESTATE = 5,    /* call out of order (e.g. stage-in before a diff) */
+    KVM_EDEVICE = 6    /* a kernel reported an error flag (bad index, timeout) */
+} kvm_status;
+
+/* ggml_type ids of the window cache formats (ggml.h enum ggml_type). */
+typedef enum kvm_type {
+    KVM_TYPE_F16 = 1,
+    KVM_TYPE_Q4_0 = 2,
+    KVM_TYPE_Q5_0 = 6,
+    KVM_TYPE_Q8_0 = 8
+} kvm_type;
+
+/* Block tiers, kvmem/include/kvmem/kvmem_store.hpp:31 (enum class KvTier). */
+typedef enum kvm_tier { KVM_TIER_GPU = 0, KVM_TIER_CPU = 1, KVM_TIER_SSD = 2 } kvm_tier;
+
+/*
+ * Session configuration: the subset of KvMemStoreConfig
+ * (kvmem/include/kvmem/kvmem_store.hpp:231-327) and llama_kvmem_params
+ * (src/adapter/llama-kvmem-hooks.h:19-39) that the reselection path reads.
+ */
+typedef struct kvm_config {
+    uint32_t block_tokens;     /* --kvmem-block-tokens (128) */
+    uint32_t select_budget;    /* --kvmem-budget, tokens; budget blocks = budget / block_tokens */
+    uint32_t gen_reserve;      /* --kvmem-gen-reserve, tokens; window slots = ceil((budget+gen)/bt) */
+    uint32_t sink_blocks;      /* always-kept prefix blocks (make_runtime_cfg maps 0 tokens -> 1) */
+    uint32_t recent_blocks;    /* always-kept suffix blocks (0 = literal none) */
+    uint32_t n_layer;          /* attention layers owned by this session */
+    uint32_t n_head_kv;
+    uint32_t head_dim;
+    uint32_t n_head_q;
+    uint32_t max_blocks;       /* block-table capacity (<= 65536) */
+    int32_t  type_k;           /* kvm_type of the window K cache */
+    int32_t  type_v;           /* kvm_type of the window V cache */
+    uint32_t optimize_stage_in;        /* 0 = reload every selected block (ablation) */
+    uint32_t immutable_source_k;       /* KvMemStoreConfig::immutable_source_k */
+    uint32_t immutable_refresh_remaps;
+    uint32_t reserved0;
+    uint64_t immutable_refresh_abs_delta_tokens;
+    uint64_t immutable_max_baked_position;
+    uint64_t staging_bytes;    /* HBM ring for host-resident sources; 0 = 256 MiB */
+} kvm_config;
+
+/* Fill `cfg` with the reference defaults (kvmem_store.hpp:231-327 and the
+ * adapter's make_runtime_cfg, llama-memory-kvmem.cpp:282-317). */
+void kvm_config_default(kvm_config *cfg);
+
+/*
+ * F16 K/V of the stored history (what RawKvStore keeps on the host).
+ * Element (layer l, block b, token t, channel e) of K is at byte offset
+ *     l*layer_stride + b*block_stride + t*row_stride + 2*e
+ * from `k` (same for V).  `location` says whether k/v are device (HBM)
+ * pointers or pinned host pointers (cudaHostAlloc / cudaHostRegister).
+ */
+typedef enum kvm_location { KVM_LOC_DEVICE = 0, KVM_LOC_HOST = 1 } kvm_location;
+typedef struct kvm_source {
+    const void *k;
+    const void *v;
+    uint64_t layer_stride;
+    uint64_t block_stride;
+    uint64_t row_stride;
+    int32_t  location;
+    int32_t  reserved0;
+} kvm_source;
+
+/*
+ * The bounded window (llama.cpp KV cache tensors, owned by the caller).
+ * d_k[l] / d_v[l] are device base pointers of layer l's K / V cache; token t
+ * of slot s lives at base + (s*block_tokens + t) * ggml_row_size(type, E).
+ * The arrays themselves are host arrays of n_layer pointers.
+ */
+typedef struct kvm_window {
+    void *const *d_k;
+    void *const *d_v;
+} kvm_window;
+
+/* KvMemPlan plus the chronological slot layout, as host arrays.  Arrays are
+ * caller-owned with capacity `capacity` entries (>= max_blocks); NULL arrays
+ * are skipped.  Semantics follow kvmem_store.hpp:108-124. */
+typedef struct kvm_plan {
+    uint32_t capacity;
+    uint32_t n_selected;                 /* selected blocks (ascending ids) */
+    uint32_t *selected;                  /* slot i holds selected[i] */
+    uint32_t n_stage_in;
+    uint32_t *stage_in;
+    uint32_t n_stage_out;
+    uint32_t *stage_out;
+    uint32_t n_remaps;                   /* == n_selected */
+    uint32_t *rm_block_id;
+    uint32_t *rm_n_tokens;
+    int32_t  *rm_from_base;
+    int32_t  *rm_to_base;
+    uint8_t  *rm_working_k_resident;
+    uint8_t  *rm_skip;
+    uint8_t  *rm_raw_refresh;
+    uint32_t total_window_tokens;
+    uint32_t selection_overlap_blocks;
+    uint32_t gpu_reused_blocks;
+    uint32_t retained_position_stable;
+    uint32_t retained_position_moved;
+    uint32_t n_moves;                    /* resident blocks moved to a new slot */
+    uint32_t *mv_block;
+    int32_t  *mv_from;
+    int32_t  *mv_to;
+    uint32_t n_cold;                     /* blocks gathered + quantized from the source */
+    uint32_t *cold_block;
+    int32_t  *cold_to;
+} kvm_plan;
+
+/* Stage timers of the last step (CUDA events), in milliseconds; field names
+ * follow the reference's KVMEM_RETR_SUM line (llama-memory-kvmem.cpp:2918-2936). */
+typedef struct kvm_timings {
+    float score_ms;
+    float plan_ms;      /* select + diff */
+    float layout_ms;    /* in-place moves of retained blocks */
+    float set_ms;       /* gather + quantize stage-in (incl. H2D for host sources) */
+    float total_ms;
+} kvm_timings;
+
+/* ------------------------------------------------------------ sessions -- */
+
+/* Allocates the session's device state on `device` (summaries, block table,
+ * plan buffers, staging ring).  Replaces the adapter-owned state built in
+ * llama_memory_kvmem's constructor (llama-memory-kvmem.cpp:430-600). */
+kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **out);
+void kvm_session_destroy(kvm_session *s);
+/* Last error message of this session (never NULL). */
+const char *kvm_last_error(const kvm_session *s);
+/* Window slots: ceil((select_budget + gen_reserve) / block_tokens)
+ * (kvmem_compute_pool, llama-memory-kvmem.cpp:363-426, without the VRAM cap). */
+uint32_t kvm_window_slots(const kvm_session *s);
+uint32_t kvm_block_count(const kvm_session *s);
+/* ggml_row_size(type, n_embd) */
+uint64_t kvm_row_bytes(int32_t type, uint32_t n_embd);
+
+/* --------------------------------------------------------- block table -- */
+
+/* KvMemStore::register_append (kvmem_store.cpp:179-205): extend the trailing
+ * partial block, then start new blocks.  `resident` = 0: the tokens exist
+ * only in the stored history (tier CPU).  `resident` = 1: the model wrote
+ * them into the window (tier GPU); new blocks take the next free window
+ * slots (alloc_slot, llama-memory-kvmem.cpp:693-700): the lowest slots not
+ * holding a block, which requires the previous step's plan to have been read
+ * with kvm_get_plan.  The device block table is updated on `stream`. */
+kvm_status kvm_register_append(kvm_session *s, kvm_stream stream, uint32_t n_new_tokens,
+                               int resident);
+/* KvMemStore::clear_working_set + drop every window slot: the next step
+ * treats the window as empty (cold).  Stream-ordered on `stream`. */
+kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream);
+
+/* ------------------------------------------------- summaries and query -- */
+
+/*
+ * RawKvStore mean-K statistics for `n` blocks of one layer: `sums` holds
+ * [n][n_head_kv*head_dim] F32 token sums, `counts` [n] the tokens behind each
+ * sum (0 = no statistics).  host or device pointers.  The mean is computed on
+ * read as sum * (1.0f / count) exactly like RawKvStore::mean_k.
+ */
+kvm_status kvm_upload_summaries(kvm_session *s, kvm_stream stream, uint32_t layer,
+                                uint32_t block0, uint32_t n, const float *sums,
+                                const uint32_t *counts);
+/* GPU producer of the same statistics from F16 K rows of the source
+ * (RawKvStore::add_mean_f32 over F16->F32 values, ordered token sum).  The
+ * source must be device-resident.  Counts are the blocks' n_tokens. */
+kvm_status kvm_summarize(kvm_session *s, kvm_stream stream, uint32_t layer0,
+                         uint32_t n_layers, uint32_t block0, uint32_t n,
+                         const kvm_source *src);
+/*
+ * Captured query (harvest_from_host 'q', llama-memory-kvmem.cpp:2157-2173):
+ * q_sum [n_layer][n_head_q*head_dim] F32 sums of pre-RoPE Q (host or device
+ * pointer), q_count [n_layer] host array of tokens summed (0 = layer has no
+ * query and does not vote).
+ */
+kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum,
+                         const uint32_t *q_count);
+
+/* ----------------------------------------------------- reselection step -- */
+
+/* Scores of every block (f64, score_retrieval); optional copy to d_scores. */
+kvm_status kvm_score(kvm_session *s, kvm_stream stream, double *d_scores);
+/* Per-layer score terms for layers [layer0, layer0+n_layers) of this session,
+ * written to d_terms[(layer0 + i) * ldt + b] = layer_sum / n_head_kv (0 for a
+ * layer without query).  Used to split one session's layers across GPUs. */
+kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0,
+                           uint32_t n_layers, double *d_terms, uint32_t ldt);
+/* Install block scores from summed terms: score = acc / n_active (0 for blocks
+ * without data).  d_acc [block_count] f64 device; n_active = layers with a
+ * query across all partitions.  KvMemStore::set_retrieval_scores. */
+kvm_status kvm_set_scores_from_sum(kvm_session *s, kvm_stream stream, const double *d_acc,
+                                   uint32_t n_active);
+/* Install externally computed scores (host or device pointer, f64 [n]). */
+kvm_status kvm_set_scores(kvm_session *s, kvm_stream stream, const double *scores,
+                          uint32_t n);
+/* pick_topk_blocks(mandatory): mandatory is a host array in reference order
+ * (walked from its end, newest first). */
+kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,
+                      uint32_t n_mandatory);
+/* Use a caller-chosen selection instead of kvm_select (any order, duplicates
+ * and out-of-range ids are dropped like set_selection does). */
+kvm_status kvm_set_selection_ids(kvm_session *s, kvm_stream stream, const uint32_t *ids,
+                                 uint32_t n);
+/* set_selection + chronological layout on the device; `force_raw_refresh`
+ * as in KvMemStore::set_selection. */
+kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh);
+/* Moves retained blocks to their new slots in place, then gathers and
+ * quantizes the cold blocks from `src` into the window.  For a host source
+ * this reads the plan back (one bounded host wait) and overlaps the H2D of
+ * the cold blocks with the quantize kernel through the HBM staging ring. */
+kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
+                       const kvm_window *win);
+/* score -> select -> diff -> stage-in in one call. */
+kvm_status kvm_step(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,
+                    uint32_t n_mandatory, const kvm_source *src, const kvm_window *win);
+
+/* Bounded host wait for all work queued on `stream`; checks the device error
+ * flags.  KVM_ETIMEOUT if not done within timeout_ms. */
+kvm_status kvm_wait(kvm_session *s, kvm_stream stream, uint32_t timeout_ms);
+/* Copy the last plan to host arrays (waits on `stream`, bounded by
+ * timeout_ms) and refresh the host view of window slots. */
+kvm_status kvm_get_plan(kvm_session *s, kvm_stream stream, kvm_plan *plan, uint32_t timeout_ms);
+/* Copy scores (f64 [n]) to a host array after a wait. */
+kvm_status kvm_get_scores(kvm_session *s, kvm_stream stream, double *scores, uint32_t n,
+                          uint32_t timeout_ms);
+/* Stage timers of the last kvm_step (needs a completed step). */
+kvm_status kvm_get_timings(kvm_session *s, kvm_timings *t);
+/* Number of kernels libkvm launched on this session since creation. */
+uint64_t kvm_kernel_launches(const kvm_session *s);
+
+/* -------------------------------------------------- standalone kernels -- */
+
+/* Quantize n_rows F16 rows of n_embd values (device pointers, rows
+ * contiguous) to `type` rows at d_dst -- the stage-in kernel on a plain
+ * row range.  Returns KVM_EINVAL for unsupported widths. */
+kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
+                             uint64_t n_rows, uint32_t n_embd, void *d_dst);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVM_H */

@@ -1,0 +1,213 @@
+// kvm_internal.cuh -- shared device helpers and session layout of libkvm.
+//
+// sm_100a only.  No fast-math: every float/double operation that must match
+// the reference's CPU arithmetic bit for bit uses an explicit _rn intrinsic
+// so nvcc cannot contract it into an FMA.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/kvm.h"
+
+namespace kvm {
+
+// ---------------------------------------------------------------- limits --
+constexpr uint32_t kMaxBlocks = 65536;      // block-table capacity per session
+constexpr uint32_t kMaxLayers = 256;
+constexpr uint32_t kMaxHeadDim = 1024;
+constexpr uint32_t kMaxHeadsKv = 64;
+
+// Device status word bits (session->d_status).
+constexpr uint32_t kErrTimeout = 1u << 0;   // a bounded mbarrier wait gave up
+constexpr uint32_t kErrIndex = 1u << 1;     // an index outside the session tables
+constexpr uint32_t kErrSlot = 1u << 2;      // a slot outside the window
+constexpr uint32_t kErrConfig = 1u << 3;    // a launch saw an impossible configuration
+
+// Bounded waits: give up after this many nanoseconds of %globaltimer.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ------------------------------------------------------------- plan header --
+// Counts written by the select / diff kernels (device), read back by
+// kvm_get_plan.  Field order is part of the D2H copy layout.
+struct PlanHeader {
+    uint32_t n_selected;
+    uint32_t n_stage_in;
+    uint32_t n_stage_out;
+    uint32_t n_remaps;
+    uint32_t total_window_tokens;
+    uint32_t selection_overlap_blocks;
+    uint32_t gpu_reused_blocks;
+    uint32_t retained_position_stable;
+    uint32_t retained_position_moved;
+    uint32_t n_moves;
+    uint32_t n_cold;
+    uint32_t n_blocks;          // block count the plan was computed for
+    uint32_t pad[4];
+};
+static_assert(sizeof(PlanHeader) == 64, "PlanHeader");
+
+// Device block table (KvMemBlock fields used by the path), SoA.
+struct BlockTable {
+    uint32_t *n_tokens;
+    uint8_t  *tier;
+    int32_t  *gpu_slot;
+    int64_t  *baked_pos;
+    uint32_t *remap_count;
+    uint64_t *remap_abs_delta;
+    uint8_t  *in_ws;
+};
+
+// Device plan arrays (capacity max_blocks each).
+struct PlanArrays {
+    PlanHeader *hdr;
+    uint32_t *selected;
+    uint32_t *stage_in;
+    uint32_t *stage_out;
+    uint32_t *rm_block_id;
+    uint32_t *rm_n_tokens;
+    int32_t  *rm_from_base;
+    int32_t  *rm_to_base;
+    uint8_t  *rm_wkr;
+    uint8_t  *rm_skip;
+    uint8_t  *rm_raw;
+    uint32_t *mv_block;
+    int32_t  *mv_from;
+    int32_t  *mv_to;
+    uint32_t *cold_block;
+    int32_t  *cold_to;
+};
+
+// ------------------------------------------------------------ PTX wrappers --
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: false after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// Bulk global -> shared copy completing on `bar` (bytes % 16 == 0, both
+// addresses 16-byte aligned).  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bulk shared -> global copy in the current bulk group.
+__device__ __forceinline__ void bulk_s2g(void *gmem_dst, const void *smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void set_status(uint32_t *status, uint32_t bits) {
+    if (status) atomicOr(status, bits);
+}
+
+// ------------------------------------------------------------ block scans --
+// Exclusive prefix sum over one value per thread of a block of `NT` threads
+// (NT multiple of 32, <= 1024).  Returns the exclusive prefix; *total gets the
+// block total.  `scratch` holds >= NT/32 + 1 uint32 in shared memory.
+template <int NT>
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *scratch,
+                                                         uint32_t *total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) scratch[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        constexpr int NW = NT / 32;
+        uint32_t w = lane < NW ? scratch[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < NW) scratch[lane] = w;      // inclusive warp totals
+        if (lane == NW - 1) scratch[NW] = w;   // block total
+    }
+    __syncthreads();
+    const uint32_t warp_prefix = warp > 0 ? scratch[warp - 1] : 0u;
+    *total = scratch[NT / 32];
+    __syncthreads();
+    return warp_prefix + x - v;
+}
+
+// Block-wide sum of one value per thread (all threads get the result).
+template <int NT>
+__device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t *scratch) {
+    uint32_t total;
+    (void)block_exclusive_scan<NT>(v, scratch, &total);
+    return total;
+}
+
+}  // namespace kvm

@@ -1,0 +1,173 @@
+// kvm_kernels.h -- launch arguments and launchers of libkvm's kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kvm_internal.cuh"
+
+namespace kvm {
+
+constexpr int kStageinThreads = 256;
+constexpr int kStageinStages = 4;
+constexpr int kPermuteThreads = 256;
+constexpr int kSelectThreads = 1024;
+constexpr int kDiffThreads = 1024;
+
+// ------------------------------------------------------------- stage-in --
+struct StageinArgs {
+    // work list: items [item0, item0 + n) of cold_block / cold_to
+    const uint32_t *cold_block;
+    const int32_t *cold_to;
+    const uint32_t *n_items_dev;   // device count (NULL: use n_items_host)
+    uint32_t n_items_host;
+    uint32_t item0;
+    uint32_t max_items;
+    uint32_t src_by_item;          // 1: source index = item - item0 (staging ring)
+    uint32_t n_kv;                 // 2: K and V tasks; 1: K only
+    // F16 source
+    const uint8_t *src_k;
+    const uint8_t *src_v;
+    uint64_t layer_stride;
+    uint64_t item_stride;
+    uint64_t row_stride;
+    // block table and window
+    const uint32_t *n_tokens;
+    uint32_t max_blocks;
+    uint8_t *const *dst_k;         // device array [n_layer]
+    uint8_t *const *dst_v;
+    uint32_t n_layer;
+    uint32_t block_tokens;
+    uint32_t n_embd;
+    uint32_t n_slots;
+    int32_t type_k;
+    int32_t type_v;
+    uint32_t row_bytes_k;
+    uint32_t row_bytes_v;
+    uint32_t rows_per_tile;
+    uint32_t tile_in_bytes;
+    uint32_t tile_out_bytes;
+    uint32_t bulk_store;
+    uint32_t *status;
+};
+
+uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens);
+size_t stagein_smem_bytes(const StageinArgs &a);
+cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap);
+
+// -------------------------------------------------------------- permute --
+struct PermuteArgs {
+    const uint32_t *n_moves_dev;
+    const uint32_t *mv_block;
+    const int32_t *mv_from;
+    const int32_t *mv_to;
+    uint32_t max_moves;
+    const uint32_t *n_tokens;
+    uint32_t max_blocks;
+    uint8_t *const *dst_k;
+    uint8_t *const *dst_v;
+    uint32_t n_layer;
+    uint32_t block_tokens;
+    uint32_t n_slots;
+    uint32_t row_bytes_k;
+    uint32_t row_bytes_v;
+    uint32_t span_k;
+    uint32_t span_v;
+    uint32_t col_bytes;
+    uint32_t vec16;
+    uint32_t *status;
+};
+
+cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream);
+
+// ---------------------------------------------------------- summaries --
+struct SummaryLayout {
+    float *sum_t;          // [n_layer][n_embd][ldb]  (channel-major, block-minor)
+    uint32_t *mean_tok;    // [n_layer][ldb]
+    float *inv_tok;        // [n_layer][ldb]  1.0f / mean_tok (0 when none)
+    uint32_t ldb;          // block capacity
+    uint32_t n_layer;
+    uint32_t n_embd;
+};
+
+cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
+                                    uint32_t n, const float *d_sums, const uint32_t *d_counts,
+                                    cudaStream_t stream);
+cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n_layers,
+                             uint32_t block0, uint32_t n, const uint8_t *src_k,
+                             uint64_t layer_stride, uint64_t block_stride, uint64_t row_stride,
+                             const uint32_t *n_tokens, uint32_t block_tokens,
+                             cudaStream_t stream);
+
+// --------------------------------------------------------------- query --
+struct QueryState {
+    float *q_sum;          // [n_layer][n_head_q*head_dim]  (device copy)
+    uint32_t *q_count;     // [n_layer]
+    float *qv;             // [n_layer][n_head_kv][head_dim]
+    float *nq;             // [n_layer][n_head_kv]
+};
+
+cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_head_kv,
+                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream);
+
+// -------------------------------------------------------------- scorer --
+struct ScoreArgs {
+    SummaryLayout sum;
+    const float *qv;
+    const float *nq;
+    const uint32_t *q_count;
+    uint32_t n_head_kv;
+    uint32_t head_dim;
+    uint32_t n_blocks;
+    uint32_t layer0;       // first layer scored by this launch
+    uint32_t n_layers;     // layers scored by this launch
+    double *terms;         // [layer][ldt]
+    uint32_t ldt;
+    // combine (only when n_layers == all layers of the session)
+    int combine;
+    uint32_t *counters;    // [ceil(ldb/BPC)]
+    double *scores;        // [ldb]
+};
+
+cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream);
+cudaError_t launch_scores_from_sum(const SummaryLayout &s, uint32_t n_blocks, const double *acc,
+                                   uint32_t n_active, double *scores, cudaStream_t stream);
+
+// -------------------------------------------------------------- select --
+struct SelectArgs {
+    const double *scores;
+    uint32_t n_blocks;
+    uint32_t budget;
+    uint32_t sink;
+    uint32_t recent;
+    const uint32_t *mandatory;
+    uint32_t n_mandatory;
+    uint32_t *selected;
+    PlanHeader *hdr;
+};
+
+cudaError_t launch_select(const SelectArgs &a, cudaStream_t stream);
+
+// Sort ascending + dedupe + drop >= n of a caller selection (device, n <= cap).
+cudaError_t launch_canon_ids(const uint32_t *ids, uint32_t n_ids, uint32_t n_blocks,
+                             uint32_t *selected, PlanHeader *hdr, cudaStream_t stream);
+
+// ---------------------------------------------------------------- diff --
+struct DiffArgs {
+    BlockTable bt;
+    uint32_t n_blocks;
+    uint32_t n_slots;
+    uint32_t optimize_stage_in;
+    uint32_t immutable_source_k;
+    uint32_t immutable_refresh_remaps;
+    uint64_t immutable_refresh_abs_delta_tokens;
+    uint64_t immutable_max_baked_position;
+    int force_raw_refresh;
+    PlanArrays plan;
+    uint32_t *status;
+};
+
+cudaError_t launch_diff(const DiffArgs &a, cudaStream_t stream);
+
+}  // namespace kvm

@@ -1,0 +1,285 @@
+// kvm_score.cu -- mean-K summaries, query preparation and the block scorer.
+//
+// Scorer: llama_memory_kvmem::score_retrieval (src/adapter/llama-memory-kvmem.cpp:2869-2916),
+// restated for the device without changing its arithmetic:
+//   per (block, layer, kv head): dot/nk accumulate in float over d in order,
+//     r = dot / (sqrt(nq) * sqrt(nk) + 1e-6f)
+//   per (block, layer): layer = sum of r over heads in order (double), term = layer / H_kv
+//   per block: score = (sum of terms over layers with a query, in layer order) / n_active
+// The summaries are stored channel-major ([layer][channel][block]) so that a
+// warp of threads, one per block, reads 128 contiguous bytes per channel while
+// each thread keeps the reference's sequential channel order -- coalesced
+// streaming without changing the float rounding of a single block's score.
+// A tree (warp-shuffle) reduction over channels would round differently, and
+// a near-tie at the top-k boundary could then flip the selection.
+//
+// The layer/head combine is done by the last CTA of each block group to
+// finish (threadfence + atomic counter, no waiting), so one launch produces
+// the final scores.
+#include "kvm_internal.cuh"
+#include "kvm_kernels.h"
+
+namespace kvm {
+
+// ------------------------------------------------------------ summaries --
+
+// [n][n_embd] F32 sums + counts -> channel-major layout (transpose through smem).
+__global__ void upload_summaries_kernel(SummaryLayout s, uint32_t layer, uint32_t block0,
+                                        uint32_t n, const float *__restrict__ sums,
+                                        const uint32_t *__restrict__ counts) {
+    __shared__ float tile[32][33];
+    const uint32_t E = s.n_embd;
+    const uint32_t i0 = blockIdx.x * 32u;
+    const uint32_t e0 = blockIdx.y * 32u;
+    for (uint32_t r = threadIdx.y; r < 32u; r += blockDim.y) {
+        const uint32_t i = i0 + r;
+        const uint32_t e = e0 + threadIdx.x;
+        tile[r][threadIdx.x] = (i < n && e < E) ? sums[static_cast<size_t>(i) * E + e] : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.y; r < 32u; r += blockDim.y) {
+        const uint32_t e = e0 + r;
+        const uint32_t i = i0 + threadIdx.x;
+        if (i < n && e < E) {
+            s.sum_t[(static_cast<size_t>(layer) * E + e) * s.ldb + block0 + i] = tile[threadIdx.x][r];
+        }
+    }
+    if (blockIdx.y == 0 && threadIdx.y == 0) {
+        const uint32_t i = i0 + threadIdx.x;
+        if (i < n) {
+            const uint32_t c = counts[i];
+            const size_t at = static_cast<size_t>(layer) * s.ldb + block0 + i;
+            s.mean_tok[at] = c;
+            // RawKvStore::mean_k: inv = 1.0f / (float)mean_tokens
+            s.inv_tok[at] = c ? __fdiv_rn(1.0f, __uint2float_rn(c)) : 0.0f;
+        }
+    }
+}
+
+// F16 K rows -> ordered F32 token sums (RawKvStore::add_mean_f32 with off == 0).
+__global__ void summarize_kernel(SummaryLayout s, uint32_t layer0, uint32_t block0, uint32_t n,
+                                 const uint8_t *__restrict__ src, uint64_t layer_stride,
+                                 uint64_t block_stride, uint64_t row_stride,
+                                 const uint32_t *__restrict__ n_tokens, uint32_t block_tokens) {
+    __shared__ float tile[8][33];
+    const uint32_t E = s.n_embd;
+    const uint32_t l = layer0 + blockIdx.z;
+    const uint32_t bl = threadIdx.y;
+    const uint32_t i = blockIdx.x * 8u + bl;
+    const uint32_t blk = block0 + i;
+    const uint32_t e = blockIdx.y * 32u + threadIdx.x;
+    float acc = 0.0f;
+    uint32_t nt = 0;
+    if (i < n) nt = min(n_tokens[blk], block_tokens);
+    if (i < n && e < E) {
+        const uint8_t *p = src + l * layer_stride + static_cast<uint64_t>(blk) * block_stride +
+                           2ull * e;
+        for (uint32_t t = 0; t < nt; ++t) {
+            const __half h = *reinterpret_cast<const __half *>(p + t * row_stride);
+            acc = __fadd_rn(acc, __half2float(h));
+        }
+    }
+    tile[bl][threadIdx.x] = acc;
+    __syncthreads();
+    const uint32_t tid = threadIdx.y * 32u + threadIdx.x;
+    const uint32_t el = tid / 8u;
+    const uint32_t bw = tid % 8u;
+    const uint32_t ew = blockIdx.y * 32u + el;
+    const uint32_t iw = blockIdx.x * 8u + bw;
+    if (iw < n && ew < E) {
+        s.sum_t[(static_cast<size_t>(l) * E + ew) * s.ldb + block0 + iw] = tile[bw][el];
+    }
+    if (blockIdx.y == 0 && threadIdx.x == 0 && i < n) {
+        const size_t at = static_cast<size_t>(l) * s.ldb + blk;
+        s.mean_tok[at] = nt;
+        s.inv_tok[at] = nt ? __fdiv_rn(1.0f, __uint2float_rn(nt)) : 0.0f;
+    }
+}
+
+// ----------------------------------------------------------------- query --
+
+// qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq and
+// nq[l][h] = sum over d of qv*qv, both exactly as the reference loop computes
+// them; invq = 1.0f / (q_count * g).
+__global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_head_q,
+                                  uint32_t head_dim) {
+    const uint32_t l = blockIdx.x;
+    const uint32_t cnt = q.q_count[l];
+    if (cnt == 0) return;
+    const uint32_t g = n_head_kv == 0 ? 1u : n_head_q / n_head_kv;
+    const uint32_t gg = g > 1u ? g : 1u;
+    const float invq = __fdiv_rn(1.0f, __uint2float_rn(cnt * gg));
+    const uint32_t E = n_head_kv * head_dim;
+    const float *qs = q.q_sum + static_cast<size_t>(l) * n_head_q * head_dim;
+    float *qv = q.qv + static_cast<size_t>(l) * E;
+    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) {
+        const uint32_t h = i / head_dim;
+        const uint32_t d = i % head_dim;
+        float qh = 0.0f;
+        for (uint32_t gi = 0; gi < g; ++gi) {
+            const uint32_t qh_i = h * g + gi;
+            if (qh_i >= n_head_q) break;
+            qh = __fadd_rn(qh, qs[static_cast<size_t>(qh_i) * head_dim + d]);
+        }
+        qv[i] = __fmul_rn(qh, invq);
+    }
+    __syncthreads();
+    for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
+        float nq = 0.0f;
+        const float *v = qv + static_cast<size_t>(h) * head_dim;
+        for (uint32_t d = 0; d < head_dim; ++d) nq = __fadd_rn(nq, __fmul_rn(v[d], v[d]));
+        q.nq[static_cast<size_t>(l) * n_head_kv + h] = nq;
+    }
+}
+
+// ---------------------------------------------------------------- scorer --
+
+template <int BPC>
+__global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
+    extern __shared__ float sh[];
+    const uint32_t H = a.n_head_kv;
+    const uint32_t D = a.head_dim;
+    const uint32_t E = H * D;
+    const uint32_t ldb = a.sum.ldb;
+    float *qv_s = sh;
+    float *nq_s = qv_s + E;
+    float *r_s = nq_s + kMaxHeadsKv;
+    const uint32_t l = a.layer0 + blockIdx.y;
+    const uint32_t b0 = blockIdx.x * BPC;
+    const uint32_t tid = threadIdx.x;
+    const bool active = a.q_count[l] > 0;
+    if (active) {
+        for (uint32_t i = tid; i < E; i += blockDim.x) qv_s[i] = a.qv[static_cast<size_t>(l) * E + i];
+        for (uint32_t h = tid; h < H; h += blockDim.x) nq_s[h] = a.nq[static_cast<size_t>(l) * H + h];
+    }
+    __syncthreads();
+    const uint32_t h = tid / BPC;
+    const uint32_t bl = tid % BPC;
+    const uint32_t b = b0 + bl;
+    float r = 0.0f;
+    if (active && h < H && b < a.n_blocks) {
+        const float inv = a.sum.inv_tok[static_cast<size_t>(l) * ldb + b];
+        const float *col = a.sum.sum_t + (static_cast<size_t>(l) * E + static_cast<size_t>(h) * D) * ldb + b;
+        const float *q = qv_s + h * D;
+        float dot = 0.0f;
+        float nk = 0.0f;
+        if (inv != 0.0f) {
+#pragma unroll 16
+            for (uint32_t d = 0; d < D; ++d) {
+                const float s = __ldg(col + static_cast<size_t>(d) * ldb);
+                const float mk = __fmul_rn(s, inv);
+                dot = __fadd_rn(dot, __fmul_rn(q[d], mk));
+                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+            }
+        }
+        const float den = __fadd_rn(__fmul_rn(__fsqrt_rn(nq_s[h]), __fsqrt_rn(nk)), 1e-6f);
+        r = __fdiv_rn(dot, den);
+    }
+    if (h < H) r_s[h * BPC + bl] = r;
+    __syncthreads();
+    if (tid < BPC && b0 + tid < a.n_blocks) {
+        double layer = 0.0;
+        for (uint32_t hh = 0; hh < H; ++hh) layer = __dadd_rn(layer, static_cast<double>(r_s[hh * BPC + tid]));
+        const double hk = static_cast<double>(H > 1u ? H : 1u);
+        a.terms[static_cast<size_t>(l) * a.ldt + b0 + tid] = active ? __ddiv_rn(layer, hk) : 0.0;
+    }
+    if (!a.combine) return;
+    __shared__ uint32_t s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.counters[blockIdx.x], 1u) == gridDim.y - 1u ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < BPC) {
+        const uint32_t bb = b0 + tid;
+        if (bb < a.n_blocks) {
+            bool has = false;
+            for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
+                has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
+            double acc = 0.0;
+            uint32_t nlay = 0;
+            for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll) {
+                if (a.q_count[ll] == 0) continue;
+                acc = __dadd_rn(acc, __ldcg(a.terms + static_cast<size_t>(ll) * a.ldt + bb));
+                ++nlay;
+            }
+            double sc = 0.0;
+            if (has && nlay) sc = __ddiv_rn(acc, static_cast<double>(nlay));
+            a.scores[bb] = sc;
+        }
+    }
+    if (tid == 0) a.counters[blockIdx.x] = 0u;
+}
+
+__global__ void scores_from_sum_kernel(SummaryLayout s, uint32_t n_blocks,
+                                       const double *__restrict__ acc, uint32_t n_active,
+                                       double *__restrict__ scores) {
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    bool has = false;
+    for (uint32_t l = 0; l < s.n_layer; ++l) has |= s.mean_tok[static_cast<size_t>(l) * s.ldb + b] > 0u;
+    scores[b] = (has && n_active) ? __ddiv_rn(acc[b], static_cast<double>(n_active)) : 0.0;
+}
+
+// ------------------------------------------------------------- launchers --
+
+cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
+                                    uint32_t n, const float *d_sums, const uint32_t *d_counts,
+                                    cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    dim3 grid((n + 31u) / 32u, (s.n_embd + 31u) / 32u);
+    dim3 block(32, 8);
+    upload_summaries_kernel<<<grid, block, 0, stream>>>(s, layer, block0, n, d_sums, d_counts);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n_layers,
+                             uint32_t block0, uint32_t n, const uint8_t *src_k,
+                             uint64_t layer_stride, uint64_t block_stride, uint64_t row_stride,
+                             const uint32_t *n_tokens, uint32_t block_tokens,
+                             cudaStream_t stream) {
+    if (n == 0 || n_layers == 0) return cudaSuccess;
+    dim3 grid((n + 7u) / 8u, (s.n_embd + 31u) / 32u, n_layers);
+    dim3 block(32, 8);
+    summarize_kernel<<<grid, block, 0, stream>>>(s, layer0, block0, n, src_k, layer_stride,
+                                                 block_stride, row_stride, n_tokens, block_tokens);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_head_kv,
+                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream) {
+    query_prep_kernel<<<n_layer, 256, 0, stream>>>(q, n_head_kv, n_head_q, head_dim);
+    return cudaGetLastError();
+}
+
+uint32_t score_blocks_per_cta(uint32_t n_head_kv) { return n_head_kv <= 16u ? 64u : 32u; }
+
+cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
+    if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
+    const uint32_t bpc = score_blocks_per_cta(a.n_head_kv);
+    const uint32_t threads = bpc * a.n_head_kv;
+    const size_t smem = (static_cast<size_t>(a.n_head_kv) * a.head_dim + kMaxHeadsKv +
+                         static_cast<size_t>(a.n_head_kv) * bpc) * sizeof(float);
+    dim3 grid((a.n_blocks + bpc - 1u) / bpc, a.n_layers);
+    if (bpc == 64u) {
+        if (smem > 48u * 1024u)
+            cudaFuncSetAttribute(score_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        score_kernel<64><<<grid, threads, smem, stream>>>(a);
+    } else {
+        if (smem > 48u * 1024u)
+            cudaFuncSetAttribute(score_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        score_kernel<32><<<grid, threads, smem, stream>>>(a);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scores_from_sum(const SummaryLayout &s, uint32_t n_blocks, const double *acc,
+                                   uint32_t n_active, double *scores, cudaStream_t stream) {
+    if (n_blocks == 0) return cudaSuccess;
+    scores_from_sum_kernel<<<(n_blocks + 255u) / 256u, 256, 0, stream>>>(s, n_blocks, acc, n_active,
+                                                                        scores);
+    return cudaGetLastError();
+}
+
+}  // namespace kvm

@@ -1,0 +1,209 @@
+// kvm_select.cu -- top-k block selection on the device.
+//
+// KvMemStore::pick_topk_blocks(mandatory) -> pick_topk_ungrouped, TopK policy
+// (kvmem/src/host/kvmem_store.cpp:357-359, :482-623):
+//   n <= budget (or budget 0): every block, ascending.
+//   else keep sinks 0..min(sink,n)-1, then the mandatory list walked from its
+//   end (newest first), then the `recent` newest blocks, each only while
+//   fewer than `budget` are kept; fill the remaining `need` slots with the
+//   best other blocks ordered by score descending, then block id descending.
+//
+// One CTA of 1024 threads per session.  The sink/mandatory/recent pins are a
+// short sequential walk (thread 0, exactly the reference's order).  The fill
+// is a radix select: 8 passes of 8-bit digits over an order-preserving 64-bit
+// key of the f64 score find the need-th best score T; every candidate above T
+// is taken, and among candidates equal to T the ones with the highest block
+// ids are taken -- the reference's strict total order (score, id), so the
+// selected set is identical to its nth_element.  -0.0 and +0.0 compare equal
+// as in the reference; NaN scores (undefined behaviour in the reference's
+// comparator) rank below every number.
+#include "kvm_internal.cuh"
+#include "kvm_kernels.h"
+
+namespace kvm {
+
+__device__ __forceinline__ uint64_t score_key(double s) {
+    if (s != s) return 0ull;
+    if (s == 0.0) s = 0.0;
+    const uint64_t u = static_cast<uint64_t>(__double_as_longlong(s));
+    return (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
+}
+
+// Ascending compaction of flags[i] != 0 (i < n) into out; returns the count.
+__device__ uint32_t compact_flags(const uint8_t *flags, uint32_t n, uint32_t *out,
+                                  uint32_t *scratch) {
+    const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
+    const uint32_t lo = min(n, threadIdx.x * per);
+    const uint32_t hi = min(n, lo + per);
+    uint32_t c = 0;
+    for (uint32_t i = lo; i < hi; ++i) c += flags[i] != 0;
+    uint32_t total;
+    uint32_t off = block_exclusive_scan<kSelectThreads>(c, scratch, &total);
+    for (uint32_t i = lo; i < hi; ++i)
+        if (flags[i]) out[off++] = i;
+    return total;
+}
+
+__global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
+    extern __shared__ uint8_t kept[];
+    __shared__ uint32_t scratch[40];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_kc;
+    __shared__ uint32_t s_remaining;
+    __shared__ uint64_t s_prefix;
+    __shared__ uint64_t s_mask;
+    const uint32_t n = a.n_blocks;
+    const uint32_t budget = a.budget;
+    const uint32_t tid = threadIdx.x;
+    if (n == 0) {
+        if (tid == 0) a.hdr->n_selected = 0;
+        return;
+    }
+    if (budget == 0 || n <= budget) {
+        for (uint32_t i = tid; i < n; i += kSelectThreads) a.selected[i] = i;
+        if (tid == 0) a.hdr->n_selected = n;
+        return;
+    }
+    for (uint32_t i = tid; i < n; i += kSelectThreads) kept[i] = 0;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t kc = 0;
+        const uint32_t sink = min(a.sink, n);
+        for (uint32_t i = 0; i < sink && kc < budget; ++i)
+            if (!kept[i]) { kept[i] = 1; ++kc; }
+        for (uint32_t i = a.n_mandatory; i > 0 && kc < budget; --i) {
+            const uint32_t id = a.mandatory[i - 1];
+            if (id < n && !kept[id]) { kept[id] = 1; ++kc; }
+        }
+        const uint32_t recent = min(a.recent, n);
+        for (uint32_t i = 0; i < recent && kc < budget; ++i) {
+            const uint32_t id = n - 1 - i;
+            if (!kept[id]) { kept[id] = 1; ++kc; }
+        }
+        s_kc = kc;
+    }
+    __syncthreads();
+    const uint32_t kc = s_kc;
+    const uint32_t need = budget - kc;
+    const uint32_t n_cand = n - kc;
+    if (need > 0 && need >= n_cand) {
+        for (uint32_t i = tid; i < n; i += kSelectThreads)
+            if (!kept[i]) kept[i] = 2;
+        __syncthreads();
+    } else if (need > 0) {
+        if (tid == 0) {
+            s_prefix = 0ull;
+            s_mask = 0ull;
+            s_remaining = need;
+        }
+        __syncthreads();
+        for (int pass = 0; pass < 8; ++pass) {
+            const int shift = 56 - 8 * pass;
+            for (uint32_t i = tid; i < 256u; i += kSelectThreads) hist[i] = 0u;
+            __syncthreads();
+            const uint64_t prefix = s_prefix;
+            const uint64_t mask = s_mask;
+            for (uint32_t i = tid; i < n; i += kSelectThreads) {
+                if (kept[i]) continue;
+                const uint64_t k = score_key(a.scores[i]);
+                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (tid < 32) {
+                // lane l owns bins 255-8l .. 248-8l (highest digits first)
+                const uint32_t lane = tid;
+                const uint32_t rem = s_remaining;   // read before any lane writes it
+                uint32_t local = 0;
+                for (int j = 0; j < 8; ++j) local += hist[255u - 8u * lane - j];
+                uint32_t cum = local;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, cum, o);
+                    if (lane >= static_cast<uint32_t>(o)) cum += y;
+                }
+                const uint32_t ex = cum - local;
+                const bool mine = ex < rem && rem <= cum;
+                if (mine) {
+                    uint32_t acc = ex;
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t bin = 255u - 8u * lane - j;
+                        const uint32_t hc = hist[bin];
+                        if (acc + hc >= rem) {
+                            s_remaining = rem - acc;
+                            s_prefix = prefix | (static_cast<uint64_t>(bin) << shift);
+                            s_mask = mask | (255ull << shift);
+                            break;
+                        }
+                        acc += hc;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        // take every candidate above the threshold key, and the `rem`
+        // highest-id candidates equal to it
+        const uint64_t thr = s_prefix;
+        const uint32_t rem = s_remaining;
+        const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
+        const uint32_t lo = min(n, tid * per);
+        const uint32_t hi = min(n, lo + per);
+        uint32_t eq = 0;
+        for (uint32_t i = lo; i < hi; ++i)
+            if (!kept[i] && score_key(a.scores[i]) == thr) ++eq;
+        uint32_t total_eq;
+        const uint32_t before = block_exclusive_scan<kSelectThreads>(eq, scratch, &total_eq);
+        uint32_t seen = before;   // equal candidates with id < i, running
+        for (uint32_t i = lo; i < hi; ++i) {
+            if (kept[i]) continue;
+            const uint64_t k = score_key(a.scores[i]);
+            if (k > thr) {
+                kept[i] = 2;
+            } else if (k == thr) {
+                ++seen;
+                const uint32_t above = total_eq - seen;   // equal candidates with id > i
+                if (above < rem) kept[i] = 2;
+            }
+        }
+        __syncthreads();
+    }
+    const uint32_t m = compact_flags(kept, n, a.selected, scratch);
+    if (tid == 0) a.hdr->n_selected = m;
+}
+
+// set_selection's canonicalisation: sort ascending, drop duplicates and ids
+// >= n (kvmem_store.cpp:761-768), via a flag per block.
+__global__ void __launch_bounds__(kSelectThreads) canon_ids_kernel(const uint32_t *ids,
+                                                                   uint32_t n_ids, uint32_t n,
+                                                                   uint32_t *selected,
+                                                                   PlanHeader *hdr) {
+    extern __shared__ uint8_t flag[];
+    __shared__ uint32_t scratch[40];
+    for (uint32_t i = threadIdx.x; i < n; i += kSelectThreads) flag[i] = 0;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < n_ids; i += kSelectThreads) {
+        const uint32_t id = ids[i];
+        if (id < n) flag[id] = 1;
+    }
+    __syncthreads();
+    const uint32_t m = compact_flags(flag, n, selected, scratch);
+    if (threadIdx.x == 0) hdr->n_selected = m;
+}
+
+cudaError_t launch_select(const SelectArgs &a, cudaStream_t stream) {
+    const size_t smem = a.n_blocks ? a.n_blocks : 1u;
+    if (smem > 48u * 1024u)
+        cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    select_kernel<<<1, kSelectThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_canon_ids(const uint32_t *ids, uint32_t n_ids, uint32_t n_blocks,
+                             uint32_t *selected, PlanHeader *hdr, cudaStream_t stream) {
+    const size_t smem = n_blocks ? n_blocks : 1u;
+    if (smem > 48u * 1024u)
+        cudaFuncSetAttribute(canon_ids_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    canon_ids_kernel<<<1, kSelectThreads, smem, stream>>>(ids, n_ids, n_blocks, selected, hdr);
+    return cudaGetLastError();
+}
+
+}  // namespace kvm

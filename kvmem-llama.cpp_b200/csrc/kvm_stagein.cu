@@ -1,0 +1,329 @@
+// kvm_stagein.cu -- fused gather + quantize stage-in and in-place slot moves.
+//
+// Replaces the reference's stage-in (write_block_to_gpu -> RawKvStore::copy_*
+// -> kvmem_stagein_enqueue_v -> kvmem_stagein_flush,
+// src/adapter/llama-memory-kvmem.cpp:2726-2791, src/adapter/llama-kvmem-stagein.cu:632-753)
+// and the layout gather/scatter of retained blocks (layout_gpu_slots_by_orig_pos,
+// llama-memory-kvmem.cpp:931-1254, kvmem_d2d_batched, stagein.cu:965-1000).
+//
+// stagein_kernel: persistent CTAs walk (cold block, layer, K|V, row tile)
+// tasks.  One elected thread streams each F16 tile (rows x n_embd halves,
+// contiguous) into shared memory with cp.async.bulk (TMA bulk copy, completed
+// on an mbarrier) NSTAGE tiles ahead; all threads quantize the tile into a
+// shared-memory output buffer (4 lanes per ggml block), then the elected
+// thread writes the tile's quantized rows (contiguous in the window) back with
+// one cp.async.bulk shared->global store.  Every wait is bounded.
+//
+// permute_kernel: moves retained blocks from their old slot to their new slot
+// in place.  Each CTA owns a byte column of the slot span for one (layer, K|V)
+// and stages that column of every moving block in shared memory before
+// writing any of them, so chains and cycles of moves need no scratch buffer
+// and each byte crosses HBM once in each direction.
+#include "kvm_internal.cuh"
+#include "kvm_quant.cuh"
+#include "kvm_kernels.h"
+
+#include <atomic>
+
+namespace kvm {
+
+namespace {
+
+struct TaskDesc {
+    const uint8_t *src;
+    uint8_t *dst;
+    uint32_t rows;
+    uint32_t kv;
+    bool valid;
+};
+
+__device__ __forceinline__ TaskDesc decode_task(const StageinArgs &a, uint64_t t,
+                                                uint32_t tiles, uint32_t n_items) {
+    TaskDesc d{nullptr, nullptr, 0u, 0u, false};
+    const uint64_t per_item = static_cast<uint64_t>(a.n_layer) * a.n_kv * tiles;
+    const uint32_t item = static_cast<uint32_t>(t / per_item);
+    uint32_t r = static_cast<uint32_t>(t % per_item);
+    const uint32_t layer = r / (a.n_kv * tiles);
+    r %= a.n_kv * tiles;
+    const uint32_t kv = r / tiles;
+    const uint32_t tile = r % tiles;
+    if (item >= n_items) return d;
+    const uint32_t idx = a.item0 + item;
+    const uint32_t block = a.cold_block[idx];
+    const int32_t slot = a.cold_to[idx];
+    if (block >= a.max_blocks) {
+        set_status(a.status, kErrIndex);
+        return d;
+    }
+    if (slot < 0 || static_cast<uint32_t>(slot) >= a.n_slots) {
+        set_status(a.status, kErrSlot);
+        return d;
+    }
+    const uint32_t nt = min(a.n_tokens[block], a.block_tokens);
+    const uint32_t row0 = tile * a.rows_per_tile;
+    if (row0 >= nt) return d;
+    d.rows = min(a.rows_per_tile, nt - row0);
+    d.kv = kv;
+    const uint64_t src_index = a.src_by_item ? item : block;
+    const uint8_t *sbase = kv ? a.src_v : a.src_k;
+    d.src = sbase + layer * a.layer_stride + src_index * a.item_stride + row0 * a.row_stride;
+    uint8_t *dbase = kv ? a.dst_v[layer] : a.dst_k[layer];
+    const uint32_t rb = kv ? a.row_bytes_v : a.row_bytes_k;
+    d.dst = dbase + (static_cast<uint64_t>(slot) * a.block_tokens + row0) * rb;
+    d.valid = true;
+    return d;
+}
+
+__device__ __forceinline__ void issue_tile_load(const StageinArgs &a, const TaskDesc &d,
+                                                uint8_t *buf, uint64_t *bar) {
+    const uint32_t row_in = a.n_embd * 2u;
+    const uint32_t bytes = d.rows * row_in;
+    mbar_arrive_expect_tx(bar, bytes);
+    if (a.row_stride == row_in) {
+        bulk_g2s(buf, d.src, bytes, bar);
+    } else {
+        for (uint32_t r = 0; r < d.rows; ++r) {
+            bulk_g2s(buf + r * row_in, d.src + r * a.row_stride, row_in, bar);
+        }
+    }
+}
+
+}  // namespace
+
+template <int NSTAGE>
+__global__ void __launch_bounds__(kStageinThreads, 2) stagein_kernel(StageinArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *in_buf = smem + 128;
+    uint8_t *out_buf = in_buf + NSTAGE * a.tile_in_bytes;
+
+    const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
+    const uint32_t n_items = min(n_items_raw, a.max_items);
+    const uint32_t tiles = (a.block_tokens + a.rows_per_tile - 1) / a.rows_per_tile;
+    const uint64_t total = static_cast<uint64_t>(n_items) * a.n_layer * a.n_kv * tiles;
+    if (static_cast<uint64_t>(blockIdx.x) >= total) return;
+
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < NSTAGE; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // Producer state (thread 0 only): next task to consider, loads issued.
+    uint64_t ptask = blockIdx.x;
+    uint32_t issued = 0;
+    if (tid == 0) {
+        while (issued < NSTAGE && ptask < total) {
+            const TaskDesc d = decode_task(a, ptask, tiles, n_items);
+            ptask += gridDim.x;
+            if (!d.valid) continue;
+            issue_tile_load(a, d, in_buf + (issued % NSTAGE) * a.tile_in_bytes,
+                            &full[issued % NSTAGE]);
+            ++issued;
+        }
+    }
+
+    const int lane = tid & 31;
+    const int sub = lane & 3;
+    uint32_t j = 0;  // non-empty tasks consumed
+    bool bad = false;
+    for (uint64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        const TaskDesc d = decode_task(a, t, tiles, n_items);
+        if (!d.valid) continue;
+        const uint32_t stage = j % NSTAGE;
+        const uint32_t ob = j & 1u;
+        const bool ok = mbar_wait_bounded(&full[stage], (j / NSTAGE) & 1u);
+        const uint8_t *ib = in_buf + stage * a.tile_in_bytes;
+        uint8_t *obuf = out_buf + ob * a.tile_out_bytes;
+        const int type = d.kv ? a.type_v : a.type_k;
+        const uint32_t nparts = d.rows * (a.n_embd / 8u);    // 8 values per lane
+        if (ok) {
+            for (uint32_t base = 0; base < nparts; base += kStageinThreads) {
+                const uint32_t p = base + tid;
+                const bool active = p < nparts;
+                uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+                if (active) raw = *reinterpret_cast<const uint4 *>(ib + static_cast<size_t>(p) * 16u);
+                quant_part(type, raw, sub, obuf, p >> 2, active);
+            }
+        }
+        (void)lane;
+        fence_proxy_async_smem();
+        bad = __syncthreads_or(!ok) != 0;
+        if (bad) break;
+        const uint32_t rb = d.kv ? a.row_bytes_v : a.row_bytes_k;
+        const uint32_t out_bytes = d.rows * rb;
+        if (a.bulk_store) {
+            if (tid == 0) {
+                bulk_s2g(d.dst, obuf, out_bytes);
+                bulk_commit();
+            }
+        } else {
+            for (uint32_t o = 2u * tid; o < out_bytes; o += 2u * kStageinThreads) {
+                *reinterpret_cast<uint16_t *>(d.dst + o) =
+                    *reinterpret_cast<const uint16_t *>(obuf + o);
+            }
+        }
+        if (tid == 0) {
+            // refill the stage just consumed
+            while (ptask < total) {
+                const TaskDesc nd = decode_task(a, ptask, tiles, n_items);
+                ptask += gridDim.x;
+                if (!nd.valid) continue;
+                issue_tile_load(a, nd, in_buf + (issued % NSTAGE) * a.tile_in_bytes,
+                                &full[issued % NSTAGE]);
+                ++issued;
+                break;
+            }
+            // the store issued last iteration must be done reading its buffer
+            // before the next iteration overwrites it
+            if (a.bulk_store) bulk_wait_read<1>();
+        }
+        __syncthreads();
+        ++j;
+    }
+    if (tid == 0) {
+        if (bad) {
+            set_status(a.status, kErrTimeout);
+            for (uint32_t k = j; k < issued; ++k) {
+                (void)mbar_wait_bounded(&full[k % NSTAGE], (k / NSTAGE) & 1u);
+            }
+        }
+        if (a.bulk_store) bulk_wait_all<0>();
+    }
+}
+
+// ------------------------------------------------------------- permute --
+
+__global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a) {
+    extern __shared__ __align__(16) uint8_t col[];
+    const uint32_t n_moves = min(*a.n_moves_dev, a.max_moves);
+    if (n_moves == 0) return;
+    const uint32_t n_cols_k = (a.span_k + a.col_bytes - 1) / a.col_bytes;
+    const uint32_t n_cols_v = (a.span_v + a.col_bytes - 1) / a.col_bytes;
+    const uint64_t units = static_cast<uint64_t>(a.n_layer) * (n_cols_k + n_cols_v);
+    for (uint64_t u = blockIdx.x; u < units; u += gridDim.x) {
+        const uint32_t layer = static_cast<uint32_t>(u / (n_cols_k + n_cols_v));
+        uint32_t c = static_cast<uint32_t>(u % (n_cols_k + n_cols_v));
+        const bool is_v = c >= n_cols_k;
+        if (is_v) c -= n_cols_k;
+        uint8_t *base = is_v ? a.dst_v[layer] : a.dst_k[layer];
+        const uint32_t span = is_v ? a.span_v : a.span_k;
+        const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
+        const uint32_t c0 = c * a.col_bytes;
+        // gather this column of every moving block
+        for (uint32_t m = 0; m < n_moves; ++m) {
+            const uint32_t blk = a.mv_block[m];
+            const int32_t from = a.mv_from[m];
+            if (blk >= a.max_blocks || from < 0 || static_cast<uint32_t>(from) >= a.n_slots) {
+                set_status(a.status, kErrSlot);
+                continue;
+            }
+            const uint32_t nbytes = min(a.n_tokens[blk], a.block_tokens) * rb;
+            if (c0 >= nbytes) continue;
+            const uint32_t w = min(a.col_bytes, nbytes - c0);
+            const uint8_t *src = base + static_cast<uint64_t>(from) * span + c0;
+            uint8_t *dst = col + static_cast<size_t>(m) * a.col_bytes;
+            if (a.vec16) {
+                for (uint32_t o = 16u * threadIdx.x; o < w; o += 16u * kPermuteThreads)
+                    *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
+            } else {
+                for (uint32_t o = 2u * threadIdx.x; o < w; o += 2u * kPermuteThreads)
+                    *reinterpret_cast<uint16_t *>(dst + o) =
+                        *reinterpret_cast<const uint16_t *>(src + o);
+            }
+        }
+        __syncthreads();
+        for (uint32_t m = 0; m < n_moves; ++m) {
+            const uint32_t blk = a.mv_block[m];
+            const int32_t from = a.mv_from[m];
+            const int32_t to = a.mv_to[m];
+            if (blk >= a.max_blocks || from < 0 || static_cast<uint32_t>(from) >= a.n_slots ||
+                to < 0 || static_cast<uint32_t>(to) >= a.n_slots) {
+                continue;
+            }
+            const uint32_t nbytes = min(a.n_tokens[blk], a.block_tokens) * rb;
+            if (c0 >= nbytes) continue;
+            const uint32_t w = min(a.col_bytes, nbytes - c0);
+            uint8_t *dst = base + static_cast<uint64_t>(to) * span + c0;
+            const uint8_t *src = col + static_cast<size_t>(m) * a.col_bytes;
+            if (a.vec16) {
+                for (uint32_t o = 16u * threadIdx.x; o < w; o += 16u * kPermuteThreads)
+                    *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
+            } else {
+                for (uint32_t o = 2u * threadIdx.x; o < w; o += 2u * kPermuteThreads)
+                    *reinterpret_cast<uint16_t *>(dst + o) =
+                        *reinterpret_cast<const uint16_t *>(src + o);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------- launchers --
+
+static int g_num_sms = 0;
+
+static int num_sms() {
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens) {
+    // 16 KiB of F16 per tile (8 rows at n_embd = 1024)
+    uint32_t r = 8192u / (n_embd ? n_embd : 1u);
+    if (r < 1u) r = 1u;
+    if (r > block_tokens) r = block_tokens;
+    return r;
+}
+
+size_t stagein_smem_bytes(const StageinArgs &a) {
+    return 128u + static_cast<size_t>(kStageinStages) * a.tile_in_bytes + 2u * a.tile_out_bytes;
+}
+
+// Dynamic shared-memory opt-in is a per-device function attribute: set it
+// once per device the process launches on.
+static bool attr_once(std::atomic<uint64_t> &done, const void *fn, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+        return false;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return true;
+}
+
+static std::atomic<uint64_t> g_stagein_attr{0};
+static std::atomic<uint64_t> g_permute_attr{0};
+
+cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
+    const size_t smem = stagein_smem_bytes(a);
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    if (!attr_once(g_stagein_attr, reinterpret_cast<const void *>(stagein_kernel<kStageinStages>),
+                   200 * 1024))
+        return cudaErrorInvalidValue;
+    int per_sm = smem <= 100 * 1024 ? 2 : 1;
+    uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
+    if (grid_cap && grid > grid_cap) grid = grid_cap;
+    if (grid == 0) grid = 1;
+    stagein_kernel<kStageinStages><<<grid, kStageinThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
+    const size_t smem = static_cast<size_t>(a.max_moves) * a.col_bytes;
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    if (!attr_once(g_permute_attr, reinterpret_cast<const void *>(permute_kernel), 200 * 1024))
+        return cudaErrorInvalidValue;
+    const uint32_t grid = static_cast<uint32_t>(num_sms() * 2);
+    permute_kernel<<<grid, kPermuteThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace kvm

@@ -1,0 +1,350 @@
+"""ctypes binding of libkvm (include/kvm.h) for tests, the bench and Python callers.
+
+libkvm is the B200-native (sm_100a) KV reselection library: score -> select ->
+diff -> gather+quantize stage-in.  This module only marshals arguments; all
+work runs in the CUDA library.  Importing it when ``libkvm.so`` is missing
+raises -- there is no CPU fallback.
+
+Device buffers are passed as integers (``tensor.data_ptr()``) or torch
+tensors; streams as ``torch.cuda.Stream`` / raw handles (0 = legacy default).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libkvm.so")
+
+TYPE_F16, TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0 = 1, 2, 6, 8
+TIER_GPU, TIER_CPU, TIER_SSD = 0, 1, 2
+LOC_DEVICE, LOC_HOST = 0, 1
+
+KVM_OK, KVM_EINVAL, KVM_ENOMEM, KVM_ECUDA, KVM_ETIMEOUT, KVM_ESTATE, KVM_EDEVICE = range(7)
+_STATUS = {1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESTATE", 6: "EDEVICE"}
+
+# every symbol include/kvm.h declares
+ABI_SYMBOLS = (
+    "kvm_config_default", "kvm_session_create", "kvm_session_destroy", "kvm_last_error",
+    "kvm_window_slots", "kvm_block_count", "kvm_row_bytes", "kvm_register_append",
+    "kvm_reset_window", "kvm_upload_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
+    "kvm_score_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
+    "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
+    "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
+)
+
+
+class KvmError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"kvm {_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+def build(force: bool = False) -> str:
+    """Compile libkvm.so in-tree (nvcc, sm_100a)."""
+    if force or not os.path.exists(LIB_PATH):
+        subprocess.run(["make", "-s", "-C", PKG], check=True)
+    return LIB_PATH
+
+
+class Config(C.Structure):
+    _fields_ = [
+        ("block_tokens", C.c_uint32), ("select_budget", C.c_uint32), ("gen_reserve", C.c_uint32),
+        ("sink_blocks", C.c_uint32), ("recent_blocks", C.c_uint32), ("n_layer", C.c_uint32),
+        ("n_head_kv", C.c_uint32), ("head_dim", C.c_uint32), ("n_head_q", C.c_uint32),
+        ("max_blocks", C.c_uint32), ("type_k", C.c_int32), ("type_v", C.c_int32),
+        ("optimize_stage_in", C.c_uint32), ("immutable_source_k", C.c_uint32),
+        ("immutable_refresh_remaps", C.c_uint32), ("reserved0", C.c_uint32),
+        ("immutable_refresh_abs_delta_tokens", C.c_uint64),
+        ("immutable_max_baked_position", C.c_uint64), ("staging_bytes", C.c_uint64),
+    ]
+
+
+class Source(C.Structure):
+    _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("layer_stride", C.c_uint64),
+                ("block_stride", C.c_uint64), ("row_stride", C.c_uint64),
+                ("location", C.c_int32), ("reserved0", C.c_int32)]
+
+
+class Window(C.Structure):
+    _fields_ = [("d_k", C.POINTER(C.c_void_p)), ("d_v", C.POINTER(C.c_void_p))]
+
+
+class _Plan(C.Structure):
+    _fields_ = [
+        ("capacity", C.c_uint32), ("n_selected", C.c_uint32), ("selected", C.POINTER(C.c_uint32)),
+        ("n_stage_in", C.c_uint32), ("stage_in", C.POINTER(C.c_uint32)),
+        ("n_stage_out", C.c_uint32), ("stage_out", C.POINTER(C.c_uint32)),
+        ("n_remaps", C.c_uint32), ("rm_block_id", C.POINTER(C.c_uint32)),
+        ("rm_n_tokens", C.POINTER(C.c_uint32)), ("rm_from_base", C.POINTER(C.c_int32)),
+        ("rm_to_base", C.POINTER(C.c_int32)), ("rm_working_k_resident", C.POINTER(C.c_uint8)),
+        ("rm_skip", C.POINTER(C.c_uint8)), ("rm_raw_refresh", C.POINTER(C.c_uint8)),
+        ("total_window_tokens", C.c_uint32), ("selection_overlap_blocks", C.c_uint32),
+        ("gpu_reused_blocks", C.c_uint32), ("retained_position_stable", C.c_uint32),
+        ("retained_position_moved", C.c_uint32), ("n_moves", C.c_uint32),
+        ("mv_block", C.POINTER(C.c_uint32)), ("mv_from", C.POINTER(C.c_int32)),
+        ("mv_to", C.POINTER(C.c_int32)), ("n_cold", C.c_uint32),
+        ("cold_block", C.POINTER(C.c_uint32)), ("cold_to", C.POINTER(C.c_int32)),
+    ]
+
+
+class Timings(C.Structure):
+    _fields_ = [("score_ms", C.c_float), ("plan_ms", C.c_float), ("layout_ms", C.c_float),
+                ("set_ms", C.c_float), ("total_ms", C.c_float)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libkvm.so (raises when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libkvm.so not built ({LIB_PATH}); run `make -C {PKG}`")
+        L = C.CDLL(LIB_PATH)
+        vp, u32, i32, u64 = C.c_void_p, C.c_uint32, C.c_int32, C.c_uint64
+        sig = {
+            "kvm_config_default": (None, [C.POINTER(Config)]),
+            "kvm_session_create": (C.c_int, [C.POINTER(Config), C.c_int, C.POINTER(vp)]),
+            "kvm_session_destroy": (None, [vp]),
+            "kvm_last_error": (C.c_char_p, [vp]),
+            "kvm_window_slots": (u32, [vp]),
+            "kvm_block_count": (u32, [vp]),
+            "kvm_row_bytes": (u64, [i32, u32]),
+            "kvm_register_append": (C.c_int, [vp, vp, u32, C.c_int]),
+            "kvm_reset_window": (C.c_int, [vp, vp]),
+            "kvm_upload_summaries": (C.c_int, [vp, vp, u32, u32, u32, vp, vp]),
+            "kvm_summarize": (C.c_int, [vp, vp, u32, u32, u32, u32, C.POINTER(Source)]),
+            "kvm_set_query": (C.c_int, [vp, vp, vp, vp]),
+            "kvm_score": (C.c_int, [vp, vp, vp]),
+            "kvm_score_terms": (C.c_int, [vp, vp, u32, u32, vp, u32]),
+            "kvm_set_scores_from_sum": (C.c_int, [vp, vp, vp, u32]),
+            "kvm_set_scores": (C.c_int, [vp, vp, vp, u32]),
+            "kvm_select": (C.c_int, [vp, vp, vp, u32]),
+            "kvm_set_selection_ids": (C.c_int, [vp, vp, vp, u32]),
+            "kvm_diff": (C.c_int, [vp, vp, C.c_int]),
+            "kvm_stagein": (C.c_int, [vp, vp, C.POINTER(Source), C.POINTER(Window)]),
+            "kvm_step": (C.c_int, [vp, vp, vp, u32, C.POINTER(Source), C.POINTER(Window)]),
+            "kvm_wait": (C.c_int, [vp, vp, u32]),
+            "kvm_get_plan": (C.c_int, [vp, vp, C.POINTER(_Plan), u32]),
+            "kvm_get_scores": (C.c_int, [vp, vp, vp, u32, u32]),
+            "kvm_get_timings": (C.c_int, [vp, C.POINTER(Timings)]),
+            "kvm_kernel_launches": (u64, [vp]),
+            "kvm_quantize_rows": (C.c_int, [vp, i32, vp, u64, u32, vp]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def row_bytes(type_: int, n_embd: int) -> int:
+    return int(lib().kvm_row_bytes(type_, n_embd))
+
+
+def _ptr(x):
+    """Device/host address of a torch tensor, numpy array or integer."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    raise TypeError(type(x))
+
+
+def _stream(stream):
+    if stream is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream
+        except Exception:  # noqa: BLE001 -- no torch: legacy default stream
+            return 0
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def default_config(**kw) -> Config:
+    c = Config()
+    lib().kvm_config_default(C.byref(c))
+    for k, v in kw.items():
+        if not hasattr(c, k):
+            raise AttributeError(k)
+        setattr(c, k, v)
+    return c
+
+
+def quantize_rows(type_: int, src, n_rows: int, n_embd: int, dst, stream=None) -> None:
+    """Standalone stage-in kernel on a plain row range (device pointers)."""
+    st = lib().kvm_quantize_rows(_stream(stream), type_, _ptr(src), n_rows, n_embd, _ptr(dst))
+    if st != KVM_OK:
+        raise KvmError(st, "kvm_quantize_rows failed")
+
+
+def make_source(k, v, layer_stride, block_stride, row_stride, location=LOC_DEVICE) -> Source:
+    return Source(_ptr(k), _ptr(v), layer_stride, block_stride, row_stride, location, 0)
+
+
+class Session:
+    """One libkvm session (one sequence on one device)."""
+
+    def __init__(self, cfg: Config, device: int = 0):
+        self.cfg = cfg
+        self.device = device
+        h = C.c_void_p()
+        st = lib().kvm_session_create(C.byref(cfg), device, C.byref(h))
+        if st != KVM_OK:
+            raise KvmError(st, lib().kvm_last_error(None).decode())
+        self.h = h
+        self.n_slots = int(lib().kvm_window_slots(h))
+        self._win_keep = None
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().kvm_session_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter teardown
+            pass
+
+    def _check(self, st, what):
+        if st != KVM_OK:
+            raise KvmError(st, f"{what}: {lib().kvm_last_error(self.h).decode()}")
+
+    # ---- block table
+    @property
+    def block_count(self) -> int:
+        return int(lib().kvm_block_count(self.h))
+
+    def register_append(self, n_tokens: int, resident: bool = False, stream=None):
+        self._check(lib().kvm_register_append(self.h, _stream(stream), n_tokens, int(resident)),
+                    "register_append")
+
+    def reset_window(self, stream=None):
+        self._check(lib().kvm_reset_window(self.h, _stream(stream)), "reset_window")
+
+    # ---- summaries and query
+    def upload_summaries(self, layer, block0, sums, counts, stream=None):
+        n = len(counts)
+        self._check(lib().kvm_upload_summaries(self.h, _stream(stream), layer, block0, n,
+                                                _ptr(sums), _ptr(counts)), "upload_summaries")
+
+    def summarize(self, src: Source, layer0=0, n_layers=None, block0=0, n=None, stream=None):
+        n_layers = self.cfg.n_layer if n_layers is None else n_layers
+        n = self.block_count if n is None else n
+        self._check(lib().kvm_summarize(self.h, _stream(stream), layer0, n_layers, block0, n,
+                                         C.byref(src)), "summarize")
+
+    def set_query(self, q_sum, q_count, stream=None):
+        qc = np.ascontiguousarray(np.asarray(q_count, dtype=np.uint32))
+        self._check(lib().kvm_set_query(self.h, _stream(stream), _ptr(q_sum), qc.ctypes.data),
+                    "set_query")
+
+    # ---- stages
+    def score(self, d_scores=None, stream=None):
+        self._check(lib().kvm_score(self.h, _stream(stream), _ptr(d_scores)), "score")
+
+    def score_terms(self, layer0, n_layers, d_terms, ldt, stream=None):
+        self._check(lib().kvm_score_terms(self.h, _stream(stream), layer0, n_layers,
+                                           _ptr(d_terms), ldt), "score_terms")
+
+    def set_scores_from_sum(self, d_acc, n_active, stream=None):
+        self._check(lib().kvm_set_scores_from_sum(self.h, _stream(stream), _ptr(d_acc), n_active),
+                    "set_scores_from_sum")
+
+    def set_scores(self, scores, stream=None):
+        if isinstance(scores, np.ndarray):
+            scores = np.ascontiguousarray(scores, dtype=np.float64)
+            n = scores.size
+        else:
+            n = scores.numel()
+        self._check(lib().kvm_set_scores(self.h, _stream(stream), _ptr(scores), n), "set_scores")
+
+    def select(self, mandatory=(), stream=None):
+        m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
+        self._check(lib().kvm_select(self.h, _stream(stream), m.ctypes.data if m.size else None,
+                                      m.size), "select")
+
+    def set_selection_ids(self, ids, stream=None):
+        m = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
+        self._check(lib().kvm_set_selection_ids(self.h, _stream(stream),
+                                                 m.ctypes.data if m.size else None, m.size),
+                    "set_selection_ids")
+
+    def diff(self, force_raw_refresh=False, stream=None):
+        self._check(lib().kvm_diff(self.h, _stream(stream), int(bool(force_raw_refresh))), "diff")
+
+    def _window(self, k_bases, v_bases):
+        L = len(k_bases)
+        ka = (C.c_void_p * L)(*[_ptr(x) for x in k_bases])
+        va = (C.c_void_p * L)(*[_ptr(x) for x in v_bases])
+        self._win_keep = (ka, va)
+        return Window(C.cast(ka, C.POINTER(C.c_void_p)), C.cast(va, C.POINTER(C.c_void_p)))
+
+    def stagein(self, src: Source, k_bases, v_bases, stream=None):
+        win = self._window(k_bases, v_bases)
+        self._check(lib().kvm_stagein(self.h, _stream(stream), C.byref(src), C.byref(win)),
+                    "stagein")
+
+    def step(self, src: Source, k_bases, v_bases, mandatory=(), stream=None):
+        m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
+        win = self._window(k_bases, v_bases)
+        self._check(lib().kvm_step(self.h, _stream(stream), m.ctypes.data if m.size else None,
+                                    m.size, C.byref(src), C.byref(win)), "step")
+
+    # ---- results
+    def wait(self, timeout_ms=60000, stream=None):
+        self._check(lib().kvm_wait(self.h, _stream(stream), timeout_ms), "wait")
+
+    def scores(self, timeout_ms=60000, stream=None) -> np.ndarray:
+        n = self.block_count
+        out = np.zeros(max(1, n), dtype=np.float64)
+        self._check(lib().kvm_get_scores(self.h, _stream(stream), out.ctypes.data, n, timeout_ms),
+                    "get_scores")
+        return out[:n]
+
+    def plan(self, timeout_ms=60000, stream=None) -> dict:
+        cap = max(1, int(self.cfg.max_blocks))
+        arrs = {name: np.zeros(cap, dtype=dt) for name, dt in (
+            ("selected", np.uint32), ("stage_in", np.uint32), ("stage_out", np.uint32),
+            ("rm_block_id", np.uint32), ("rm_n_tokens", np.uint32), ("rm_from_base", np.int32),
+            ("rm_to_base", np.int32), ("rm_working_k_resident", np.uint8), ("rm_skip", np.uint8),
+            ("rm_raw_refresh", np.uint8), ("mv_block", np.uint32), ("mv_from", np.int32),
+            ("mv_to", np.int32), ("cold_block", np.uint32), ("cold_to", np.int32))}
+        ctype = {np.dtype(np.uint32): C.c_uint32, np.dtype(np.int32): C.c_int32,
+                 np.dtype(np.uint8): C.c_uint8}
+        p = _Plan()
+        p.capacity = cap
+        for name, a in arrs.items():
+            setattr(p, name, a.ctypes.data_as(C.POINTER(ctype[a.dtype])))
+        self._check(lib().kvm_get_plan(self.h, _stream(stream), C.byref(p), timeout_ms), "get_plan")
+        n = {"selected": p.n_selected, "stage_in": p.n_stage_in, "stage_out": p.n_stage_out,
+             "mv_block": p.n_moves, "mv_from": p.n_moves, "mv_to": p.n_moves,
+             "cold_block": p.n_cold, "cold_to": p.n_cold}
+        out = {name: a[:n.get(name, p.n_remaps)].copy() for name, a in arrs.items()}
+        for f in ("total_window_tokens", "selection_overlap_blocks", "gpu_reused_blocks",
+                  "retained_position_stable", "retained_position_moved"):
+            out[f] = int(getattr(p, f))
+        return out
+
+    def timings(self) -> dict:
+        t = Timings()
+        self._check(lib().kvm_get_timings(self.h, C.byref(t)), "get_timings")
+        return {f: float(getattr(t, f)) for f, _ in Timings._fields_}
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(lib().kvm_kernel_launches(self.h))

@@ -1,0 +1,270 @@
+"""GPU parity of libkvm against the CPU oracle, through the C ABI.
+
+Bit-exact bars: quantized window bytes, selected block ids, KvMemPlan
+fields, slot layout.  Scores: the device restates the reference arithmetic
+operation for operation, so they are compared bit for bit as well (the
+north-star tolerance of 1e-4 relative is asserted separately as the floor).
+"""
+import numpy as np
+import pytest
+
+from kvm_testlib import OracleModel, Shape, make_query, make_rig
+
+pytestmark = pytest.mark.gpu
+
+
+def _cuda():
+    import torch
+    return torch
+
+
+# ----------------------------------------------------------- quantizers ---
+
+@pytest.mark.parametrize("type_id", [8, 2, 6, 1])
+def test_quantize_rows_bitexact(kvm_lib, oracle, type_id):
+    torch = _cuda()
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "quant_golden.npz"))
+    rng = np.random.default_rng(type_id)
+    rows = np.concatenate([
+        g["rows_f16"].view(np.float16),
+        oracle.synth_f16(rng, (37, 256), 256),           # row count not a tile multiple
+    ])
+    n, E = rows.shape
+    src = torch.from_numpy(rows).cuda()
+    rb = kvm_lib.row_bytes(type_id, E)
+    dst = torch.zeros(n * rb, dtype=torch.uint8, device="cuda")
+    kvm_lib.quantize_rows(type_id, src.data_ptr(), n, E, dst.data_ptr())
+    got = dst.cpu().numpy().reshape(n, rb)
+    want = oracle.quantize_rows_f16(type_id, rows)
+    assert np.array_equal(got, want)
+    if type_id != 1:
+        # against the third-party golden bytes too (same -0.0 caveat as the oracle test)
+        name = {8: "q8_0", 2: "q4_0", 6: "q5_0"}[type_id]
+        gold = g[name]
+        k = gold.shape[0]
+        blk = g["rows_f16"].view(np.float16).astype(np.float32).reshape(k, -1, 32)
+        neg0 = np.all(blk == 0, axis=2) & np.signbit(blk[:, :, 0])
+        bs = {8: 34, 2: 18, 6: 22}[type_id]
+        differ = np.any(got[:k].reshape(k, -1, bs) != gold.reshape(k, -1, bs), axis=2)
+        assert not np.any(differ & ~neg0)
+
+
+def test_quantize_rows_wide_and_narrow(kvm_lib, oracle):
+    torch = _cuda()
+    rng = np.random.default_rng(9)
+    for E in (32, 96, 1024, 4096):
+        rows = oracle.synth_f16(rng, (19, E), E)
+        src = torch.from_numpy(rows).cuda()
+        for t in (8, 2, 6):
+            rb = kvm_lib.row_bytes(t, E)
+            dst = torch.zeros(19 * rb, dtype=torch.uint8, device="cuda")
+            kvm_lib.quantize_rows(t, src.data_ptr(), 19, E, dst.data_ptr())
+            assert np.array_equal(dst.cpu().numpy().reshape(19, rb),
+                                  oracle.quantize_rows_f16(t, rows)), (E, t)
+
+
+# --------------------------------------------------------------- scorer ---
+
+def test_score_bitexact_uploaded_summaries(kvm_lib, oracle):
+    torch = _cuda()
+    rng = np.random.default_rng(21)
+    L, B, Hkv, D, Hq = 3, 300, 4, 64, 12
+    E = Hkv * D
+    cfg = kvm_lib.default_config(n_layer=L, n_head_kv=Hkv, head_dim=D, n_head_q=Hq,
+                                 max_blocks=512, block_tokens=128, select_budget=128 * 32,
+                                 gen_reserve=128 * 8)
+    s = kvm_lib.Session(cfg, 0)
+    s.register_append(B * 128 - 77)
+    sums = (rng.standard_normal((L, B, E)) * 40).astype(np.float32)
+    cnt = np.full((L, B), 128, np.uint32)
+    cnt[:, -1] = 128 - 77
+    cnt[2, 5] = 0                                    # no statistics in one layer
+    for l in range(L):
+        s.upload_summaries(l, 0, sums[l], cnt[l])
+    q = rng.standard_normal((L, Hq * D)).astype(np.float32)
+    qc = np.array([1, 2, 0], np.uint32)
+    s.set_query(torch.from_numpy(q).cuda(), qc)
+    s.score()
+    got = s.scores()
+    has = np.ones(B, np.uint8)
+    want = oracle.score(sums, cnt, has, q, qc, Hkv, Hq, D)
+    assert got.tobytes() == want.tobytes()
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
+    assert rel.max() <= 1e-4
+
+
+def test_score_from_summarize_kernel(kvm_lib, oracle):
+    shape = Shape(n_layer=2, n_blocks=70, block_tokens=32, partial_tokens=9)
+    rig = make_rig(shape, seed=3)
+    om = OracleModel(rig)
+    q, qc = make_query(shape, np.random.default_rng(4))
+    rig.sess.set_query(q, qc)
+    rig.sess.score()
+    assert rig.sess.scores().tobytes() == om.score(q, qc).tobytes()
+
+
+# ------------------------------------------------------------- selection ---
+
+@pytest.mark.parametrize("seed", range(6))
+def test_select_matches_oracle(kvm_lib, oracle, seed):
+    rng = np.random.default_rng(100 + seed)
+    n = int(rng.integers(1, 3000))
+    budget = int(rng.integers(1, 400))
+    sink, recent = int(rng.integers(0, 4)), int(rng.integers(0, 4))
+    if sink + recent > budget:
+        sink = recent = 0
+    cfg = kvm_lib.default_config(block_tokens=128, select_budget=budget * 128,
+                                 gen_reserve=128, sink_blocks=sink, recent_blocks=recent,
+                                 max_blocks=4096)
+    s = kvm_lib.Session(cfg, 0)
+    s.register_append(n * 128)
+    ocfg = oracle.make_cfg(128, budget, sink, recent)
+    for trial in range(5):
+        scores = rng.standard_normal(n)
+        if trial == 1:
+            scores = np.round(scores * 3) / 3            # many exact ties
+        if trial == 2:
+            scores[:] = 0.0
+            scores[rng.integers(0, n, n // 3)] = -0.0    # +0 / -0 compare equal
+        if trial == 3:
+            scores = np.abs(scores) * 1e-300             # subnormal / tiny
+        mand = rng.integers(0, n + 5, size=int(rng.integers(0, 40))).astype(np.uint32)
+        s.set_scores(scores)
+        s.select(mand)
+        got = s.plan()["selected"]
+        want = oracle.pick_topk(ocfg, scores, mand)
+        assert np.array_equal(got, want), (trial, n, budget)
+
+
+def test_select_empty_and_all_fit(kvm_lib, oracle):
+    cfg = kvm_lib.default_config(block_tokens=128, select_budget=128 * 100, max_blocks=256)
+    s = kvm_lib.Session(cfg, 0)
+    s.set_scores(np.zeros(0))
+    s.select([])
+    s.diff()
+    assert s.plan()["selected"].size == 0
+    s.register_append(3 * 128)
+    s.set_scores(np.array([3.0, 1.0, 2.0]))
+    s.select([])
+    s.diff()
+    assert s.plan()["selected"].tolist() == [0, 1, 2]
+
+
+# --------------------------------------------------------- diff + layout ---
+
+@pytest.mark.parametrize("imm,osi", [(False, True), (True, True), (False, False)])
+def test_diff_sequence_matches_oracle(kvm_lib, oracle, imm, osi):
+    rng = np.random.default_rng(7 + imm + 2 * osi)
+    n, budget, bt = 200, 40, 32
+    cfg = kvm_lib.default_config(block_tokens=bt, select_budget=budget * bt, gen_reserve=8 * bt,
+                                 sink_blocks=1, recent_blocks=1, max_blocks=256,
+                                 immutable_source_k=int(imm), optimize_stage_in=int(osi),
+                                 immutable_refresh_remaps=2, immutable_refresh_abs_delta_tokens=bt * 30)
+    s = kvm_lib.Session(cfg, 0)
+    s.register_append(n * bt - 5)
+    ocfg = oracle.make_cfg(bt, budget, 1, 1, osi, imm, 2, bt * 30, 262144)
+    blocks = oracle.Blocks.appended(n * bt - 5, bt, tier=oracle.TIER_CPU)
+    prev = None
+    for step in range(8):
+        scores = rng.standard_normal(n)
+        if prev is not None and step % 2:
+            scores[prev] += 1.0                          # overlap with the previous selection
+        mand = rng.integers(0, n, size=3).astype(np.uint32)
+        s.set_scores(scores)
+        s.select(mand)
+        s.diff()
+        got = s.plan()
+        sel = oracle.pick_topk(ocfg, scores, mand)
+        before = blocks.gpu_slot.copy()
+        if not osi:
+            before[:] = -1
+        plan = oracle.set_selection(ocfg, blocks, sel)
+        slot_after, moves, cold = oracle.layout(sel, before)
+        blocks.gpu_slot[:] = slot_after
+        blocks.tier[(slot_after < 0) & (blocks.tier == oracle.TIER_GPU)] = oracle.TIER_CPU
+        blocks.tier[sel] = oracle.TIER_GPU
+        assert np.array_equal(got["selected"], sel)
+        assert np.array_equal(got["stage_in"], plan.stage_in)
+        assert np.array_equal(got["stage_out"], plan.stage_out)
+        for f in ("rm_block_id", "rm_n_tokens", "rm_from_base", "rm_to_base",
+                  "rm_working_k_resident", "rm_skip", "rm_raw_refresh"):
+            assert np.array_equal(got[f], getattr(plan, f)), f
+        assert (got["total_window_tokens"], got["selection_overlap_blocks"],
+                got["gpu_reused_blocks"], got["retained_position_stable"],
+                got["retained_position_moved"]) == plan.counters()
+        assert np.array_equal(np.stack([got["mv_block"], got["mv_from"], got["mv_to"]], 1)
+                              .astype(np.int64), moves.astype(np.int64))
+        assert np.array_equal(np.stack([got["cold_block"], got["cold_to"]], 1).astype(np.int64),
+                              cold.astype(np.int64))
+        prev = sel
+
+
+# ------------------------------------------------------ full reselection ---
+
+def _check_window(rig, om):
+    mk, mv = om.window_valid_mask()
+    gk = rig.win_k.cpu().numpy()
+    gv = rig.win_v.cpu().numpy()
+    assert np.array_equal(gk[:, mk], om.win_k[:, mk])
+    assert np.array_equal(gv[:, mv], om.win_v[:, mv])
+
+
+@pytest.mark.parametrize("tk,tv", [(8, 8), (8, 2), (6, 6), (1, 1)])
+def test_step_window_bytes(kvm_lib, oracle, tk, tv):
+    shape = Shape(n_layer=2, n_blocks=64, block_tokens=32, budget_blocks=12, gen_blocks=4,
+                  type_k=tk, type_v=tv, partial_tokens=20)
+    rig = make_rig(shape, seed=11)
+    om = OracleModel(rig)
+    rng = np.random.default_rng(12)
+    q, qc = make_query(shape, rng)
+    for step in range(4):
+        if step:
+            q2, _ = make_query(shape, rng)
+            q = (0.8 * q + 0.6 * q2).astype(np.float32)  # overlapping selections
+        rig.sess.set_query(q, qc)
+        rig.sess.step(rig.src, rig.k_bases(), rig.v_bases(), mandatory=[shape.n_blocks - 1])
+        _, sel, plan, moves, cold = om.step(q, qc, [shape.n_blocks - 1])
+        got = rig.sess.plan()
+        assert np.array_equal(got["selected"], sel)
+        assert np.array_equal(np.stack([got["mv_block"], got["mv_from"], got["mv_to"]], 1)
+                              .astype(np.int64), moves.astype(np.int64))
+        _check_window(rig, om)
+        if step:
+            assert moves.shape[0] > 0 or cold.shape[0] < sel.size
+
+
+def test_step_host_source(kvm_lib, oracle):
+    torch = _cuda()
+    shape = Shape(n_layer=2, n_blocks=48, block_tokens=32, budget_blocks=10, gen_blocks=2)
+    rig = make_rig(shape, seed=5)
+    om = OracleModel(rig)
+    L, B, T, E = shape.n_layer, shape.n_blocks, shape.block_tokens, shape.n_embd
+    hk = torch.from_numpy(rig.k_np).pin_memory()
+    hv = torch.from_numpy(rig.v_np).pin_memory()
+    src = kvm_lib.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2,
+                              location=kvm_lib.LOC_HOST)
+    rng = np.random.default_rng(6)
+    q, qc = make_query(shape, rng)
+    for step in range(3):
+        if step:
+            q = (0.7 * q + 0.7 * make_query(shape, rng)[0]).astype(np.float32)
+        rig.sess.set_query(q, qc)
+        rig.sess.step(src, rig.k_bases(), rig.v_bases())
+        om.step(q, qc)
+        rig.sess.wait()
+        _check_window(rig, om)
+
+
+def test_resident_append_and_reset(kvm_lib, oracle):
+    shape = Shape(n_layer=1, n_blocks=40, block_tokens=32, budget_blocks=8, gen_blocks=4)
+    rig = make_rig(shape, seed=8)
+    q, qc = make_query(shape, np.random.default_rng(1))
+    rig.sess.set_query(q, qc)
+    rig.sess.step(rig.src, rig.k_bases(), rig.v_bases())
+    p = rig.sess.plan()
+    assert p["selected"].size == 8
+    # a decode block written by the model lands in the first free slot (8)
+    rig.sess.register_append(32, resident=True)
+    rig.sess.reset_window()
+    rig.sess.wait()
