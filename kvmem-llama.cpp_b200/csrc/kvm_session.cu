@@ -1026,9 +1026,9 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     // device work list: identity block ids / slots, per-item row counts
     uint32_t *d_list = nullptr;
     uint8_t **d_dst_arr = nullptr;
-    const size_t list_bytes = 3ull * n_items * sizeof(uint32_t);
+    const size_t list_bytes = (3ull * n_items * sizeof(uint32_t) + 255u) & ~static_cast<size_t>(255u);
     if (cudaMalloc(&d_list, list_bytes + 256) != cudaSuccess) return KVM_ENOMEM;
-    d_dst_arr = reinterpret_cast<uint8_t **>(reinterpret_cast<uint8_t *>(d_list) + list_bytes + 0);
+    d_dst_arr = reinterpret_cast<uint8_t **>(reinterpret_cast<uint8_t *>(d_list) + list_bytes);
     std::vector<uint32_t> h(3ull * n_items);
     for (uint32_t i = 0; i < n_items; ++i) {
         h[i] = i;
@@ -1038,7 +1038,8 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     }
     cudaStream_t st = as_stream(stream);
     uint8_t *dst_ptrs[2] = {static_cast<uint8_t *>(d_dst), static_cast<uint8_t *>(d_dst)};
-    cudaError_t e = cudaMemcpyAsync(d_list, h.data(), list_bytes, cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaMemcpyAsync(d_list, h.data(), h.size() * sizeof(uint32_t),
+                                    cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_dst_arr, dst_ptrs, sizeof dst_ptrs, cudaMemcpyHostToDevice, st);
     StageinArgs a{};
     a.cold_block = d_list;
