@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--config", type=int, choices=(1, 2), default=2,
+                    help="2: BASELINE configs[1] (16 layers, the bench line); "
+                         "1: configs[0] (one layer, the small profiling case)")
     return ap.parse_args()
 
 
@@ -206,6 +209,8 @@ def run_kvm(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     c = dict(CFG2)
+    if args.config == 1:
+        c["n_layer"] = 1
     L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
     E = c["n_head_kv"] * c["head_dim"]
     seed = args.seed + 1000 * rank
@@ -303,8 +308,8 @@ def run_kvm(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16->q8_0",
         "data": "synthetic: seeded N(0,1) F16 K/V, 1% outlier channels x20, new seeded query per step",
-        "config": {"workload": "config 2: 16 attention layers x 2048 blocks x 128 tokens "
-                               "(262144-token history), 4 KV heads x 256, 24 Q heads, "
+        "config": {"workload": f"config {args.config}: {L} attention layer(s) x 2048 blocks x "
+                               "128 tokens (262144-token history), 4 KV heads x 256, 24 Q heads, "
                                "budget 32768 (256 blocks), gen-reserve 16384, sink 1, q8_0 K+V, "
                                "cold window (256 blocks staged per step)",
                    "sessions_per_gpu": 1, "parallelism": f"sessions x{world} (no collective)",

@@ -193,6 +193,14 @@ uint64_t kvm_row_bytes(int32_t type, uint32_t n_embd);
  * with kvm_get_plan.  The device block table is updated on `stream`. */
 kvm_status kvm_register_append(kvm_session *s, kvm_stream stream, uint32_t n_new_tokens,
                                int resident);
+/* KvMemStore::set_block_tier (kvmem_store.cpp:250-276): a tier other than
+ * GPU also drops the block's window slot.  Stream-ordered. */
+kvm_status kvm_set_block_tier(kvm_session *s, kvm_stream stream, uint32_t block_id,
+                              int32_t tier);
+/* KvMemStore::set_block_gpu_slot (kvmem_store.cpp:278-281): record that the
+ * block's rows are in window slot `slot` (-1 = none).  Stream-ordered. */
+kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t block_id,
+                                  int32_t slot);
 /* KvMemStore::clear_working_set + drop every window slot: the next step
  * treats the window as empty (cold).  Stream-ordered on `stream`. */
 kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream);

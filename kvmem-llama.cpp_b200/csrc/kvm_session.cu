@@ -462,9 +462,9 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
     if (!type_ok(c.type_k) || !type_ok(c.type_v)) return bad("type_k/type_v must be F16, Q8_0, Q4_0 or Q5_0");
     const uint32_t budget = align_tokens(c.select_budget, c.block_tokens);
     const uint32_t gen = align_tokens(c.gen_reserve ? c.gen_reserve : 256u, c.block_tokens);
+    // Like KvMemStore, sink + recent beyond the budget is accepted: the pins
+    // are best effort in the selector (kvmem_store.cpp:505-535).
     const uint32_t budget_blocks = budget / c.block_tokens;
-    if (static_cast<uint64_t>(c.sink_blocks) + c.recent_blocks > budget_blocks)
-        return bad("KVMem sink + recent allocation exceeds the selection budget");
     const uint64_t slots = (static_cast<uint64_t>(budget) + gen) / c.block_tokens;
     if (slots > kMaxBlocks) return bad("window slots exceed 65536");
 
@@ -665,6 +665,34 @@ kvm_status kvm_register_append(kvm_session *s, kvm_stream stream, uint32_t n_new
     s->n_blocks = n;
     s->total_tokens = total;
     return KVM_OK;
+}
+
+kvm_status kvm_set_block_tier(kvm_session *s, kvm_stream stream, uint32_t block_id, int32_t tier) {
+    if (!s) return KVM_EINVAL;
+    if (block_id >= s->n_blocks) return KVM_OK;   // the reference ignores unknown ids
+    if (tier != KVM_TIER_GPU && tier != KVM_TIER_CPU && tier != KVM_TIER_SSD)
+        return fail(s, KVM_EINVAL, "bad tier %d", tier);
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    const uint8_t t = static_cast<uint8_t>(tier);
+    kvm_status r = upload_small(s, st, s->bt.tier + block_id, &t, 1);
+    if (r == KVM_OK && tier != KVM_TIER_GPU) {
+        const int32_t none = -1;
+        r = upload_small(s, st, s->bt.gpu_slot + block_id, &none, sizeof none);
+        if (r == KVM_OK && block_id < s->h_slot.size()) s->h_slot[block_id] = -1;
+    }
+    return r;
+}
+
+kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t block_id, int32_t slot) {
+    if (!s) return KVM_EINVAL;
+    if (block_id >= s->n_blocks) return KVM_OK;
+    if (slot >= static_cast<int32_t>(s->n_slots)) return fail(s, KVM_EINVAL, "slot %d >= window slots", slot);
+    DeviceGuard g(s->device);
+    const int32_t v = slot < 0 ? -1 : slot;
+    kvm_status r = upload_small(s, as_stream(stream), s->bt.gpu_slot + block_id, &v, sizeof v);
+    if (r == KVM_OK && block_id < s->h_slot.size()) s->h_slot[block_id] = v;
+    return r;
 }
 
 kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream) {

@@ -31,7 +31,7 @@ _STATUS = {1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESTATE", 6: 
 ABI_SYMBOLS = (
     "kvm_config_default", "kvm_session_create", "kvm_session_destroy", "kvm_last_error",
     "kvm_window_slots", "kvm_block_count", "kvm_row_bytes", "kvm_register_append",
-    "kvm_reset_window", "kvm_upload_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
+    "kvm_reset_window", "kvm_set_block_tier", "kvm_set_block_gpu_slot", "kvm_upload_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
     "kvm_score_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
@@ -118,6 +118,8 @@ def lib():
             "kvm_row_bytes": (u64, [i32, u32]),
             "kvm_register_append": (C.c_int, [vp, vp, u32, C.c_int]),
             "kvm_reset_window": (C.c_int, [vp, vp]),
+            "kvm_set_block_tier": (C.c_int, [vp, vp, u32, i32]),
+            "kvm_set_block_gpu_slot": (C.c_int, [vp, vp, u32, i32]),
             "kvm_upload_summaries": (C.c_int, [vp, vp, u32, u32, u32, vp, vp]),
             "kvm_summarize": (C.c_int, [vp, vp, u32, u32, u32, u32, C.POINTER(Source)]),
             "kvm_set_query": (C.c_int, [vp, vp, vp, vp]),
@@ -232,6 +234,14 @@ class Session:
     def register_append(self, n_tokens: int, resident: bool = False, stream=None):
         self._check(lib().kvm_register_append(self.h, _stream(stream), n_tokens, int(resident)),
                     "register_append")
+
+    def set_block_tier(self, block_id, tier, stream=None):
+        self._check(lib().kvm_set_block_tier(self.h, _stream(stream), block_id, tier),
+                    "set_block_tier")
+
+    def set_block_gpu_slot(self, block_id, slot, stream=None):
+        self._check(lib().kvm_set_block_gpu_slot(self.h, _stream(stream), block_id, slot),
+                    "set_block_gpu_slot")
 
     def reset_window(self, stream=None):
         self._check(lib().kvm_reset_window(self.h, _stream(stream)), "reset_window")

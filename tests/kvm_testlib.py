@@ -66,7 +66,7 @@ def make_rig(shape: Shape, seed: int = 0, device: int = 0, outlier_channels=None
         block_tokens=T, select_budget=shape.budget_blocks * T, gen_reserve=shape.gen_blocks * T,
         sink_blocks=shape.sink_blocks, recent_blocks=shape.recent_blocks, n_layer=L,
         n_head_kv=shape.n_head_kv, head_dim=shape.head_dim, n_head_q=shape.n_head_q,
-        max_blocks=max(B, 4), type_k=shape.type_k, type_v=shape.type_v)
+        max_blocks=B + 8, type_k=shape.type_k, type_v=shape.type_v)
     sess = kvm.Session(cfg, device)
     dev = torch.device("cuda", device)
     k = O.synth_f16(rng, (L, B, T, E), E, outlier_channels=outlier_channels)

@@ -50,9 +50,11 @@ def test_host_only_calls_without_gpu():
     assert kvm.row_bytes(kvm.TYPE_F16, 1024) == 2048
     # invalid configurations are rejected before any device work
     h = C.c_void_p()
-    bad = kvm.default_config(sink_blocks=5, recent_blocks=5, select_budget=128 * 8)
+    bad = kvm.default_config(max_blocks=0)
     assert L.kvm_session_create(C.byref(bad), 0, C.byref(h)) == kvm.KVM_EINVAL
-    assert b"sink + recent" in L.kvm_last_error(None)
+    assert b"max_blocks" in L.kvm_last_error(None)
+    bad = kvm.default_config(type_k=3)
+    assert L.kvm_session_create(C.byref(bad), 0, C.byref(h)) == kvm.KVM_EINVAL
     bad = kvm.default_config(n_head_kv=3, head_dim=10)
     assert L.kvm_session_create(C.byref(bad), 0, C.byref(h)) == kvm.KVM_EINVAL
     assert L.kvm_session_create(None, 0, C.byref(h)) == kvm.KVM_EINVAL

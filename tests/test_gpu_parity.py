@@ -264,7 +264,21 @@ def test_resident_append_and_reset(kvm_lib, oracle):
     rig.sess.step(rig.src, rig.k_bases(), rig.v_bases())
     p = rig.sess.plan()
     assert p["selected"].size == 8
-    # a decode block written by the model lands in the first free slot (8)
-    rig.sess.register_append(32, resident=True)
+    # decode tokens written by the model take the first free window slots (8, 9)
+    rig.sess.register_append(40, resident=True)
+    assert rig.sess.block_count == 42
+    # the next reselection sees them as resident: selected ones move, others drop
+    rig.sess.set_scores(np.r_[np.zeros(40), 5.0, 4.0])
+    rig.sess.select([])
+    rig.sess.diff()
+    p = rig.sess.plan()
+    assert 40 in p["selected"] and 41 in p["selected"]
+    mv = dict(zip(p["mv_block"].tolist(), zip(p["mv_from"].tolist(), p["mv_to"].tolist())))
+    assert mv[40][0] == 8 and mv[41][0] == 9
+    assert 40 not in p["cold_block"] and 41 not in p["cold_block"]
     rig.sess.reset_window()
-    rig.sess.wait()
+    rig.sess.set_scores(np.zeros(42))
+    rig.sess.select([])
+    rig.sess.diff()
+    p = rig.sess.plan()
+    assert p["mv_block"].size == 0 and p["cold_block"].size == 8
