@@ -9,8 +9,9 @@
 
 namespace kvm {
 
-constexpr int kStageinThreads = 256;
-constexpr int kStageinStages = 4;
+constexpr int kStageinConsumerWarps = 8;
+constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
+constexpr int kStageinStages = 3;
 constexpr int kPermuteThreads = 256;
 constexpr int kSelectThreads = 1024;
 constexpr int kDiffThreads = 1024;

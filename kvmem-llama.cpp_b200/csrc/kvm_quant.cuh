@@ -1,15 +1,21 @@
-// kvm_quant.cuh -- ggml q8_0 / q4_0 / q5_0 block quantizers for a warp.
+// kvm_quant.cuh -- ggml q8_0 / q4_0 / q5_0 block quantizers, one thread per
+// 32-value block.
 //
-// One 32-value ggml block is handled by 4 consecutive lanes (sub = lane & 3),
-// each holding 8 consecutive values.  The arithmetic is the reference's
-// (src/adapter/llama-kvmem-stagein.cu:180-233, ggml's quantize_row_*_ref):
+// The arithmetic is the reference's (src/adapter/llama-kvmem-stagein.cu:180-233,
+// ggml's quantize_row_*_ref):
 //   q8_0: d = amax/127, id = d ? 1/d : 0, q = roundf(x*id)
 //   q4_0: vmax = first value of largest |x|, d = vmax/-8, q = min(15, (int)(x*id + 8.5))
 //   q5_0: d = vmax/-16, q = min(31, (int)(x*id + 16.5)), bit 4 of q_i -> bit i of qh
-// with every operation an IEEE round-to-nearest intrinsic (no FMA
-// contraction, no fast reciprocals) so the bytes match the CPU bit for bit.
-// All 32 lanes of the warp must call these (they shuffle); `active` masks the
-// shared-memory stores of lanes without a block.
+// Every float operation is an IEEE round-to-nearest intrinsic (no FMA
+// contraction, no approximate reciprocal), so the bytes match the CPU bit for
+// bit.
+//
+// Data arrive as four 16-byte chunks (8 halves each).  A lane loads the
+// chunks of its block in a lane-dependent rotation (chunk c[k] at step k) so
+// that the 128-bit shared-memory loads of a quarter warp hit 8 different
+// bank groups; the chunk index is then only used as an output offset --
+// the max is order-free, each value is coded independently, and the q4/q5
+// nibble partner of chunk c (c+2 mod 4) is always the register k+2 mod 4.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -32,149 +38,182 @@ __device__ __forceinline__ void st_u16(uint8_t *p, uint32_t v) {
     *reinterpret_cast<uint16_t *>(p) = static_cast<uint16_t>(v);
 }
 
-// 8 halves (one uint4) -> 8 floats, exact.
-__device__ __forceinline__ void unpack8(const uint4 raw, float v[8]) {
-    const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(h[k]);
-        v[2 * k] = f.x;
-        v[2 * k + 1] = f.y;
-    }
-}
-
 __device__ __forceinline__ uint32_t f16_bits(float d) {
     return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(d)));
 }
 
-// q8_0: blk = start of the 34-byte block in shared memory.
-__device__ __forceinline__ void quant_q8_0_part(const float v[8], int sub, uint8_t *blk,
-                                                bool active) {
-    float amax = 0.0f;
+// C roundf (round half away from zero) as an integer for |x| < 2^23:
+// truncate x + copysign(0.49999997, x).  Adding the largest float below 0.5
+// instead of 0.5 keeps the sum exact or correctly rounded on both sides of
+// every half-integer; equality with roundf was checked for every float of
+// magnitude below 2^23.  q8_0 codes are at most 127.x in magnitude.
+__device__ __forceinline__ int round_half_away(float x) {
+    return __float2int_rz(__fadd_rn(x, copysignf(0x1.fffffep-2f, x)));
+}
+
+struct Block32 {
+    uint4 raw[4];      // raw[k] = chunk cidx(k) of the block (8 halves)
+    int c0;            // chunk index of raw[0]; raw[k] holds chunk (c0 + k) & 3
+};
+
+__device__ __forceinline__ int chunk_of(const Block32 &b, int k) { return (b.c0 + k) & 3; }
+
+__device__ __forceinline__ const __half2 *halves(const uint4 &r) {
+    return reinterpret_cast<const __half2 *>(&r);
+}
+
+__device__ __forceinline__ float absmax32(const Block32 &b) {
+    __half2 m = __habs2(halves(b.raw[0])[0]);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int i = (k == 0 ? 1 : 0); i < 4; ++i) m = __hmax2(m, __habs2(halves(b.raw[k])[i]));
+    }
+    return fmaxf(__low2float(m), __high2float(m));
+}
+
+// Signed value of the first element (in block order) whose magnitude equals
+// amax: the reference's strict `amax < |v|` scan.  +0.0 when amax is 0.
+__device__ __forceinline__ float first_of_absmax(const Block32 &b, float amax) {
+    if (amax == 0.0f) return 0.0f;
+    float best = 0.0f;
+    int best_c = 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float v = 0.0f;
+        bool hit = false;
+#pragma unroll
+        for (int i = 3; i >= 0; --i) {
+            const float2 x = __half22float2(halves(b.raw[k])[i]);
+            const bool hy = fabsf(x.y) == amax;
+            const bool hx = fabsf(x.x) == amax;
+            v = hy ? x.y : v;
+            v = hx ? x.x : v;
+            hit = hit || hx || hy;
+        }
+        const int c = chunk_of(b, k);
+        const bool take = hit && c < best_c;
+        best = take ? v : best;
+        best_c = take ? c : best_c;
+    }
+    return best;
+}
+
+// q8_0: 34 bytes = f16 d + 32 int8 codes.
+__device__ __forceinline__ void quant_q8_0(const Block32 &b, uint8_t *blk) {
+    const float amax = absmax32(b);
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    if (!active) return;
-    if (sub == 0) st_u16(blk, f16_bits(d));
+    st_u16(blk, f16_bits(d));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half2 *h = halves(b.raw[k]);
+        uint32_t w[2];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const float2 a = __half22float2(h[2 * p]);
+            const float2 c = __half22float2(h[2 * p + 1]);
+            const uint32_t q0 = static_cast<uint32_t>(round_half_away(__fmul_rn(a.x, id))) & 0xffu;
+            const uint32_t q1 = static_cast<uint32_t>(round_half_away(__fmul_rn(a.y, id))) & 0xffu;
+            const uint32_t q2 = static_cast<uint32_t>(round_half_away(__fmul_rn(c.x, id))) & 0xffu;
+            const uint32_t q3 = static_cast<uint32_t>(round_half_away(__fmul_rn(c.y, id))) & 0xffu;
+            w[p] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+        }
+        uint8_t *qs = blk + 2 + 8 * chunk_of(b, k);
+        st_u16(qs, w[0] & 0xffffu);
+        st_u16(qs + 2, w[0] >> 16);
+        st_u16(qs + 4, w[1] & 0xffffu);
+        st_u16(qs + 6, w[1] >> 16);
+    }
+}
+
+// Nibble / 5-bit code of one value: min(maxq, (int)(x*id + off)).
+__device__ __forceinline__ uint32_t code_q(float x, float id, float off, int maxq) {
+    const int q = __float2int_rz(__fadd_rn(__fmul_rn(x, id), off));
+    return static_cast<uint32_t>(q > maxq ? maxq : q);
+}
+
+// 8 codes of one chunk: code m (q & 15) at bits 4m of `nib`, bit 4 of the
+// code at bit m of `hi` (q5_0).
+__device__ __forceinline__ void chunk_codes(const uint4 &r, float id, float off, int maxq,
+                                            uint32_t &nib, uint32_t &hi) {
+    const __half2 *h = halves(r);
+    nib = 0;
+    hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 x = __half22float2(h[i]);
+        const uint32_t c0 = code_q(x.x, id, off, maxq);
+        const uint32_t c1 = code_q(x.y, id, off, maxq);
+        nib |= ((c0 & 15u) << (8 * i)) | ((c1 & 15u) << (8 * i + 4));
+        hi |= ((c0 >> 4) << (2 * i)) | ((c1 >> 4) << (2 * i + 1));
+    }
+}
+
+// Interleave two chunks' nibbles into the 8 bytes j | (j+16) << 4.
+__device__ __forceinline__ void store_nibble_pairs(uint8_t *qs, uint32_t lo, uint32_t hi) {
+    // lo/hi hold code m at bits 4m; byte m = lo_m | hi_m << 4
     uint32_t b[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int q = static_cast<int>(roundf(__fmul_rn(v[k], id)));
-        b[k] = static_cast<uint32_t>(q) & 0xffu;
-    }
-    uint8_t *qs = blk + 2 + sub * 8;
+    for (int m = 0; m < 8; ++m) b[m] = ((lo >> (4 * m)) & 15u) | (((hi >> (4 * m)) & 15u) << 4);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) st_u16(qs + 2 * k, b[2 * k] | (b[2 * k + 1] << 8));
+    for (int m = 0; m < 8; m += 2) st_u16(qs + m, b[m] | (b[m + 1] << 8));
 }
 
-// Signed value of the first element of largest magnitude across the 4 lanes
-// (strict `amax < |v|` scan in index order; ties resolve to the lower index).
-__device__ __forceinline__ float group_first_absmax(const float v[8], int sub) {
-    float amax = 0.0f;
-    float vmax = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const float a = fabsf(v[k]);
-        if (amax < a) {
-            amax = a;
-            vmax = v[k];
-        }
-    }
-#pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, vmax, o);
-        const bool other_first = (sub ^ o) < sub;
-        if (oa > amax || (oa == amax && other_first)) {
-            amax = oa;
-            vmax = ov;
-        }
-    }
-    return vmax;
-}
-
-// q4_0: blk = start of the 18-byte block.
-__device__ __forceinline__ void quant_q4_0_part(const float v[8], int sub, uint8_t *blk,
-                                                bool active) {
-    const float vmax = group_first_absmax(v, sub);
-    const float d = __fdiv_rn(vmax, -8.0f);
+// q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes).
+template <bool Q5>
+__device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
+    const float amax = absmax32(b);
+    const float vmax = first_of_absmax(b, amax);
+    const float d = __fdiv_rn(vmax, Q5 ? -16.0f : -8.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t packed = 0;
+    const float off = Q5 ? 16.5f : 8.5f;
+    const int maxq = Q5 ? 31 : 15;
+    uint32_t nib[4], hb[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        int q = __float2int_rz(__fadd_rn(__fmul_rn(v[k], id), 8.5f));
-        q = q > 15 ? 15 : q;
-        packed |= (static_cast<uint32_t>(q) & 15u) << (4 * k);
+    for (int k = 0; k < 4; ++k) chunk_codes(b.raw[k], id, off, maxq, nib[k], hb[k]);
+    st_u16(blk, f16_bits(d));
+    uint8_t *qs = blk + (Q5 ? 6 : 2);
+    uint32_t qh = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        // chunks k and k+2 are a nibble pair; the lower chunk index is byte 8*c
+        const int ca = chunk_of(b, k);
+        const bool a_low = ca < 2;
+        const uint32_t lo = a_low ? nib[k] : nib[k + 2];
+        const uint32_t hi = a_low ? nib[k + 2] : nib[k];
+        store_nibble_pairs(qs + 8 * (a_low ? ca : chunk_of(b, k + 2)), lo, hi);
     }
-    // element j (j < 16) pairs with element j + 16, held by lane sub ^ 2
-    const uint32_t partner = __shfl_xor_sync(0xffffffffu, packed, 2);
-    if (!active) return;
-    if (sub == 0) st_u16(blk, f16_bits(d));
-    if (sub < 2) {
-        uint8_t *qs = blk + 2 + sub * 8;
+    if (Q5) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t b0 = ((packed >> (8 * k)) & 15u) | (((partner >> (8 * k)) & 15u) << 4);
-            const uint32_t b1 = ((packed >> (8 * k + 4)) & 15u) |
-                                (((partner >> (8 * k + 4)) & 15u) << 4);
-            st_u16(qs + 2 * k, b0 | (b1 << 8));
-        }
+        for (int k = 0; k < 4; ++k) qh |= hb[k] << (8 * chunk_of(b, k));
+        st_u16(blk + 2, qh & 0xffffu);
+        st_u16(blk + 4, qh >> 16);
     }
 }
 
-// q5_0: blk = start of the 22-byte block (d, qh[4], qs[16]).
-__device__ __forceinline__ void quant_q5_0_part(const float v[8], int sub, uint8_t *blk,
-                                                bool active) {
-    const float vmax = group_first_absmax(v, sub);
-    const float d = __fdiv_rn(vmax, -16.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t packed = 0;
-    uint32_t hi = 0;
+// Load block `qb` of a tile (64 bytes per block in shared memory) with the
+// lane rotation, so a quarter warp reads 8 different 16-byte bank groups.
+__device__ __forceinline__ void load_block(const uint8_t *tile, uint32_t qb, int lane, Block32 &b) {
+    b.c0 = (lane >> 1) & 3;
+    const uint8_t *p = tile + static_cast<size_t>(qb) * 64u;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        int q = __float2int_rz(__fadd_rn(__fmul_rn(v[k], id), 16.5f));
-        q = q > 31 ? 31 : q;
-        packed |= (static_cast<uint32_t>(q) & 15u) << (4 * k);
-        hi |= ((static_cast<uint32_t>(q) >> 4) & 1u) << (sub * 8 + k);
-    }
-    hi |= __shfl_xor_sync(0xffffffffu, hi, 1);
-    hi |= __shfl_xor_sync(0xffffffffu, hi, 2);
-    const uint32_t partner = __shfl_xor_sync(0xffffffffu, packed, 2);
-    if (!active) return;
-    if (sub == 0) {
-        st_u16(blk, f16_bits(d));
-        st_u16(blk + 2, hi & 0xffffu);
-        st_u16(blk + 4, hi >> 16);
-    }
-    if (sub < 2) {
-        uint8_t *qs = blk + 6 + sub * 8;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t b0 = ((packed >> (8 * k)) & 15u) | (((partner >> (8 * k)) & 15u) << 4);
-            const uint32_t b1 = ((packed >> (8 * k + 4)) & 15u) |
-                                (((partner >> (8 * k + 4)) & 15u) << 4);
-            st_u16(qs + 2 * k, b0 | (b1 << 8));
-        }
-    }
+    for (int k = 0; k < 4; ++k) b.raw[k] = *reinterpret_cast<const uint4 *>(p + 16 * ((b.c0 + k) & 3));
 }
 
-// Quantize the 8 values of lane `sub` of ggml block `qb` into `out`
-// (type-dispatched; warp-uniform type).  For F16 the 8 halves are copied.
-__device__ __forceinline__ void quant_part(int type, const uint4 raw, int sub, uint8_t *out_tile,
-                                           uint32_t qb, bool active) {
-    float v[8];
-    unpack8(raw, v);
+// One 32-value block of `type` into out_tile (block qb).
+__device__ __forceinline__ void quant_block(int type, const Block32 &b, uint8_t *out_tile, uint32_t qb) {
     if (type == KVM_TYPE_Q8_0) {
-        quant_q8_0_part(v, sub, out_tile + static_cast<size_t>(qb) * kBlockBytesQ8, active);
+        quant_q8_0(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ8);
     } else if (type == KVM_TYPE_Q4_0) {
-        quant_q4_0_part(v, sub, out_tile + static_cast<size_t>(qb) * kBlockBytesQ4, active);
+        quant_q4q5<false>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ4);
     } else if (type == KVM_TYPE_Q5_0) {
-        quant_q5_0_part(v, sub, out_tile + static_cast<size_t>(qb) * kBlockBytesQ5, active);
-    } else if (active) {
-        *reinterpret_cast<uint4 *>(out_tile + static_cast<size_t>(qb) * 64 + sub * 16) = raw;
+        quant_q4q5<true>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ5);
+    } else {
+        uint8_t *o = out_tile + static_cast<size_t>(qb) * 64u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<uint4 *>(o + 16 * chunk_of(b, k)) = b.raw[k];
     }
 }
 

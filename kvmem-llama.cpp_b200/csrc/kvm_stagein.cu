@@ -90,12 +90,34 @@ __device__ __forceinline__ void issue_tile_load(const StageinArgs &a, const Task
 
 }  // namespace
 
-template <int NSTAGE>
-__global__ void __launch_bounds__(kStageinThreads, 2) stagein_kernel(StageinArgs a) {
+// Per-stage tile description, written by the producer before it arms the
+// stage's `full` barrier (release) and read by consumers after their wait
+// (acquire).  rows == 0 marks the end of this CTA's work.
+struct TileSlot {
+    uint8_t *dst;
+    uint32_t rows;
+    int32_t type;
+    uint32_t out_bytes;
+    uint32_t pad;
+};
+static_assert(sizeof(TileSlot) == 24, "TileSlot");
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Shared memory: [0,128) barriers (full[NS], done[NS]); [128,384) tile slots;
+// then NS input tiles and NS output tiles.
+constexpr uint32_t kStageinHeader = 384;
+
+template <int NS>
+__global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint8_t *in_buf = smem + 128;
-    uint8_t *out_buf = in_buf + NSTAGE * a.tile_in_bytes;
+    uint64_t *done = full + NS;
+    TileSlot *slot = reinterpret_cast<TileSlot *>(smem + 128);
+    uint8_t *in_buf = smem + kStageinHeader;
+    uint8_t *out_buf = in_buf + NS * a.tile_in_bytes;
 
     const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
     const uint32_t n_items = min(n_items_raw, a.max_items);
@@ -104,92 +126,121 @@ __global__ void __launch_bounds__(kStageinThreads, 2) stagein_kernel(StageinArgs
     if (static_cast<uint64_t>(blockIdx.x) >= total) return;
 
     const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < NSTAGE; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&done[s], kStageinConsumerWarps);
+        }
         fence_mbar_init();
     }
-    __syncthreads();
+    __syncthreads();   // the only CTA-wide barrier
 
-    // Producer state (thread 0 only): next task to consider, loads issued.
-    uint64_t ptask = blockIdx.x;
-    uint32_t issued = 0;
-    if (tid == 0) {
-        while (issued < NSTAGE && ptask < total) {
-            const TaskDesc d = decode_task(a, ptask, tiles, n_items);
-            ptask += gridDim.x;
-            if (!d.valid) continue;
-            issue_tile_load(a, d, in_buf + (issued % NSTAGE) * a.tile_in_bytes,
-                            &full[issued % NSTAGE]);
-            ++issued;
-        }
-    }
-
-    const int lane = tid & 31;
-    const int sub = lane & 3;
-    uint32_t j = 0;  // non-empty tasks consumed
-    bool bad = false;
-    for (uint64_t t = blockIdx.x; t < total; t += gridDim.x) {
-        const TaskDesc d = decode_task(a, t, tiles, n_items);
-        if (!d.valid) continue;
-        const uint32_t stage = j % NSTAGE;
-        const uint32_t ob = j & 1u;
-        const bool ok = mbar_wait_bounded(&full[stage], (j / NSTAGE) & 1u);
-        const uint8_t *ib = in_buf + stage * a.tile_in_bytes;
-        uint8_t *obuf = out_buf + ob * a.tile_out_bytes;
-        const int type = d.kv ? a.type_v : a.type_k;
-        const uint32_t nparts = d.rows * (a.n_embd / 8u);    // 8 values per lane
-        if (ok) {
-            for (uint32_t base = 0; base < nparts; base += kStageinThreads) {
-                const uint32_t p = base + tid;
-                const bool active = p < nparts;
-                uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-                if (active) raw = *reinterpret_cast<const uint4 *>(ib + static_cast<size_t>(p) * 16u);
-                quant_part(type, raw, sub, obuf, p >> 2, active);
-            }
-        }
-        (void)lane;
-        fence_proxy_async_smem();
-        bad = __syncthreads_or(!ok) != 0;
-        if (bad) break;
-        const uint32_t rb = d.kv ? a.row_bytes_v : a.row_bytes_k;
-        const uint32_t out_bytes = d.rows * rb;
-        if (a.bulk_store) {
-            if (tid == 0) {
-                bulk_s2g(d.dst, obuf, out_bytes);
-                bulk_commit();
-            }
-        } else {
-            for (uint32_t o = 2u * tid; o < out_bytes; o += 2u * kStageinThreads) {
-                *reinterpret_cast<uint16_t *>(d.dst + o) =
-                    *reinterpret_cast<const uint16_t *>(obuf + o);
-            }
-        }
-        if (tid == 0) {
-            // refill the stage just consumed
+    if (warp == kStageinConsumerWarps) {
+        // ---------------------------------------------------------- producer
+        uint64_t ptask = blockIdx.x;
+        uint32_t issued = 0;      // tiles armed with data
+        bool ended = false;       // end marker placed
+        // Arm the stage of tile index `issued` with the next task, or with
+        // the end marker when none is left.  Lane 0 only.
+        auto arm_next = [&]() {
+            const uint32_t s = issued % NS;
             while (ptask < total) {
-                const TaskDesc nd = decode_task(a, ptask, tiles, n_items);
+                const TaskDesc d = decode_task(a, ptask, tiles, n_items);
                 ptask += gridDim.x;
-                if (!nd.valid) continue;
-                issue_tile_load(a, nd, in_buf + (issued % NSTAGE) * a.tile_in_bytes,
-                                &full[issued % NSTAGE]);
+                if (!d.valid) continue;
+                TileSlot &ts = slot[s];
+                ts.dst = d.dst;
+                ts.rows = d.rows;
+                ts.type = d.kv ? a.type_v : a.type_k;
+                ts.out_bytes = d.rows * (d.kv ? a.row_bytes_v : a.row_bytes_k);
+                issue_tile_load(a, d, in_buf + s * a.tile_in_bytes, &full[s]);
                 ++issued;
+                return;
+            }
+            slot[s].rows = 0;
+            mbar_arrive(&full[s]);
+            ended = true;
+        };
+        if (lane == 0) {
+            while (!ended && issued < static_cast<uint32_t>(NS)) arm_next();
+        }
+        __syncwarp();   // slot[] written by lane 0 is read by every producer lane
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+        ended = __shfl_sync(0xffffffffu, ended ? 1 : 0, 0) != 0;
+        const uint32_t lag = a.bulk_store ? 1u : 0u;
+        bool bad = false;
+        for (uint32_t j = 0; j < issued; ++j) {
+            const uint32_t s = j % NS;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded(&done[s], (j / NS) & 1u);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) {
+                bad = true;
                 break;
             }
-            // the store issued last iteration must be done reading its buffer
-            // before the next iteration overwrites it
-            if (a.bulk_store) bulk_wait_read<1>();
-        }
-        __syncthreads();
-        ++j;
-    }
-    if (tid == 0) {
-        if (bad) {
-            set_status(a.status, kErrTimeout);
-            for (uint32_t k = j; k < issued; ++k) {
-                (void)mbar_wait_bounded(&full[k % NSTAGE], (k / NSTAGE) & 1u);
+            const TileSlot ts = slot[s];
+            const uint8_t *ob = out_buf + s * a.tile_out_bytes;
+            if (a.bulk_store) {
+                if (lane == 0) {
+                    fence_proxy_async_smem();
+                    bulk_s2g(ts.dst, ob, ts.out_bytes);
+                    bulk_commit();
+                }
+            } else {
+                for (uint32_t o = 2u * lane; o < ts.out_bytes; o += 64u)
+                    *reinterpret_cast<uint16_t *>(ts.dst + o) =
+                        *reinterpret_cast<const uint16_t *>(ob + o);
+                __syncwarp();
             }
+            if (j >= lag && lane == 0 && !ended) {
+                // the stage of tile j - lag is free once its store has read it
+                if (a.bulk_store) bulk_wait_read<1>();
+                arm_next();
+            }
+            __syncwarp();
+            issued = __shfl_sync(0xffffffffu, issued, 0);
+            ended = __shfl_sync(0xffffffffu, ended ? 1 : 0, 0) != 0;
         }
-        if (a.bulk_store) bulk_wait_all<0>();
+        if (lane == 0) {
+            if (bad) {
+                set_status(a.status, kErrTimeout);
+                // bounded wait for loads still landing in this CTA's smem
+                for (int s = 0; s < NS; ++s) {
+                    const uint32_t last = issued > static_cast<uint32_t>(s)
+                                              ? issued - 1 - ((issued - 1 - s) % NS) : 0u;
+                    if (issued > static_cast<uint32_t>(s))
+                        (void)mbar_wait_bounded(&full[s], (last / NS) & 1u);
+                }
+            }
+            if (a.bulk_store) bulk_wait_all<0>();
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------- consumers
+    const uint32_t qb_per_row = a.n_embd / 32u;
+    for (uint32_t j = 0;; ++j) {
+        const uint32_t s = j % NS;
+        if (!mbar_wait_bounded(&full[s], (j / NS) & 1u)) {
+            set_status(a.status, kErrTimeout);
+            break;
+        }
+        const TileSlot ts = slot[s];
+        if (ts.rows == 0) break;
+        const uint8_t *ib = in_buf + s * a.tile_in_bytes;
+        uint8_t *ob = out_buf + s * a.tile_out_bytes;
+        const uint32_t nqb = ts.rows * qb_per_row;
+        for (uint32_t qb = static_cast<uint32_t>(warp * 32 + lane); qb < nqb;
+             qb += kStageinConsumerWarps * 32u) {
+            Block32 b;
+            load_block(ib, qb, lane, b);
+            quant_block(ts.type, b, ob, qb);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&done[s]);
     }
 }
 
@@ -283,7 +334,8 @@ uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens) {
 }
 
 size_t stagein_smem_bytes(const StageinArgs &a) {
-    return 128u + static_cast<size_t>(kStageinStages) * a.tile_in_bytes + 2u * a.tile_out_bytes;
+    return kStageinHeader +
+           static_cast<size_t>(kStageinStages) * (a.tile_in_bytes + a.tile_out_bytes);
 }
 
 // Dynamic shared-memory opt-in is a per-device function attribute: set it
@@ -308,7 +360,10 @@ cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t g
     if (!attr_once(g_stagein_attr, reinterpret_cast<const void *>(stagein_kernel<kStageinStages>),
                    200 * 1024))
         return cudaErrorInvalidValue;
-    int per_sm = smem <= 100 * 1024 ? 2 : 1;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages>,
+                                                  kStageinThreads, smem);
+    if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
