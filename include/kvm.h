@@ -291,6 +291,24 @@ uint64_t kvm_kernel_launches(const kvm_session *s);
 kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
                              uint64_t n_rows, uint32_t n_embd, void *d_dst);
 
+/*
+ * kvm_quantize_rows without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc while they
+ * run -- code being recorded into a CUDA graph, runtimes whose caching
+ * allocator owns all free HBM, latency-critical loops that cannot take the
+ * device-wide synchronisation of cudaMalloc/cudaFree.  Same arguments and
+ * bytes as kvm_quantize_rows; stream-ordered, no host wait.
+ * The work list lives in a fixed device array of 16384 row tiles (a tile is
+ * 8192 / n_embd rows, at most 128: 131072 rows at n_embd 1024); larger calls
+ * return KVM_EINVAL (message in kvm_last_error(NULL)).  The array is shared
+ * by every call in the process, so calls that overlap on the GPU (for
+ * example on two streams) race: serialise them.  The first call on each
+ * device looks the array's device address up (cudaGetSymbolAddress) and
+ * should come before any stream capture.
+ */
+kvm_status kvm_quantize_rows_noalloc(kvm_stream stream, int32_t type, const void *d_src,
+                                     uint64_t n_rows, uint32_t n_embd, void *d_dst);
+
 #ifdef __cplusplus
 }
 #endif

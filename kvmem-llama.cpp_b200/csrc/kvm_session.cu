@@ -370,6 +370,13 @@ kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *
 
 }  // namespace
 
+static thread_local std::string g_create_err;
+
+namespace kvm {
+// Message for kvm_last_error(NULL) from entry points that take no session.
+void set_sessionless_error(const char *msg) { g_create_err = msg ? msg : ""; }
+}  // namespace kvm
+
 // ==================================================================== ABI ==
 
 extern "C" {
@@ -407,7 +414,6 @@ uint64_t kvm_row_bytes(int32_t type, uint32_t n_embd) {
     }
 }
 
-static thread_local std::string g_create_err;
 
 const char *kvm_last_error(const kvm_session *s) {
     if (!s) return g_create_err.c_str();

@@ -35,6 +35,7 @@ ABI_SYMBOLS = (
     "kvm_score_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
+    "kvm_quantize_rows_noalloc",
 )
 
 
@@ -138,6 +139,7 @@ def lib():
             "kvm_get_timings": (C.c_int, [vp, C.POINTER(Timings)]),
             "kvm_kernel_launches": (u64, [vp]),
             "kvm_quantize_rows": (C.c_int, [vp, i32, vp, u64, u32, vp]),
+            "kvm_quantize_rows_noalloc": (C.c_int, [vp, i32, vp, u64, u32, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
