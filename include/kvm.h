@@ -240,6 +240,13 @@ kvm_status kvm_score(kvm_session *s, kvm_stream stream, double *d_scores);
  * layer without query).  Used to split one session's layers across GPUs. */
 kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0,
                            uint32_t n_layers, double *d_terms, uint32_t ldt);
+/* Ordered sum of per-layer terms: d_acc[b] = ((0 + t[0][b]) + t[1][b]) + ...
+ * over the n_layers rows of d_terms (row stride ldt), the reference's
+ * layer order (llama-memory-kvmem.cpp:2881-2912).  Rows of layers without a
+ * query hold 0.0, which adds exactly.  Used to combine terms gathered from
+ * the ranks of a layer-split session, or a rank's partial sum. */
+kvm_status kvm_reduce_terms(kvm_session *s, kvm_stream stream, const double *d_terms,
+                            uint32_t n_layers, uint32_t ldt, double *d_acc);
 /* Install block scores from summed terms: score = acc / n_active (0 for blocks
  * without data).  d_acc [block_count] f64 device; n_active = layers with a
  * query across all partitions.  KvMemStore::set_retrieval_scores. */

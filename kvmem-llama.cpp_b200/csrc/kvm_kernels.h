@@ -132,6 +132,8 @@ struct ScoreArgs {
 };
 
 cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream);
+cudaError_t launch_reduce_terms(const double *terms, uint32_t n_layers, uint32_t ldt,
+                                uint32_t n_blocks, double *acc, cudaStream_t stream);
 cudaError_t launch_scores_from_sum(const SummaryLayout &s, uint32_t n_blocks, const double *acc,
                                    uint32_t n_active, double *scores, cudaStream_t stream);
 

@@ -103,6 +103,7 @@ __global__ void summarize_kernel(SummaryLayout s, uint32_t layer0, uint32_t bloc
 // them; invq = 1.0f / (q_count * g).
 __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_head_q,
                                   uint32_t head_dim) {
+    extern __shared__ float qv_s[];
     const uint32_t l = blockIdx.x;
     const uint32_t cnt = q.q_count[l];
     if (cnt == 0) return;
@@ -121,12 +122,16 @@ __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_h
             if (qh_i >= n_head_q) break;
             qh = __fadd_rn(qh, qs[static_cast<size_t>(qh_i) * head_dim + d]);
         }
-        qv[i] = __fmul_rn(qh, invq);
+        const float v = __fmul_rn(qh, invq);
+        qv[i] = v;
+        qv_s[i] = v;
     }
     __syncthreads();
+    // nq per head: the reference's sequential sum over d, one thread per head,
+    // reading the prepared vector from shared memory
     for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
         float nq = 0.0f;
-        const float *v = qv + static_cast<size_t>(h) * head_dim;
+        const float *v = qv_s + static_cast<size_t>(h) * head_dim;
         for (uint32_t d = 0; d < head_dim; ++d) nq = __fadd_rn(nq, __fmul_rn(v[d], v[d]));
         q.nq[static_cast<size_t>(l) * n_head_kv + h] = nq;
     }
@@ -212,6 +217,15 @@ __global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
     if (tid == 0) a.counters[blockIdx.x] = 0u;
 }
 
+__global__ void reduce_terms_kernel(const double *__restrict__ terms, uint32_t n_layers,
+                                    uint32_t ldt, uint32_t n_blocks, double *__restrict__ acc) {
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    double a = 0.0;
+    for (uint32_t l = 0; l < n_layers; ++l) a = __dadd_rn(a, terms[static_cast<size_t>(l) * ldt + b]);
+    acc[b] = a;
+}
+
 __global__ void scores_from_sum_kernel(SummaryLayout s, uint32_t n_blocks,
                                        const double *__restrict__ acc, uint32_t n_active,
                                        double *__restrict__ scores) {
@@ -249,7 +263,10 @@ cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n
 
 cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_head_kv,
                               uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream) {
-    query_prep_kernel<<<n_layer, 256, 0, stream>>>(q, n_head_kv, n_head_q, head_dim);
+    const size_t smem = static_cast<size_t>(n_head_kv) * head_dim * sizeof(float);
+    if (smem > 48u * 1024u)
+        cudaFuncSetAttribute(query_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    query_prep_kernel<<<n_layer, 256, smem, stream>>>(q, n_head_kv, n_head_q, head_dim);
     return cudaGetLastError();
 }
 
@@ -271,6 +288,13 @@ cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
             cudaFuncSetAttribute(score_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         score_kernel<32><<<grid, threads, smem, stream>>>(a);
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_terms(const double *terms, uint32_t n_layers, uint32_t ldt,
+                                uint32_t n_blocks, double *acc, cudaStream_t stream) {
+    if (n_blocks == 0) return cudaSuccess;
+    reduce_terms_kernel<<<(n_blocks + 255u) / 256u, 256, 0, stream>>>(terms, n_layers, ldt, n_blocks, acc);
     return cudaGetLastError();
 }
 

@@ -823,6 +823,17 @@ kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0, u
     return KVM_OK;
 }
 
+kvm_status kvm_reduce_terms(kvm_session *s, kvm_stream stream, const double *d_terms, uint32_t n_layers,
+                            uint32_t ldt, double *d_acc) {
+    if (!s) return KVM_EINVAL;
+    if (!d_terms || !d_acc || ldt < s->n_blocks) return fail(s, KVM_EINVAL, "bad terms/acc buffer");
+    DeviceGuard g(s->device);
+    KVM_CUDA(s, launch_reduce_terms(d_terms, n_layers, ldt, s->n_blocks, d_acc, as_stream(stream)),
+             "reduce terms");
+    s->launches++;
+    return KVM_OK;
+}
+
 kvm_status kvm_set_scores_from_sum(kvm_session *s, kvm_stream stream, const double *d_acc, uint32_t n_active) {
     if (!s || !d_acc) return KVM_EINVAL;
     DeviceGuard g(s->device);

@@ -32,7 +32,7 @@ ABI_SYMBOLS = (
     "kvm_config_default", "kvm_session_create", "kvm_session_destroy", "kvm_last_error",
     "kvm_window_slots", "kvm_block_count", "kvm_row_bytes", "kvm_register_append",
     "kvm_reset_window", "kvm_set_block_tier", "kvm_set_block_gpu_slot", "kvm_upload_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
-    "kvm_score_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
+    "kvm_score_terms", "kvm_reduce_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
     "kvm_quantize_rows_noalloc",
@@ -126,6 +126,7 @@ def lib():
             "kvm_set_query": (C.c_int, [vp, vp, vp, vp]),
             "kvm_score": (C.c_int, [vp, vp, vp]),
             "kvm_score_terms": (C.c_int, [vp, vp, u32, u32, vp, u32]),
+            "kvm_reduce_terms": (C.c_int, [vp, vp, vp, u32, u32, vp]),
             "kvm_set_scores_from_sum": (C.c_int, [vp, vp, vp, u32]),
             "kvm_set_scores": (C.c_int, [vp, vp, vp, u32]),
             "kvm_select": (C.c_int, [vp, vp, vp, u32]),
@@ -272,6 +273,10 @@ class Session:
     def score_terms(self, layer0, n_layers, d_terms, ldt, stream=None):
         self._check(lib().kvm_score_terms(self.h, _stream(stream), layer0, n_layers,
                                            _ptr(d_terms), ldt), "score_terms")
+
+    def reduce_terms(self, d_terms, n_layers, ldt, d_acc, stream=None):
+        self._check(lib().kvm_reduce_terms(self.h, _stream(stream), _ptr(d_terms), n_layers, ldt,
+                                            _ptr(d_acc)), "reduce_terms")
 
     def set_scores_from_sum(self, d_acc, n_active, stream=None):
         self._check(lib().kvm_set_scores_from_sum(self.h, _stream(stream), _ptr(d_acc), n_active),
