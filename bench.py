@@ -54,6 +54,11 @@ def parse():
     ap.add_argument("--profile-case", choices=("score",), default=None,
                     help="small profiling case: the scorer alone over config-2 summaries "
                          "(134 MB on the device, no history)")
+    ap.add_argument("--mode", choices=("sessions", "layer-split"), default="sessions",
+                    help="sessions: one independent config-2 session per GPU (the bench line); "
+                         "layer-split: one 1M-token session (8192 blocks) whose 16 layers are "
+                         "spread over the GPUs, scores combined over NCCL")
+    ap.add_argument("--combine", choices=("allgather", "allreduce"), default="allgather")
     ap.add_argument("--config", type=int, choices=(1, 2), default=2,
                     help="2: BASELINE configs[1] (16 layers, the bench line); "
                          "1: configs[0] (one layer, the small profiling case)")
@@ -596,9 +601,104 @@ def run_profile_score(args):
     sess.close()
 
 
+def run_layer_split(args):
+    """One session of 1048576 tokens (8192 blocks) x 16 layers, layers split
+    over the ranks; per step every rank scores its layers, the terms meet in
+    one NCCL collective, every rank selects identically and stages in its own
+    layers (cold window, q8_0)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import kvm
+    from kvm.dist import LayerSplit, layer_split_scores
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl" if world > 1 else "gloo",
+                            init_method=None if world > 1 else "tcp://127.0.0.1:29533",
+                            rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300),
+                            **({"device_id": dev} if world > 1 else {}))
+    c = dict(CFG2)
+    c["n_blocks"] = 8192
+    L_all = c["n_layer"]
+    split = LayerSplit(L_all, rank, world, args.combine)
+    c_loc = dict(c)
+    c_loc["n_layer"] = split.n_local
+    L, B, T = split.n_local, c["n_blocks"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    hk, hv = gen_history(torch, c_loc, args.seed + 17 * split.l0, dev)
+    cfg = kvm.default_config(block_tokens=T, select_budget=c["budget_tokens"],
+                             gen_reserve=c["gen_reserve"], sink_blocks=c["sink_blocks"],
+                             n_layer=L, n_head_kv=c["n_head_kv"], head_dim=c["head_dim"],
+                             n_head_q=c["n_head_q"], max_blocks=B, type_k=c["type_k"],
+                             type_v=c["type_v"])
+    sess = kvm.Session(cfg, local)
+    stream = torch.cuda.current_stream()
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    sess.register_append(B * T)
+    sess.summarize(src)
+    rbk, rbv = row_bytes(c["type_k"], E), row_bytes(c["type_v"], E)
+    win_k = torch.empty((L, sess.n_slots * T * rbk), dtype=torch.uint8, device=dev)
+    win_v = torch.empty((L, sess.n_slots * T * rbv), dtype=torch.uint8, device=dev)
+    kb = [win_k[l].data_ptr() for l in range(L)]
+    vb = [win_v[l].data_ptr() for l in range(L)]
+    qs_all = gen_queries(torch, c, args.warmup + args.steps, args.seed, dev)   # all layers
+    qs = qs_all[:, split.l0:split.l1].contiguous()
+    qc = np.ones(L, np.uint32)
+    terms = torch.zeros((L, B), dtype=torch.float64, device=dev)
+    acc = torch.zeros(B, dtype=torch.float64, device=dev)
+
+    def one_step(i):
+        sess.reset_window(stream)
+        sess.set_query(qs[i].data_ptr(), qc, stream)
+        layer_split_scores(sess, split, terms, acc, L_all, stream=stream)
+        sess.select(stream=stream)
+        sess.diff(stream=stream)
+        sess.stagein(src, kb, vb, stream=stream)
+
+    for i in range(args.warmup):
+        one_step(i)
+    torch.cuda.synchronize()
+    n_staged = int(sess.plan()["cold_block"].size)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = sess.kernel_launches
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(args.steps):
+        one_step(args.warmup + i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev if world > 1 else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    score_b, stage_b, _ = algo_bytes(c, n_staged)     # whole session, all 16 layers
+    value = (score_b + stage_b) / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16->q8_0", "data": "synthetic (as the sessions mode)",
+            "config": {"workload": "config 5 single session: 1048576 tokens (8192 blocks) x 16 "
+                                   "layers, q8_0 K+V, budget 32768, cold window, layers split "
+                                   f"over {world} GPU(s), {args.combine} of per-layer terms",
+                       "parallelism": f"layer split x{world}"},
+            "gpu_launches": int(sess.kernel_launches - launches0)}), flush=True)
+    sess.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
-    if args.profile_case == "score":
+    if args.mode == "layer-split":
+        run_layer_split(args)
+    elif args.profile_case == "score":
         run_profile_score(args)
     elif args.impl == "reference":
         run_reference(args)
