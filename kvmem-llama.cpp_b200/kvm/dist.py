@@ -54,6 +54,8 @@ class LayerSplit:
 
     def gather_terms(self, local_terms):
         """[n_local, B] f64 (any device) -> [n_layers, B] in global layer order."""
+        if self.world == 1:
+            return local_terms.contiguous()
         import torch
         import torch.distributed as dist
         B = local_terms.shape[1]
@@ -66,6 +68,8 @@ class LayerSplit:
 
     def reduce_partial(self, partial):
         """In-place sum over ranks of each rank's [B] f64 partial layer sum."""
+        if self.world == 1:
+            return partial
         import torch.distributed as dist
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
         return partial
