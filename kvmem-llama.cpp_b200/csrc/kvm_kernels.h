@@ -13,6 +13,11 @@ constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
 constexpr int kStageinStages = 3;
 constexpr int kPermuteThreads = 256;
+constexpr int kScoreBlocks = 64;                   // blocks per scorer CTA (one thread each)
+constexpr int kScoreChannels = 16;                 // channel rows per pipeline stage
+constexpr int kScoreStages = 3;
+constexpr uint32_t kSumGroup = 64;                 // blocks per summary tile (== kScoreBlocks)
+constexpr int kScoreThreads = kScoreBlocks + 32;   // + 1 TMA producer warp
 constexpr int kSelectThreads = 1024;
 constexpr int kDiffThreads = 1024;
 
@@ -83,14 +88,23 @@ struct PermuteArgs {
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream);
 
 // ---------------------------------------------------------- summaries --
+// Summary tensor, tiled: [layer][block group of 64][channel][64 blocks], so
+// the channel rows of one (layer, group) are contiguous 256-byte rows and one
+// (layer, kv head, group) scorer unit is D*256 contiguous bytes.
 struct SummaryLayout {
-    float *sum_t;          // [n_layer][n_embd][ldb]  (channel-major, block-minor)
+    float *sum_t;          // [n_layer][ldb/64][n_embd][64]
     uint32_t *mean_tok;    // [n_layer][ldb]
     float *inv_tok;        // [n_layer][ldb]  1.0f / mean_tok (0 when none)
-    uint32_t ldb;          // block capacity
+    uint32_t ldb;          // block capacity, a multiple of 64
     uint32_t n_layer;
     uint32_t n_embd;
 };
+
+__host__ __device__ inline size_t sum_index(const SummaryLayout &s, uint32_t l, uint32_t e,
+                                            uint32_t b) {
+    return ((static_cast<size_t>(l) * (s.ldb / kSumGroup) + b / kSumGroup) * s.n_embd + e) * kSumGroup +
+           (b % kSumGroup);
+}
 
 cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
                                     uint32_t n, const float *d_sums, const uint32_t *d_counts,
@@ -125,9 +139,11 @@ struct ScoreArgs {
     uint32_t n_layers;     // layers scored by this launch
     double *terms;         // [layer][ldt]
     uint32_t ldt;
+    float *rbuf;           // [layer][n_head_kv][ldb] per-head results
+    uint32_t *status;
     // combine (only when n_layers == all layers of the session)
     int combine;
-    uint32_t *counters;    // [ceil(ldb/BPC)]
+    uint32_t *counters;    // [ceil(ldb/kScoreBlocks)]
     double *scores;        // [ldb]
 };
 

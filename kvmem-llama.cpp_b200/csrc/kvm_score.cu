@@ -19,6 +19,8 @@
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
+#include <atomic>
+
 namespace kvm {
 
 // ------------------------------------------------------------ summaries --
@@ -41,7 +43,7 @@ __global__ void upload_summaries_kernel(SummaryLayout s, uint32_t layer, uint32_
         const uint32_t e = e0 + r;
         const uint32_t i = i0 + threadIdx.x;
         if (i < n && e < E) {
-            s.sum_t[(static_cast<size_t>(layer) * E + e) * s.ldb + block0 + i] = tile[threadIdx.x][r];
+            s.sum_t[sum_index(s, layer, e, block0 + i)] = tile[threadIdx.x][r];
         }
     }
     if (blockIdx.y == 0 && threadIdx.y == 0) {
@@ -87,7 +89,7 @@ __global__ void summarize_kernel(SummaryLayout s, uint32_t layer0, uint32_t bloc
     const uint32_t ew = blockIdx.y * 32u + el;
     const uint32_t iw = blockIdx.x * 8u + bw;
     if (iw < n && ew < E) {
-        s.sum_t[(static_cast<size_t>(l) * E + ew) * s.ldb + block0 + iw] = tile[bw][el];
+        s.sum_t[sum_index(s, l, ew, block0 + iw)] = tile[bw][el];
     }
     if (blockIdx.y == 0 && threadIdx.x == 0 && i < n) {
         const size_t at = static_cast<size_t>(l) * s.ldb + blk;
@@ -139,82 +141,158 @@ __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_h
 
 // ---------------------------------------------------------------- scorer --
 
-template <int BPC>
-__global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
-    extern __shared__ float sh[];
+// One CTA = (group of kScoreBlocks blocks, one KV head, one layer): D*256
+// contiguous bytes of the tiled summary tensor.  A producer warp streams them
+// in kScoreChannels-row chunks (one cp.async.bulk each) through a
+// kScoreStages-deep ring; each consumer thread owns one block and walks the
+// channels in the reference's order.  Small units (2048 at config 2) and
+// small CTAs (~14 per SM) make one balanced wave.  Per-head results go to rbuf; the last CTA of a
+// block range (over heads x layers) forms the per-layer terms in head order
+// and, when combining, the final scores in layer order.
+__global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kScoreStages;
+    float *q_s = reinterpret_cast<float *>(smem + 128);
+    float *ring = reinterpret_cast<float *>(smem + 128 + ((a.head_dim * sizeof(float) + 127u) & ~127u));
+    __shared__ uint32_t s_last;
     const uint32_t H = a.n_head_kv;
     const uint32_t D = a.head_dim;
-    const uint32_t E = H * D;
     const uint32_t ldb = a.sum.ldb;
-    float *qv_s = sh;
-    float *nq_s = qv_s + E;
-    float *r_s = nq_s + kMaxHeadsKv;
-    const uint32_t l = a.layer0 + blockIdx.y;
-    const uint32_t b0 = blockIdx.x * BPC;
-    const uint32_t tid = threadIdx.x;
+    const uint32_t g = blockIdx.x;
+    const uint32_t h = blockIdx.y;
+    const uint32_t l = a.layer0 + blockIdx.z;
+    const uint32_t b0 = g * kScoreBlocks;
+    const uint32_t nb = min(static_cast<uint32_t>(kScoreBlocks), a.n_blocks - b0);
     const bool active = a.q_count[l] > 0;
-    if (active) {
-        for (uint32_t i = tid; i < E; i += blockDim.x) qv_s[i] = a.qv[static_cast<size_t>(l) * E + i];
-        for (uint32_t h = tid; h < H; h += blockDim.x) nq_s[h] = a.nq[static_cast<size_t>(l) * H + h];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < kScoreStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kScoreBlocks / 32);
+        }
+        fence_mbar_init();
     }
+    for (uint32_t i = tid; i < D; i += blockDim.x)
+        q_s[i] = active ? a.qv[(static_cast<size_t>(l) * H + h) * D + i] : 0.0f;
     __syncthreads();
-    const uint32_t h = tid / BPC;
-    const uint32_t bl = tid % BPC;
-    const uint32_t b = b0 + bl;
-    float r = 0.0f;
-    if (active && h < H && b < a.n_blocks) {
-        const float inv = a.sum.inv_tok[static_cast<size_t>(l) * ldb + b];
-        const float *col = a.sum.sum_t + (static_cast<size_t>(l) * E + static_cast<size_t>(h) * D) * ldb + b;
-        const float *q = qv_s + h * D;
+    const uint32_t n_chunks = active ? (D + kScoreChannels - 1) / kScoreChannels : 0u;
+    bool ok = true;
+    if (warp == kScoreBlocks / 32) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            // rows h*D .. h*D+D-1 of tile (l, g): contiguous, kSumGroup floats each
+            const float *col0 = a.sum.sum_t + sum_index(a.sum, l, h * D, b0);
+            for (uint32_t k = 0; k < n_chunks; ++k) {
+                const uint32_t s = k % kScoreStages;
+                if (k >= static_cast<uint32_t>(kScoreStages) &&
+                    !mbar_wait_bounded(&empty[s], ((k / kScoreStages) - 1u) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t rows = min(static_cast<uint32_t>(kScoreChannels), D - k * kScoreChannels);
+                const uint32_t bytes = rows * kSumGroup * 4u;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(ring + s * kScoreChannels * kScoreBlocks,
+                         col0 + static_cast<size_t>(k) * kScoreChannels * kSumGroup, bytes, &full[s]);
+            }
+            if (!ok) set_status(a.status, kErrTimeout);
+        }
+    } else {
+        // ------------------------------------------------------ consumers
+        const uint32_t b = b0 + tid;
+        const float inv = (active && static_cast<uint32_t>(tid) < nb)
+                              ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
         float dot = 0.0f;
         float nk = 0.0f;
-        if (inv != 0.0f) {
-#pragma unroll 16
-            for (uint32_t d = 0; d < D; ++d) {
-                const float s = __ldg(col + static_cast<size_t>(d) * ldb);
-                const float mk = __fmul_rn(s, inv);
-                dot = __fadd_rn(dot, __fmul_rn(q[d], mk));
-                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+        for (uint32_t k = 0; k < n_chunks; ++k) {
+            const uint32_t s = k % kScoreStages;
+            if (!mbar_wait_bounded(&full[s], (k / kScoreStages) & 1u)) {
+                set_status(a.status, kErrTimeout);
+                ok = false;
+                break;
             }
+            const uint32_t rows = min(static_cast<uint32_t>(kScoreChannels), D - k * kScoreChannels);
+            if (inv != 0.0f) {
+                const float *col = ring + s * kScoreChannels * kScoreBlocks + tid;
+                const float *q = q_s + k * kScoreChannels;
+#pragma unroll
+                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreChannels); ++r) {
+                    if (r < rows) {
+                        const float mk = __fmul_rn(col[r * kScoreBlocks], inv);
+                        dot = __fadd_rn(dot, __fmul_rn(q[r], mk));
+                        nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        const float den = __fadd_rn(__fmul_rn(__fsqrt_rn(nq_s[h]), __fsqrt_rn(nk)), 1e-6f);
-        r = __fdiv_rn(dot, den);
+        if (static_cast<uint32_t>(tid) < nb) {
+            float rr = 0.0f;
+            if (active) {
+                const float den = __fadd_rn(__fmul_rn(__fsqrt_rn(a.nq[static_cast<size_t>(l) * H + h]),
+                                                      __fsqrt_rn(nk)), 1e-6f);
+                rr = __fdiv_rn(dot, den);
+            }
+            a.rbuf[(static_cast<size_t>(l) * H + h) * ldb + b] = rr;
+        }
     }
-    if (h < H) r_s[h * BPC + bl] = r;
+    // ---- last CTA of this block group combines heads (and layers)
+    if (warp < kScoreBlocks / 32 && static_cast<uint32_t>(tid) < nb) __threadfence();
     __syncthreads();
-    if (tid < BPC && b0 + tid < a.n_blocks) {
-        double layer = 0.0;
-        for (uint32_t hh = 0; hh < H; ++hh) layer = __dadd_rn(layer, static_cast<double>(r_s[hh * BPC + tid]));
-        const double hk = static_cast<double>(H > 1u ? H : 1u);
-        a.terms[static_cast<size_t>(l) * a.ldt + b0 + tid] = active ? __ddiv_rn(layer, hk) : 0.0;
+    if (tid == 0) {
+        const uint32_t want = gridDim.y * gridDim.z - 1u;
+        s_last = atomicAdd(&a.counters[g], 1u) == want ? 1u : 0u;
     }
-    if (!a.combine) return;
-    __shared__ uint32_t s_last;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.counters[blockIdx.x], 1u) == gridDim.y - 1u ? 1u : 0u;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (tid < BPC) {
-        const uint32_t bb = b0 + tid;
-        if (bb < a.n_blocks) {
-            bool has = false;
-            for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
-                has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
-            double acc = 0.0;
-            uint32_t nlay = 0;
-            for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll) {
-                if (a.q_count[ll] == 0) continue;
-                acc = __dadd_rn(acc, __ldcg(a.terms + static_cast<size_t>(ll) * a.ldt + bb));
-                ++nlay;
+    // Stage the group's per-head results a layer chunk at a time through the
+    // (now idle) ring with coalesced 256-byte row loads by every thread, then
+    // let each block's thread add them in head order and layer order.
+    const uint32_t ring_floats = kScoreStages * kScoreChannels * kScoreBlocks;
+    const uint32_t chunk = max(1u, ring_floats / (H * kScoreBlocks));
+    const uint32_t bb = b0 + tid;
+    const bool mine = tid < kScoreBlocks && static_cast<uint32_t>(tid) < nb;
+    const double hk = static_cast<double>(H > 1u ? H : 1u);
+    double acc = 0.0;
+    uint32_t nlay = 0;
+    for (uint32_t c0 = a.layer0; c0 < a.layer0 + a.n_layers; c0 += chunk) {
+        const uint32_t nl = min(chunk, a.layer0 + a.n_layers - c0);
+        const uint32_t nvals = nl * H * kScoreBlocks;
+        __syncthreads();
+        for (uint32_t i = tid; i < nvals; i += blockDim.x) {
+            const uint32_t row = i / kScoreBlocks;            // (layer - c0) * H + head
+            const uint32_t col = i % kScoreBlocks;
+            ring[i] = __ldcg(a.rbuf + (static_cast<size_t>(c0) * H + row) * ldb + b0 + col);
+        }
+        __syncthreads();
+        if (mine) {
+            for (uint32_t li = 0; li < nl; ++li) {
+                const uint32_t ll = c0 + li;
+                double term = 0.0;
+                if (a.q_count[ll] > 0) {
+                    double layer = 0.0;
+                    for (uint32_t hh = 0; hh < H; ++hh)
+                        layer = __dadd_rn(layer, static_cast<double>(ring[(li * H + hh) * kScoreBlocks + tid]));
+                    term = __ddiv_rn(layer, hk);
+                    acc = __dadd_rn(acc, term);
+                    ++nlay;
+                }
+                a.terms[static_cast<size_t>(ll) * a.ldt + bb] = term;
             }
-            double sc = 0.0;
-            if (has && nlay) sc = __ddiv_rn(acc, static_cast<double>(nlay));
-            a.scores[bb] = sc;
         }
     }
-    if (tid == 0) a.counters[blockIdx.x] = 0u;
+    if (mine && a.combine) {
+        bool has = false;
+        for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
+            has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
+        a.scores[bb] = (has && nlay) ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
+    }
+    if (tid == 0) a.counters[g] = 0u;
 }
 
 __global__ void reduce_terms_kernel(const double *__restrict__ terms, uint32_t n_layers,
@@ -270,24 +348,17 @@ cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_
     return cudaGetLastError();
 }
 
-uint32_t score_blocks_per_cta(uint32_t n_head_kv) { return n_head_kv <= 16u ? 64u : 32u; }
-
 cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
     if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
-    const uint32_t bpc = score_blocks_per_cta(a.n_head_kv);
-    const uint32_t threads = bpc * a.n_head_kv;
-    const size_t smem = (static_cast<size_t>(a.n_head_kv) * a.head_dim + kMaxHeadsKv +
-                         static_cast<size_t>(a.n_head_kv) * bpc) * sizeof(float);
-    dim3 grid((a.n_blocks + bpc - 1u) / bpc, a.n_layers);
-    if (bpc == 64u) {
-        if (smem > 48u * 1024u)
-            cudaFuncSetAttribute(score_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        score_kernel<64><<<grid, threads, smem, stream>>>(a);
-    } else {
-        if (smem > 48u * 1024u)
-            cudaFuncSetAttribute(score_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        score_kernel<32><<<grid, threads, smem, stream>>>(a);
+    const size_t smem = 128u + ((a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u)) +
+                        static_cast<size_t>(kScoreStages) * kScoreChannels * kScoreBlocks * sizeof(float);
+    if (smem > 48u * 1024u) {
+        cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
     }
+    dim3 grid((a.n_blocks + kScoreBlocks - 1u) / kScoreBlocks, a.n_head_kv, a.n_layers);
+    score_kernel<<<grid, kScoreThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -63,6 +63,7 @@ struct kvm_session {
     SummaryLayout sum{};
     QueryState q{};
     double *d_terms = nullptr;
+    float *d_rbuf = nullptr;           // per-head scorer results [L][H][ldb]
     double *d_scores = nullptr;
     double *d_acc = nullptr;
     uint32_t *d_counters = nullptr;
@@ -499,7 +500,7 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         return st;
     };
     cudaError_t e;
-    const uint32_t ldb = (c.max_blocks + 3u) & ~3u;
+    const uint32_t ldb = (c.max_blocks + kSumGroup - 1u) / kSumGroup * kSumGroup;
     const uint32_t L = c.n_layer;
     s->sum.ldb = ldb;
     s->sum.n_layer = L;
@@ -524,6 +525,7 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->q.qv), sizeof(float) * L * E},
         {reinterpret_cast<void **>(&s->q.nq), sizeof(float) * L * c.n_head_kv},
         {reinterpret_cast<void **>(&s->d_terms), sizeof(double) * L * ldb},
+        {reinterpret_cast<void **>(&s->d_rbuf), sizeof(float) * L * c.n_head_kv * ldb},
         {reinterpret_cast<void **>(&s->d_scores), sizeof(double) * ldb},
         {reinterpret_cast<void **>(&s->d_acc), sizeof(double) * ldb},
         {reinterpret_cast<void **>(&s->d_counters), sizeof(uint32_t) * n_groups * 2},
@@ -785,6 +787,8 @@ static ScoreArgs score_args(kvm_session *s) {
     a.n_blocks = s->n_blocks;
     a.terms = s->d_terms;
     a.ldt = s->sum.ldb;
+    a.rbuf = s->d_rbuf;
+    a.status = s->d_status;
     a.counters = s->d_counters;
     a.scores = s->d_scores;
     return a;

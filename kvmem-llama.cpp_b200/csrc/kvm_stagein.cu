@@ -102,10 +102,6 @@ struct TileSlot {
 };
 static_assert(sizeof(TileSlot) == 24, "TileSlot");
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Shared memory: [0,128) barriers (full[NS], done[NS]); [128,384) tile slots;
 // then NS input tiles and NS output tiles.
 constexpr uint32_t kStageinHeader = 384;
