@@ -216,6 +216,12 @@ kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream);
 kvm_status kvm_upload_summaries(kvm_session *s, kvm_stream stream, uint32_t layer,
                                 uint32_t block0, uint32_t n, const float *sums,
                                 const uint32_t *counts);
+/* The inverse of kvm_upload_summaries: copy n blocks' F32 sums ([n][E]) and
+ * counts of one layer to `sums` / `counts` (host or device pointers; either
+ * may be NULL).  Stream-ordered.  Serves checkpoint/resume of a session
+ * (RawKvStore::mean_checkpoint, raw_kv_store.cpp:1131-1164). */
+kvm_status kvm_download_summaries(kvm_session *s, kvm_stream stream, uint32_t layer,
+                                  uint32_t block0, uint32_t n, float *sums, uint32_t *counts);
 /* GPU producer of the same statistics from F16 K rows of the source
  * (RawKvStore::add_mean_f32 over F16->F32 values, ordered token sum).  The
  * source must be device-resident.  Counts are the blocks' n_tokens. */

@@ -109,6 +109,8 @@ __host__ __device__ inline size_t sum_index(const SummaryLayout &s, uint32_t l, 
 cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
                                     uint32_t n, const float *d_sums, const uint32_t *d_counts,
                                     cudaStream_t stream);
+cudaError_t launch_download_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
+                                      uint32_t n, float *d_sums, cudaStream_t stream);
 cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n_layers,
                              uint32_t block0, uint32_t n, const uint8_t *src_k,
                              uint64_t layer_stride, uint64_t block_stride, uint64_t row_stride,

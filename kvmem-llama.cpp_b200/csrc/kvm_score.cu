@@ -58,6 +58,26 @@ __global__ void upload_summaries_kernel(SummaryLayout s, uint32_t layer, uint32_
     }
 }
 
+// Tiled layout -> [n][n_embd] rows (transpose through smem).
+__global__ void download_summaries_kernel(SummaryLayout s, uint32_t layer, uint32_t block0,
+                                          uint32_t n, float *__restrict__ sums) {
+    __shared__ float tile[32][33];
+    const uint32_t E = s.n_embd;
+    const uint32_t i0 = blockIdx.x * 32u;
+    const uint32_t e0 = blockIdx.y * 32u;
+    for (uint32_t r = threadIdx.y; r < 32u; r += blockDim.y) {
+        const uint32_t e = e0 + r;
+        const uint32_t i = i0 + threadIdx.x;
+        tile[r][threadIdx.x] = (i < n && e < E) ? s.sum_t[sum_index(s, layer, e, block0 + i)] : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.y; r < 32u; r += blockDim.y) {
+        const uint32_t i = i0 + r;
+        const uint32_t e = e0 + threadIdx.x;
+        if (i < n && e < E) sums[static_cast<size_t>(i) * E + e] = tile[threadIdx.x][r];
+    }
+}
+
 // F16 K rows -> ordered F32 token sums (RawKvStore::add_mean_f32 with off == 0).
 __global__ void summarize_kernel(SummaryLayout s, uint32_t layer0, uint32_t block0, uint32_t n,
                                  const uint8_t *__restrict__ src, uint64_t layer_stride,
@@ -323,6 +343,14 @@ cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint
     dim3 grid((n + 31u) / 32u, (s.n_embd + 31u) / 32u);
     dim3 block(32, 8);
     upload_summaries_kernel<<<grid, block, 0, stream>>>(s, layer, block0, n, d_sums, d_counts);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_download_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
+                                      uint32_t n, float *d_sums, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    dim3 grid((n + 31u) / 32u, (s.n_embd + 31u) / 32u);
+    download_summaries_kernel<<<grid, dim3(32, 8), 0, stream>>>(s, layer, block0, n, d_sums);
     return cudaGetLastError();
 }
 

@@ -741,6 +741,29 @@ kvm_status kvm_upload_summaries(kvm_session *s, kvm_stream stream, uint32_t laye
     return KVM_OK;
 }
 
+kvm_status kvm_download_summaries(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t block0,
+                                  uint32_t n, float *sums, uint32_t *counts) {
+    if (!s) return KVM_EINVAL;
+    if (layer >= s->cfg.n_layer) return fail(s, KVM_EINVAL, "layer %u >= n_layer", layer);
+    if (static_cast<uint64_t>(block0) + n > s->max_blocks) return fail(s, KVM_EINVAL, "blocks beyond max_blocks");
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    const uint32_t E = s->n_embd;
+    if (counts && n)
+        KVM_CUDA(s, cudaMemcpyAsync(counts, s->sum.mean_tok + static_cast<size_t>(layer) * s->sum.ldb + block0,
+                                    sizeof(uint32_t) * n, cudaMemcpyDefault, st), "counts copy");
+    for (uint32_t off = 0; sums && off < n;) {
+        const uint32_t m = std::min<uint32_t>(n - off, static_cast<uint32_t>(s->stage_sums_cap));
+        KVM_CUDA(s, launch_download_summaries(s->sum, layer, block0 + off, m, s->d_stage_sums, st),
+                 "summary download");
+        s->launches++;
+        KVM_CUDA(s, cudaMemcpyAsync(sums + static_cast<size_t>(off) * E, s->d_stage_sums,
+                                    sizeof(float) * m * E, cudaMemcpyDefault, st), "sums copy");
+        off += m;
+    }
+    return KVM_OK;
+}
+
 kvm_status kvm_summarize(kvm_session *s, kvm_stream stream, uint32_t layer0, uint32_t n_layers,
                          uint32_t block0, uint32_t n, const kvm_source *src) {
     if (!s) return KVM_EINVAL;

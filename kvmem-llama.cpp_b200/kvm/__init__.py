@@ -31,7 +31,8 @@ _STATUS = {1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESTATE", 6: 
 ABI_SYMBOLS = (
     "kvm_config_default", "kvm_session_create", "kvm_session_destroy", "kvm_last_error",
     "kvm_window_slots", "kvm_block_count", "kvm_row_bytes", "kvm_register_append",
-    "kvm_reset_window", "kvm_set_block_tier", "kvm_set_block_gpu_slot", "kvm_upload_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
+    "kvm_reset_window", "kvm_set_block_tier", "kvm_set_block_gpu_slot", "kvm_upload_summaries",
+    "kvm_download_summaries", "kvm_summarize", "kvm_set_query", "kvm_score",
     "kvm_score_terms", "kvm_reduce_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
@@ -122,6 +123,7 @@ def lib():
             "kvm_set_block_tier": (C.c_int, [vp, vp, u32, i32]),
             "kvm_set_block_gpu_slot": (C.c_int, [vp, vp, u32, i32]),
             "kvm_upload_summaries": (C.c_int, [vp, vp, u32, u32, u32, vp, vp]),
+            "kvm_download_summaries": (C.c_int, [vp, vp, u32, u32, u32, vp, vp]),
             "kvm_summarize": (C.c_int, [vp, vp, u32, u32, u32, u32, C.POINTER(Source)]),
             "kvm_set_query": (C.c_int, [vp, vp, vp, vp]),
             "kvm_score": (C.c_int, [vp, vp, vp]),
@@ -254,6 +256,18 @@ class Session:
         n = len(counts)
         self._check(lib().kvm_upload_summaries(self.h, _stream(stream), layer, block0, n,
                                                 _ptr(sums), _ptr(counts)), "upload_summaries")
+
+    def download_summaries(self, layer, block0=0, n=None, stream=None):
+        """(sums [n, E] f32, counts [n] u32) of one layer, read back to the host."""
+        n = self.block_count - block0 if n is None else n
+        E = self.cfg.n_head_kv * self.cfg.head_dim
+        sums = np.zeros((max(1, n), E), np.float32)
+        counts = np.zeros(max(1, n), np.uint32)
+        self._check(lib().kvm_download_summaries(self.h, _stream(stream), layer, block0, n,
+                                                  sums.ctypes.data, counts.ctypes.data),
+                    "download_summaries")
+        self.wait(stream=stream)
+        return sums[:n], counts[:n]
 
     def summarize(self, src: Source, layer0=0, n_layers=None, block0=0, n=None, stream=None):
         n_layers = self.cfg.n_layer if n_layers is None else n_layers
