@@ -152,7 +152,7 @@ def test_config4_incremental_40_steps(kvm_lib, oracle):
         cfg = oracle.make_cfg(T, 256, 1, 0)
         slots = np.full(B, -1, np.int32)
         q = _query(rng, L)
-        alpha = 0.93
+        alpha = 0.94
         overlaps, moved_total = [], 0
         prev = None
         for step in range(40):
