@@ -54,10 +54,15 @@ def parse():
     ap.add_argument("--profile-case", choices=("score",), default=None,
                     help="small profiling case: the scorer alone over config-2 summaries "
                          "(134 MB on the device, no history)")
-    ap.add_argument("--mode", choices=("sessions", "layer-split"), default="sessions",
+    ap.add_argument("--mode", choices=("sessions", "layer-split", "incremental", "multi-session"),
+                    default="sessions",
                     help="sessions: one independent config-2 session per GPU (the bench line); "
                          "layer-split: one 1M-token session (8192 blocks) whose 16 layers are "
-                         "spread over the GPUs, scores combined over NCCL")
+                         "spread over the GPUs, scores combined over NCCL; "
+                         "incremental: config 4, 40 overlapping reselections of a 1M-token "
+                         "session without a window reset; "
+                         "multi-session: config 5, 64 sessions of 131072 tokens split over the "
+                         "GPUs, each on its own stream")
     ap.add_argument("--combine", choices=("allgather", "allreduce"), default="allgather")
     ap.add_argument("--config", type=int, choices=(1, 2), default=2,
                     help="2: BASELINE configs[1] (16 layers, the bench line); "
@@ -601,6 +606,219 @@ def run_profile_score(args):
     sess.close()
 
 
+def _dist_init(torch):
+    import datetime
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        return world, rank, local, dev, dist
+    return 1, 0, local, dev, None
+
+
+def _max_over_ranks(torch, dist, dev, x):
+    if not dist:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _make_session(kvm, c, B, device):
+    L, T = c["n_layer"], c["block_tokens"]
+    cfg = kvm.default_config(block_tokens=T, select_budget=c["budget_tokens"],
+                             gen_reserve=c["gen_reserve"], sink_blocks=c["sink_blocks"],
+                             recent_blocks=c["recent_blocks"], n_layer=L,
+                             n_head_kv=c["n_head_kv"], head_dim=c["head_dim"],
+                             n_head_q=c["n_head_q"], max_blocks=B, type_k=c["type_k"],
+                             type_v=c["type_v"])
+    return kvm.Session(cfg, device)
+
+
+def _window(torch, c, slots, dev):
+    L, T = c["n_layer"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    wk = torch.empty((L, slots * T * row_bytes(c["type_k"], E)), dtype=torch.uint8, device=dev)
+    wv = torch.empty((L, slots * T * row_bytes(c["type_v"], E)), dtype=torch.uint8, device=dev)
+    return wk, wv, [wk[l].data_ptr() for l in range(L)], [wv[l].data_ptr() for l in range(L)]
+
+
+def run_incremental(args):
+    """Config 4: one 1048576-token session (8192 blocks x 16 layers), 40
+    consecutive reselections whose queries drift (q_t = a q_{t-1} + sqrt(1-a^2)
+    noise, a = 0.94: ~70% overlap of consecutive selections); the window is
+    kept, so only changed blocks are moved or staged.  Sessions per GPU are
+    independent (weak scaling)."""
+    import torch
+    import kvm
+    world, rank, local, dev, dist = _dist_init(torch)
+    c = dict(CFG2)
+    B, L, T = 8192, c["n_layer"], c["block_tokens"]
+    c["n_blocks"] = B
+    E = c["n_head_kv"] * c["head_dim"]
+    steps = 40 if args.steps == 200 else args.steps
+    seed = args.seed + 1000 * rank
+    hk, hv = gen_history(torch, c, seed, dev)
+    sess = _make_session(kvm, c, B, local)
+    stream = torch.cuda.current_stream()
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    sess.register_append(B * T)
+    sess.summarize(src)
+    wk, wv, kb, vb = _window(torch, c, sess.n_slots, dev)
+    n_q = args.warmup + steps
+    noise = gen_queries(torch, c, n_q, seed, dev)
+    alpha = 0.94
+    qs = torch.empty_like(noise)
+    qs[0] = noise[0]
+    for i in range(1, n_q):
+        qs[i] = (alpha * qs[i - 1] + (1 - alpha * alpha) ** 0.5 * noise[i]).half().float()
+    qc = np.ones(L, np.uint32)
+
+    def run(timed):
+        sess.reset_window(stream)
+        evs, counts = [], []
+        for i in range(n_q):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            sess.set_query(qs[i].data_ptr(), qc, stream)
+            sess.score(stream=stream)
+            sess.select(stream=stream)
+            sess.diff(stream=stream)
+            sess.stagein(src, kb, vb, stream=stream)
+            b.record(stream)
+            if i >= args.warmup:
+                evs.append((a, b))
+            if not timed:
+                p = sess.plan()
+                counts.append((int(p["cold_block"].size), int(p["mv_block"].size),
+                               np.asarray(p["selected"]).copy()))
+        torch.cuda.synchronize()
+        return evs, counts
+
+    _, counts = run(timed=False)          # per-step plan sizes (same deterministic sequence)
+    if dist:
+        dist.barrier()
+    launches0 = sess.kernel_launches
+    evs, _ = run(timed=True)
+    launches = sess.kernel_launches - launches0
+    per_step = [a.elapsed_time(b) for a, b in evs]
+    ms = _max_over_ranks(torch, dist, dev, statistics.mean(per_step))
+    cs = counts[args.warmup:]
+    n_cold = statistics.mean(x[0] for x in cs)
+    n_mv = statistics.mean(x[1] for x in cs)
+    overl = statistics.mean(len(np.intersect1d(counts[i - 1][2], counts[i][2])) / counts[i][2].size
+                            for i in range(max(1, args.warmup), len(counts)))
+    score_b, stage_b, per_bl = algo_bytes(c, n_cold)
+    move_b = n_mv * L * 2 * T * (row_bytes(c["type_k"], E) + row_bytes(c["type_v"], E))
+    step_b = score_b + stage_b + move_b
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(world * step_b / (ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16->q8_0",
+            "data": "synthetic: seeded F16 history, drifting seeded queries",
+            "config": {"workload": "config 4: 1048576-token session (8192 blocks) x 16 layers, "
+                                   "q8_0 K+V, budget 32768, 40 incremental reselections, window kept",
+                       "parallelism": f"sessions x{world}"},
+            "per_step_ms": {"mean": round(statistics.mean(per_step), 4),
+                            "min": round(min(per_step), 4), "max": round(max(per_step), 4)},
+            "mean_overlap": round(overl, 3), "staged_blocks_per_step": round(n_cold, 1),
+            "moved_blocks_per_step": round(n_mv, 1),
+            "h2d_bytes_per_step_host_source": int(n_cold * L * 2 * T * E * 2),
+            "algorithmic_bytes_per_step": {"score": score_b, "stagein": int(stage_b),
+                                           "moves": int(move_b)},
+            "gpu_launches": int(launches)}), flush=True)
+    sess.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_multi_session(args):
+    """Config 5: 64 independent sessions of 131072 tokens (1024 blocks x 16
+    layers, q8_0, budget 32768), split evenly over the GPUs; every session
+    steps on its own stream (cold window, new query per step).  The sessions of
+    a GPU read one shared seeded F16 history (8.6 GB) -- the traffic per
+    session is the same as with private histories, which would need 550 GB."""
+    import torch
+    import kvm
+    world, rank, local, dev, dist = _dist_init(torch)
+    c = dict(CFG2)
+    B, L, T = 1024, c["n_layer"], c["block_tokens"]
+    c["n_blocks"] = B
+    E = c["n_head_kv"] * c["head_dim"]
+    n_sess = max(1, 64 // world)
+    steps = 5 if args.steps == 200 else args.steps
+    seed = args.seed + 1000 * rank
+    hk, hv = gen_history(torch, c, seed, dev)
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    sessions, streams, wins, queries = [], [], [], []
+    for i in range(n_sess):
+        s = _make_session(kvm, c, B, local)
+        s.register_append(B * T)
+        s.summarize(src)
+        sessions.append(s)
+        streams.append(torch.cuda.Stream(device=dev))
+        wins.append(_window(torch, c, s.n_slots, dev))
+        queries.append(gen_queries(torch, c, args.warmup + steps, seed + 7 * i, dev))
+    qc = np.ones(L, np.uint32)
+    main = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+
+    def step(i):
+        start = torch.cuda.Event()
+        start.record(main)
+        for s, st, w, q in zip(sessions, streams, wins, queries):
+            st.wait_event(start)
+            s.reset_window(st)
+            s.set_query(q[i].data_ptr(), qc, st)
+            s.step(src, w[2], w[3], stream=st)
+            done = torch.cuda.Event()
+            done.record(st)
+            main.wait_event(done)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    n_staged = int(sessions[0].plan()["cold_block"].size)
+    if dist:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = sum(s.kernel_launches for s in sessions)
+    t0.record(main)
+    for i in range(steps):
+        step(args.warmup + i)
+    t1.record(main)
+    torch.cuda.synchronize()
+    launches = sum(s.kernel_launches for s in sessions) - launches0
+    ms = _max_over_ranks(torch, dist, dev, t0.elapsed_time(t1) / steps)
+    score_b, stage_b, _ = algo_bytes(c, n_staged)
+    total_sessions = n_sess * world
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC,
+            "value": round(total_sessions * (score_b + stage_b) / (ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16->q8_0",
+            "data": "synthetic; the sessions of a GPU share one seeded F16 history",
+            "config": {"workload": f"config 5: {total_sessions} sessions x 131072 tokens (1024 "
+                                   "blocks) x 16 layers, q8_0 K+V, budget 32768, cold window",
+                       "sessions_per_gpu": n_sess, "parallelism": f"sessions over {world} GPU(s)"},
+            "session_steps_per_s": round(total_sessions / (ms * 1e-3), 1),
+            "ms_per_session_step": round(ms / n_sess, 4),
+            "gpu_launches": int(launches)}), flush=True)
+    for s in sessions:
+        s.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def run_layer_split(args):
     """One session of 1048576 tokens (8192 blocks) x 16 layers, layers split
     over the ranks; per step every rank scores its layers, the terms meet in
@@ -698,6 +916,10 @@ def main():
     args = parse()
     if args.mode == "layer-split":
         run_layer_split(args)
+    elif args.mode == "incremental":
+        run_incremental(args)
+    elif args.mode == "multi-session":
+        run_multi_session(args)
     elif args.profile_case == "score":
         run_profile_score(args)
     elif args.impl == "reference":
