@@ -87,7 +87,8 @@ typedef struct kvm_config {
     uint32_t reserved0;
     uint64_t immutable_refresh_abs_delta_tokens;
     uint64_t immutable_max_baked_position;
-    uint64_t staging_bytes;    /* HBM ring for host-resident sources; 0 = 256 MiB */
+    uint64_t staging_bytes;    /* HBM ring for host-resident sources, allocated on the first
+                                  host-source stage-in; 0 = 256 MiB */
 } kvm_config;
 
 /* Fill `cfg` with the reference defaults (kvmem_store.hpp:231-327 and the

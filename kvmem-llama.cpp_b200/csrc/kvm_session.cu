@@ -315,6 +315,11 @@ kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *
         return fail(s, KVM_ENOMEM, "staging ring (%zu B) smaller than one block (%llu B) per slot",
                     s->ring_bytes, static_cast<unsigned long long>(item_bytes));
     const uint64_t slot_bytes = item_bytes * per_slot;
+    if (!s->d_ring) {
+        // first host-source stage-in: the ring is only needed on this path
+        KVM_CUDA(s, cudaStreamSynchronize(st), "ring allocation sync");
+        KVM_CUDA(s, cudaMalloc(&s->d_ring, s->ring_bytes), "staging ring allocation");
+    }
     StageinArgs a = stagein_common(s);
     a.src_by_item = 1;
     a.layer_stride = span;
@@ -575,9 +580,8 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
     // gpu_slot = -1 everywhere
     e = cudaMemset(s->bt.gpu_slot, 0xff, sizeof(int32_t) * nb);
     if (e != cudaSuccess) return cleanup(e, "slot clear");
+    // the HBM staging ring is allocated on the first stage-in from a host source
     s->ring_bytes = c.staging_bytes ? c.staging_bytes : (256ull << 20);
-    e = cudaMalloc(&s->d_ring, s->ring_bytes);
-    if (e != cudaSuccess) return cleanup(e, "staging ring allocation");
     s->pin_slot_bytes = std::max<size_t>(64u * 1024u, std::max<size_t>(4u * nb, sizeof(void *) * 2 * L));
     e = cudaHostAlloc(reinterpret_cast<void **>(&s->h_pin), s->pin_slot_bytes * kPinSlots, cudaHostAllocDefault);
     if (e != cudaSuccess) return cleanup(e, "pinned ring allocation");
