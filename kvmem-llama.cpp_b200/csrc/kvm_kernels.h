@@ -85,6 +85,10 @@ struct PermuteArgs {
     uint32_t *status;
 };
 
+// shared-memory bytes of the per-move metadata table (12 bytes a move, 16-aligned)
+__host__ __device__ inline size_t permute_meta_bytes(uint32_t max_moves) {
+    return (static_cast<size_t>(max_moves) * 12u + 15u) & ~static_cast<size_t>(15u);
+}
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream);
 
 // ---------------------------------------------------------- summaries --

@@ -242,10 +242,82 @@ __global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs
 
 // ------------------------------------------------------------- permute --
 
+// Per-move metadata, validated once per CTA and kept in shared memory so the
+// copy loops issue one independent global access each.
+struct MoveMeta {
+    uint32_t from;
+    uint32_t to;
+    uint32_t n_tok;   // 0 for an invalid move: nothing of it is touched
+};
+
+template <typename V>
+__device__ __forceinline__ void permute_column(const PermuteArgs &a, const MoveMeta *meta,
+                                               uint8_t *col, uint32_t n_moves, uint8_t *base,
+                                               uint32_t span, uint32_t rb, uint32_t c0) {
+    constexpr uint32_t G = sizeof(V);
+    constexpr uint32_t U = 4;                 // accesses in flight per thread
+    const uint32_t per_move = a.col_bytes / G;
+    const uint32_t n_acc = n_moves * per_move;
+    const uint32_t stride = kPermuteThreads * U;
+    // gather this column of every moving block into shared memory
+    for (uint32_t i0 = threadIdx.x; i0 < n_acc; i0 += stride) {
+        V r[U];
+        uint32_t off[U];
+        bool ok[U];
+#pragma unroll
+        for (uint32_t j = 0; j < U; ++j) {
+            const uint32_t i = i0 + j * kPermuteThreads;
+            ok[j] = false;
+            if (i < n_acc) {
+                const uint32_t m = i / per_move;
+                const uint32_t o = (i - m * per_move) * G;
+                const MoveMeta mm = meta[m];
+                off[j] = m * a.col_bytes + o;
+                if (c0 + o < mm.n_tok * rb) {
+                    r[j] = *reinterpret_cast<const V *>(base + static_cast<uint64_t>(mm.from) * span + c0 + o);
+                    ok[j] = true;
+                }
+            }
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < U; ++j)
+            if (ok[j]) *reinterpret_cast<V *>(col + off[j]) = r[j];
+    }
+    __syncthreads();
+    // scatter it to the new slots
+    for (uint32_t i = threadIdx.x; i < n_acc; i += kPermuteThreads) {
+        const uint32_t m = i / per_move;
+        const uint32_t o = (i - m * per_move) * G;
+        const MoveMeta mm = meta[m];
+        if (c0 + o < mm.n_tok * rb)
+            *reinterpret_cast<V *>(base + static_cast<uint64_t>(mm.to) * span + c0 + o) =
+                *reinterpret_cast<const V *>(col + m * a.col_bytes + o);
+    }
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a) {
-    extern __shared__ __align__(16) uint8_t col[];
+    extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t n_moves = min(*a.n_moves_dev, a.max_moves);
     if (n_moves == 0) return;
+    MoveMeta *meta = reinterpret_cast<MoveMeta *>(smem);
+    uint8_t *col = smem + permute_meta_bytes(a.max_moves);
+    for (uint32_t m = threadIdx.x; m < n_moves; m += kPermuteThreads) {
+        const uint32_t blk = a.mv_block[m];
+        const int32_t from = a.mv_from[m];
+        const int32_t to = a.mv_to[m];
+        MoveMeta mm{0u, 0u, 0u};
+        if (blk < a.max_blocks && from >= 0 && static_cast<uint32_t>(from) < a.n_slots && to >= 0 &&
+            static_cast<uint32_t>(to) < a.n_slots) {
+            mm.from = static_cast<uint32_t>(from);
+            mm.to = static_cast<uint32_t>(to);
+            mm.n_tok = min(a.n_tokens[blk], a.block_tokens);
+        } else if (blockIdx.x == 0) {
+            set_status(a.status, kErrSlot);
+        }
+        meta[m] = mm;
+    }
+    __syncthreads();
     const uint32_t n_cols_k = (a.span_k + a.col_bytes - 1) / a.col_bytes;
     const uint32_t n_cols_v = (a.span_v + a.col_bytes - 1) / a.col_bytes;
     const uint64_t units = static_cast<uint64_t>(a.n_layer) * (n_cols_k + n_cols_v);
@@ -257,53 +329,10 @@ __global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a)
         uint8_t *base = is_v ? a.dst_v[layer] : a.dst_k[layer];
         const uint32_t span = is_v ? a.span_v : a.span_k;
         const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
-        const uint32_t c0 = c * a.col_bytes;
-        // gather this column of every moving block
-        for (uint32_t m = 0; m < n_moves; ++m) {
-            const uint32_t blk = a.mv_block[m];
-            const int32_t from = a.mv_from[m];
-            if (blk >= a.max_blocks || from < 0 || static_cast<uint32_t>(from) >= a.n_slots) {
-                set_status(a.status, kErrSlot);
-                continue;
-            }
-            const uint32_t nbytes = min(a.n_tokens[blk], a.block_tokens) * rb;
-            if (c0 >= nbytes) continue;
-            const uint32_t w = min(a.col_bytes, nbytes - c0);
-            const uint8_t *src = base + static_cast<uint64_t>(from) * span + c0;
-            uint8_t *dst = col + static_cast<size_t>(m) * a.col_bytes;
-            if (a.vec16) {
-                for (uint32_t o = 16u * threadIdx.x; o < w; o += 16u * kPermuteThreads)
-                    *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
-            } else {
-                for (uint32_t o = 2u * threadIdx.x; o < w; o += 2u * kPermuteThreads)
-                    *reinterpret_cast<uint16_t *>(dst + o) =
-                        *reinterpret_cast<const uint16_t *>(src + o);
-            }
-        }
-        __syncthreads();
-        for (uint32_t m = 0; m < n_moves; ++m) {
-            const uint32_t blk = a.mv_block[m];
-            const int32_t from = a.mv_from[m];
-            const int32_t to = a.mv_to[m];
-            if (blk >= a.max_blocks || from < 0 || static_cast<uint32_t>(from) >= a.n_slots ||
-                to < 0 || static_cast<uint32_t>(to) >= a.n_slots) {
-                continue;
-            }
-            const uint32_t nbytes = min(a.n_tokens[blk], a.block_tokens) * rb;
-            if (c0 >= nbytes) continue;
-            const uint32_t w = min(a.col_bytes, nbytes - c0);
-            uint8_t *dst = base + static_cast<uint64_t>(to) * span + c0;
-            const uint8_t *src = col + static_cast<size_t>(m) * a.col_bytes;
-            if (a.vec16) {
-                for (uint32_t o = 16u * threadIdx.x; o < w; o += 16u * kPermuteThreads)
-                    *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
-            } else {
-                for (uint32_t o = 2u * threadIdx.x; o < w; o += 2u * kPermuteThreads)
-                    *reinterpret_cast<uint16_t *>(dst + o) =
-                        *reinterpret_cast<const uint16_t *>(src + o);
-            }
-        }
-        __syncthreads();
+        if (a.vec16)
+            permute_column<uint4>(a, meta, col, n_moves, base, span, rb, c * a.col_bytes);
+        else
+            permute_column<uint16_t>(a, meta, col, n_moves, base, span, rb, c * a.col_bytes);
     }
 }
 
@@ -368,7 +397,7 @@ cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t g
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(a.max_moves) * a.col_bytes;
+    const size_t smem = permute_meta_bytes(a.max_moves) + static_cast<size_t>(a.max_moves) * a.col_bytes;
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
     if (!attr_once(g_permute_attr, reinterpret_cast<const void *>(permute_kernel), 200 * 1024))
         return cudaErrorInvalidValue;
