@@ -52,12 +52,15 @@ typedef enum kvm_status {
     KVM_EDEVICE = 6    /* a kernel reported an error flag (bad index, timeout) */
 } kvm_status;
 
-/* ggml_type ids of the window cache formats (ggml.h enum ggml_type). */
+/* ggml_type ids (ggml.h enum ggml_type): the window cache formats F16, Q4_0,
+ * Q5_0, Q8_0, and the captured-activation formats F32, F16, BF16. */
 typedef enum kvm_type {
+    KVM_TYPE_F32 = 0,
     KVM_TYPE_F16 = 1,
     KVM_TYPE_Q4_0 = 2,
     KVM_TYPE_Q5_0 = 6,
-    KVM_TYPE_Q8_0 = 8
+    KVM_TYPE_Q8_0 = 8,
+    KVM_TYPE_BF16 = 30
 } kvm_type;
 
 /* Block tiers, kvmem/include/kvmem/kvmem_store.hpp:31 (enum class KvTier). */
@@ -229,6 +232,62 @@ kvm_status kvm_download_summaries(kvm_session *s, kvm_stream stream, uint32_t la
 kvm_status kvm_summarize(kvm_session *s, kvm_stream stream, uint32_t layer0,
                          uint32_t n_layers, uint32_t block0, uint32_t n,
                          const kvm_source *src);
+/*
+ * A captured activation tensor in device memory, laid out like the ggml
+ * tensor the attention graph hands to the capture hook
+ * (patches/0002-attn-qk-capture-hook.patch): element (token t, head h,
+ * dim d) is at data + t*nb_tok + h*nb_head + d*nb_dim (ggml nb[2], nb[1],
+ * nb[0]).  `type` is KVM_TYPE_F32, KVM_TYPE_F16 or KVM_TYPE_BF16; values are
+ * widened to F32 exactly.  n_head * head_dim must equal the row width the
+ * call expects (n_head_kv*head_dim for K, n_head_q*head_dim for Q).
+ */
+typedef struct kvm_rows {
+    const void *data;
+    int32_t type;
+    uint32_t n_head;
+    uint32_t head_dim;
+    uint32_t reserved0;
+    uint64_t nb_dim;
+    uint64_t nb_head;
+    uint64_t nb_tok;
+} kvm_rows;
+
+/* Device producers of the statistics the scorer reads.  Every one is an
+ * ordered F32 sum that continues the reference's own association, so the
+ * summaries and the query stay bit-identical to the reference host store
+ * while never leaving HBM. */
+
+/* RawKvStore::write_layer_mean_k (raw_kv_store.cpp:674-694, add_mean_f32
+ * :204-223) for tokens [pos0, pos0+n) of one layer, row i of `k` holding
+ * position pos0+i: per block, a write starting at offset 0 restarts the sum,
+ * rows are added in token order, and the block's mean_tokens becomes `take`
+ * (offset 0) or max(mean_tokens, offset+take).  Stream-ordered. */
+kvm_status kvm_write_mean_k(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t pos0,
+                            uint32_t n, const kvm_rows *k);
+/* Decode accumulator of one layer (kvmem_meank_add, llama-kvmem-stagein.cu:
+ * 269-315 and :1039-1063): acc[layer] += rows tok0 .. tok0+n-1 of `k`, in
+ * order.  The session holds one F32 [n_head_kv*head_dim] accumulator per
+ * layer, zero at creation. */
+kvm_status kvm_meank_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t tok0,
+                         uint32_t n, const kvm_rows *k);
+/* decode_mean_flush (llama-memory-kvmem.cpp:2665-2724) for layers
+ * [layer0, layer0+n_layers): RawKvStore::write_layer_mean_sum(pos0, n, il,
+ * acc[il]) (raw_kv_store.cpp:696-720) on the device, then acc[il] = 0. */
+kvm_status kvm_meank_flush(kvm_session *s, kvm_stream stream, uint32_t layer0,
+                           uint32_t n_layers, uint32_t pos0, uint32_t n);
+/* kvmem_meank_zero (llama-kvmem-stagein.cu:1031-1037) for layers
+ * [layer0, layer0+n_layers) (decode_mean_zero_acc, llama-memory-kvmem.cpp:2470). */
+kvm_status kvm_meank_zero(kvm_session *s, kvm_stream stream, uint32_t layer0,
+                          uint32_t n_layers);
+/* reset_query_acc (llama-memory-kvmem.cpp:2059-2064): q_sum = 0, q_count = 0. */
+kvm_status kvm_query_reset(kvm_session *s, kvm_stream stream);
+/* harvest 'q' (llama-memory-kvmem.cpp:2157-2173, :2206-2219) for one layer:
+ * for each token i < n with keep[i] != 0 (keep = host array of
+ * query_contains(pos_i); NULL keeps all), in order, q_sum[layer] += Q[i] and
+ * q_count[layer] += 1.  The next score picks the accumulated query up. */
+kvm_status kvm_query_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t n,
+                         const kvm_rows *q, const uint8_t *keep);
+
 /*
  * Captured query (harvest_from_host 'q', llama-memory-kvmem.cpp:2157-2173):
  * q_sum [n_layer][n_head_q*head_dim] F32 sums of pre-RoPE Q (host or device

@@ -115,11 +115,54 @@ cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint
                                     cudaStream_t stream);
 cudaError_t launch_download_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
                                       uint32_t n, float *d_sums, cudaStream_t stream);
-cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n_layers,
-                             uint32_t block0, uint32_t n, const uint8_t *src_k,
-                             uint64_t layer_stride, uint64_t block_stride, uint64_t row_stride,
-                             const uint32_t *n_tokens, uint32_t block_tokens,
-                             cudaStream_t stream);
+
+// ----------------------------------------------------------- producers --
+// ggml type ids of captured activations
+constexpr int32_t kActF32 = 0;
+constexpr int32_t kActF16 = 1;
+constexpr int32_t kActBF16 = 30;
+
+struct MeanKArgs {
+    SummaryLayout sum;
+    const uint8_t *src;    // row addressing: see kvm_produce.cu
+    int32_t type;          // kActF32 / kActF16 / kActBF16
+    uint32_t vec;          // channels per lane: 8, 4 or 1 (mean_k_vec)
+    uint32_t head_dim;
+    uint64_t nb_dim;
+    uint64_t nb_head;
+    uint64_t nb_row;       // between consecutive tokens
+    uint64_t nb_block;     // table mode: between blocks
+    uint64_t nb_layer;     // table mode: between layers (0 in token mode)
+    uint32_t layer0;
+    uint32_t block0;
+    uint32_t n_blk;
+    uint32_t block_tokens;
+    uint32_t pos0;         // token mode
+    uint32_t n;            // token mode
+    const uint32_t *n_tokens;  // table mode when non-null
+};
+
+struct AddRowsArgs {
+    float *acc;
+    uint32_t n_elem;
+    const uint8_t *src;
+    int32_t type;
+    uint32_t head_dim;
+    uint64_t nb_dim;
+    uint64_t nb_head;
+    uint64_t nb_tok;
+    const uint32_t *tok_list;  // optional: token indices to add, in order
+    uint32_t tok0;             // without a list: tokens tok0 .. tok0+n-1
+    uint32_t n;
+};
+
+// channels per lane the mean-K kernel may use for this source; align_mask is
+// the OR of the base pointer and every stride the rows are addressed with
+uint32_t mean_k_vec(int32_t type, uint32_t head_dim, uint64_t nb_dim, uint64_t align_mask);
+cudaError_t launch_mean_k(const MeanKArgs &a, uint32_t n_layers, cudaStream_t stream);
+cudaError_t launch_add_rows(const AddRowsArgs &a, cudaStream_t stream);
+cudaError_t launch_meank_flush(const SummaryLayout &s, float *meank, uint32_t layer0, uint32_t n_layers,
+                               uint32_t pos0, uint32_t n, uint32_t block_tokens, cudaStream_t stream);
 
 // --------------------------------------------------------------- query --
 struct QueryState {

@@ -78,46 +78,6 @@ __global__ void download_summaries_kernel(SummaryLayout s, uint32_t layer, uint3
     }
 }
 
-// F16 K rows -> ordered F32 token sums (RawKvStore::add_mean_f32 with off == 0).
-__global__ void summarize_kernel(SummaryLayout s, uint32_t layer0, uint32_t block0, uint32_t n,
-                                 const uint8_t *__restrict__ src, uint64_t layer_stride,
-                                 uint64_t block_stride, uint64_t row_stride,
-                                 const uint32_t *__restrict__ n_tokens, uint32_t block_tokens) {
-    __shared__ float tile[8][33];
-    const uint32_t E = s.n_embd;
-    const uint32_t l = layer0 + blockIdx.z;
-    const uint32_t bl = threadIdx.y;
-    const uint32_t i = blockIdx.x * 8u + bl;
-    const uint32_t blk = block0 + i;
-    const uint32_t e = blockIdx.y * 32u + threadIdx.x;
-    float acc = 0.0f;
-    uint32_t nt = 0;
-    if (i < n) nt = min(n_tokens[blk], block_tokens);
-    if (i < n && e < E) {
-        const uint8_t *p = src + l * layer_stride + static_cast<uint64_t>(blk) * block_stride +
-                           2ull * e;
-        for (uint32_t t = 0; t < nt; ++t) {
-            const __half h = *reinterpret_cast<const __half *>(p + t * row_stride);
-            acc = __fadd_rn(acc, __half2float(h));
-        }
-    }
-    tile[bl][threadIdx.x] = acc;
-    __syncthreads();
-    const uint32_t tid = threadIdx.y * 32u + threadIdx.x;
-    const uint32_t el = tid / 8u;
-    const uint32_t bw = tid % 8u;
-    const uint32_t ew = blockIdx.y * 32u + el;
-    const uint32_t iw = blockIdx.x * 8u + bw;
-    if (iw < n && ew < E) {
-        s.sum_t[sum_index(s, l, ew, block0 + iw)] = tile[bw][el];
-    }
-    if (blockIdx.y == 0 && threadIdx.x == 0 && i < n) {
-        const size_t at = static_cast<size_t>(l) * s.ldb + blk;
-        s.mean_tok[at] = nt;
-        s.inv_tok[at] = nt ? __fdiv_rn(1.0f, __uint2float_rn(nt)) : 0.0f;
-    }
-}
-
 // ----------------------------------------------------------------- query --
 
 // qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq and
@@ -351,19 +311,6 @@ cudaError_t launch_download_summaries(const SummaryLayout &s, uint32_t layer, ui
     if (n == 0) return cudaSuccess;
     dim3 grid((n + 31u) / 32u, (s.n_embd + 31u) / 32u);
     download_summaries_kernel<<<grid, dim3(32, 8), 0, stream>>>(s, layer, block0, n, d_sums);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_summarize(const SummaryLayout &s, uint32_t layer0, uint32_t n_layers,
-                             uint32_t block0, uint32_t n, const uint8_t *src_k,
-                             uint64_t layer_stride, uint64_t block_stride, uint64_t row_stride,
-                             const uint32_t *n_tokens, uint32_t block_tokens,
-                             cudaStream_t stream) {
-    if (n == 0 || n_layers == 0) return cudaSuccess;
-    dim3 grid((n + 7u) / 8u, (s.n_embd + 31u) / 32u, n_layers);
-    dim3 block(32, 8);
-    summarize_kernel<<<grid, block, 0, stream>>>(s, layer0, block0, n, src_k, layer_stride,
-                                                 block_stride, row_stride, n_tokens, block_tokens);
     return cudaGetLastError();
 }
 

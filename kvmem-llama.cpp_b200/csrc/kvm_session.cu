@@ -79,6 +79,11 @@ struct kvm_session {
     size_t stage_sums_cap = 0;
     uint8_t *d_ring = nullptr;
     size_t ring_bytes = 0;
+    float *d_meank = nullptr;          // decode mean-K accumulators [L][E]
+    uint32_t *d_keep = nullptr;        // kept query token indices
+    uint32_t keep_cap = 0;
+    std::vector<uint32_t> h_q_count;   // host copy of q_count
+    bool q_dirty = false;              // q_sum / q_count changed since the last query prep
     void *d_base = nullptr;            // one allocation for the small arrays
 
     // pinned ring for small host uploads / plan reads
@@ -438,6 +443,7 @@ void kvm_session_destroy(kvm_session *s) {
         cudaFree(s->sum.sum_t);
         cudaFree(s->d_base);
         cudaFree(s->d_ring);
+        cudaFree(s->d_keep);
         if (s->h_pin) cudaFreeHost(s->h_pin);
         if (s->h_plan) cudaFreeHost(s->h_plan);
         for (auto &e : s->pin_ev) if (e) cudaEventDestroy(e);
@@ -563,6 +569,7 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->d_win), sizeof(void *) * 2 * L},
         {reinterpret_cast<void **>(&s->d_stage_sums), sizeof(float) * stage_cap * E},
         {reinterpret_cast<void **>(&s->d_stage_counts), sizeof(uint32_t) * stage_cap},
+        {reinterpret_cast<void **>(&s->d_meank), sizeof(float) * L * E},
     };
     size_t total = 0;
     for (auto &it : items) total += (it.bytes + 255u) & ~static_cast<size_t>(255u);
@@ -778,12 +785,196 @@ kvm_status kvm_summarize(kvm_session *s, kvm_stream stream, uint32_t layer0, uin
     if ((reinterpret_cast<uintptr_t>(src->k) | src->row_stride | src->layer_stride | src->block_stride) & 1u)
         return fail(s, KVM_EINVAL, "F16 source must be 2-byte aligned");
     DeviceGuard g(s->device);
-    KVM_CUDA(s, launch_summarize(s->sum, layer0, n_layers, block0, n,
-                                 static_cast<const uint8_t *>(src->k), src->layer_stride,
-                                 src->block_stride, src->row_stride, s->bt.n_tokens,
-                                 s->cfg.block_tokens, as_stream(stream)),
-             "summarize launch");
+    MeanKArgs a{};
+    a.sum = s->sum;
+    a.src = static_cast<const uint8_t *>(src->k);
+    a.type = kActF16;
+    a.head_dim = s->cfg.head_dim;
+    a.nb_dim = 2;
+    a.nb_head = 2ull * s->cfg.head_dim;
+    a.nb_row = src->row_stride;
+    a.nb_block = src->block_stride;
+    a.nb_layer = src->layer_stride;
+    a.vec = mean_k_vec(a.type, a.head_dim, a.nb_dim,
+                       reinterpret_cast<uintptr_t>(src->k) | src->row_stride | src->block_stride |
+                           src->layer_stride | a.nb_head);
+    a.layer0 = layer0;
+    a.block0 = block0;
+    a.n_blk = n;
+    a.block_tokens = s->cfg.block_tokens;
+    a.n_tokens = s->bt.n_tokens;
+    KVM_CUDA(s, launch_mean_k(a, n_layers, as_stream(stream)), "summarize launch");
     s->launches++;
+    return KVM_OK;
+}
+
+namespace {
+
+kvm_status check_rows(kvm_session *s, const kvm_rows *r, uint32_t width, const char *what) {
+    if (!r || !r->data) return fail(s, KVM_EINVAL, "%s: null rows", what);
+    if (r->type != KVM_TYPE_F32 && r->type != KVM_TYPE_F16 && r->type != KVM_TYPE_BF16)
+        return fail(s, KVM_EINVAL, "%s: rows must be F32, F16 or BF16", what);
+    if (r->head_dim == 0 || static_cast<uint64_t>(r->n_head) * r->head_dim != width)
+        return fail(s, KVM_EINVAL, "%s: n_head*head_dim must be %u", what, width);
+    const uint64_t es = r->type == KVM_TYPE_F32 ? 4u : 2u;
+    const uint64_t m = reinterpret_cast<uintptr_t>(r->data) | r->nb_dim | r->nb_head | r->nb_tok;
+    if (m & (es - 1u)) return fail(s, KVM_EINVAL, "%s: rows not aligned to their element size", what);
+    return KVM_OK;
+}
+
+AddRowsArgs add_rows_args(const kvm_rows *r, float *acc, uint32_t n_elem) {
+    AddRowsArgs a{};
+    a.acc = acc;
+    a.n_elem = n_elem;
+    a.src = static_cast<const uint8_t *>(r->data);
+    a.type = r->type;
+    a.head_dim = r->head_dim;
+    a.nb_dim = r->nb_dim;
+    a.nb_head = r->nb_head;
+    a.nb_tok = r->nb_tok;
+    return a;
+}
+
+// Query prep (qv, nq) after the query accumulators changed.
+kvm_status ensure_query(kvm_session *s, cudaStream_t st) {
+    if (!s->q_dirty) return KVM_OK;
+    const uint32_t L = s->cfg.n_layer;
+    kvm_status r = upload_small(s, st, s->q.q_count, s->h_q_count.data(), sizeof(uint32_t) * L);
+    if (r != KVM_OK) return r;
+    KVM_CUDA(s, launch_query_prep(s->q, L, s->cfg.n_head_kv, s->cfg.n_head_q, s->cfg.head_dim, st),
+             "query prep");
+    s->launches++;
+    s->q_dirty = false;
+    return KVM_OK;
+}
+
+}  // namespace
+
+kvm_status kvm_write_mean_k(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t pos0, uint32_t n,
+                            const kvm_rows *k) {
+    if (!s) return KVM_EINVAL;
+    if (n == 0) return KVM_OK;
+    if (layer >= s->cfg.n_layer) return fail(s, KVM_EINVAL, "layer out of range");
+    const uint32_t T = s->cfg.block_tokens;
+    if (static_cast<uint64_t>(pos0) + n > static_cast<uint64_t>(s->max_blocks) * T)
+        return fail(s, KVM_EINVAL, "positions beyond max_blocks");
+    kvm_status r = check_rows(s, k, s->n_embd, "kvm_write_mean_k");
+    if (r != KVM_OK) return r;
+    DeviceGuard g(s->device);
+    MeanKArgs a{};
+    a.sum = s->sum;
+    a.src = static_cast<const uint8_t *>(k->data);
+    a.type = k->type;
+    a.head_dim = k->head_dim;
+    a.nb_dim = k->nb_dim;
+    a.nb_head = k->nb_head;
+    a.nb_row = k->nb_tok;
+    a.vec = mean_k_vec(a.type, a.head_dim, a.nb_dim,
+                       reinterpret_cast<uintptr_t>(k->data) | k->nb_head | k->nb_tok);
+    a.layer0 = layer;
+    a.block0 = pos0 / T;
+    a.n_blk = (pos0 + n - 1u) / T - a.block0 + 1u;
+    a.block_tokens = T;
+    a.pos0 = pos0;
+    a.n = n;
+    KVM_CUDA(s, launch_mean_k(a, 1, as_stream(stream)), "mean-k launch");
+    s->launches++;
+    return KVM_OK;
+}
+
+kvm_status kvm_meank_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t tok0, uint32_t n,
+                         const kvm_rows *k) {
+    if (!s) return KVM_EINVAL;
+    if (n == 0) return KVM_OK;
+    if (layer >= s->cfg.n_layer) return fail(s, KVM_EINVAL, "layer out of range");
+    kvm_status r = check_rows(s, k, s->n_embd, "kvm_meank_add");
+    if (r != KVM_OK) return r;
+    DeviceGuard g(s->device);
+    AddRowsArgs a = add_rows_args(k, s->d_meank + static_cast<size_t>(layer) * s->n_embd, s->n_embd);
+    a.tok0 = tok0;
+    a.n = n;
+    KVM_CUDA(s, launch_add_rows(a, as_stream(stream)), "meank add");
+    s->launches++;
+    return KVM_OK;
+}
+
+kvm_status kvm_meank_flush(kvm_session *s, kvm_stream stream, uint32_t layer0, uint32_t n_layers, uint32_t pos0,
+                           uint32_t n) {
+    if (!s) return KVM_EINVAL;
+    if (n == 0 || n_layers == 0) return KVM_OK;
+    if (static_cast<uint64_t>(layer0) + n_layers > s->cfg.n_layer) return fail(s, KVM_EINVAL, "layers out of range");
+    if (pos0 / s->cfg.block_tokens >= s->max_blocks) return fail(s, KVM_EINVAL, "position beyond max_blocks");
+    DeviceGuard g(s->device);
+    KVM_CUDA(s, launch_meank_flush(s->sum, s->d_meank, layer0, n_layers, pos0, n, s->cfg.block_tokens,
+                                   as_stream(stream)),
+             "meank flush");
+    s->launches++;
+    return KVM_OK;
+}
+
+kvm_status kvm_meank_zero(kvm_session *s, kvm_stream stream, uint32_t layer0, uint32_t n_layers) {
+    if (!s) return KVM_EINVAL;
+    if (static_cast<uint64_t>(layer0) + n_layers > s->cfg.n_layer) return fail(s, KVM_EINVAL, "layers out of range");
+    DeviceGuard g(s->device);
+    KVM_CUDA(s, cudaMemsetAsync(s->d_meank + static_cast<size_t>(layer0) * s->n_embd, 0,
+                                sizeof(float) * n_layers * s->n_embd, as_stream(stream)),
+             "meank zero");
+    return KVM_OK;
+}
+
+kvm_status kvm_query_reset(kvm_session *s, kvm_stream stream) {
+    if (!s) return KVM_EINVAL;
+    DeviceGuard g(s->device);
+    const uint32_t L = s->cfg.n_layer;
+    KVM_CUDA(s, cudaMemsetAsync(s->q.q_sum, 0, sizeof(float) * L * s->cfg.n_head_q * s->cfg.head_dim,
+                                as_stream(stream)),
+             "query reset");
+    s->h_q_count.assign(L, 0u);
+    s->q_dirty = true;
+    return KVM_OK;
+}
+
+kvm_status kvm_query_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t n, const kvm_rows *q,
+                         const uint8_t *keep) {
+    if (!s) return KVM_EINVAL;
+    if (layer >= s->cfg.n_layer) return fail(s, KVM_EINVAL, "layer out of range");
+    if (n == 0) return KVM_OK;
+    const uint32_t qdim = s->cfg.n_head_q * s->cfg.head_dim;
+    kvm_status r = check_rows(s, q, qdim, "kvm_query_add");
+    if (r != KVM_OK) return r;
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    AddRowsArgs a = add_rows_args(q, s->q.q_sum + static_cast<size_t>(layer) * qdim, qdim);
+    uint32_t kept = n;
+    if (keep) {
+        std::vector<uint32_t> list;
+        list.reserve(n);
+        for (uint32_t i = 0; i < n; ++i)
+            if (keep[i]) list.push_back(i);
+        kept = static_cast<uint32_t>(list.size());
+        if (kept == 0) return KVM_OK;
+        if (kept < n) {
+            if (kept > s->keep_cap) {
+                KVM_CUDA(s, cudaStreamSynchronize(st), "keep list sync");
+                if (s->d_keep) cudaFree(s->d_keep);
+                s->d_keep = nullptr;
+                s->keep_cap = 0;
+                const uint32_t cap = std::max(kept, 1024u);
+                KVM_CUDA(s, cudaMalloc(&s->d_keep, sizeof(uint32_t) * cap), "keep list allocation");
+                s->keep_cap = cap;
+            }
+            r = upload_small(s, st, s->d_keep, list.data(), sizeof(uint32_t) * kept);
+            if (r != KVM_OK) return r;
+            a.tok_list = s->d_keep;
+        }
+    }
+    a.tok0 = 0;
+    a.n = kept;
+    KVM_CUDA(s, launch_add_rows(a, st), "query add");
+    s->launches++;
+    if (s->h_q_count.size() != s->cfg.n_layer) s->h_q_count.assign(s->cfg.n_layer, 0u);
+    s->h_q_count[layer] += kept;
+    s->q_dirty = true;
     return KVM_OK;
 }
 
@@ -795,12 +986,9 @@ kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum, 
     const uint32_t L = s->cfg.n_layer;
     KVM_CUDA(s, cudaMemcpyAsync(s->q.q_sum, q_sum, sizeof(float) * L * s->cfg.n_head_q * s->cfg.head_dim,
                                 cudaMemcpyDefault, st), "query copy");
-    kvm_status r = upload_small(s, st, s->q.q_count, q_count, sizeof(uint32_t) * L);
-    if (r != KVM_OK) return r;
-    KVM_CUDA(s, launch_query_prep(s->q, L, s->cfg.n_head_kv, s->cfg.n_head_q, s->cfg.head_dim, st),
-             "query prep");
-    s->launches++;
-    return KVM_OK;
+    s->h_q_count.assign(q_count, q_count + L);
+    s->q_dirty = true;
+    return ensure_query(s, st);
 }
 
 static ScoreArgs score_args(kvm_session *s) {
@@ -825,6 +1013,8 @@ kvm_status kvm_score(kvm_session *s, kvm_stream stream, double *d_scores) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
     cudaStream_t st = as_stream(stream);
+    kvm_status r = ensure_query(s, st);
+    if (r != KVM_OK) return r;
     ScoreArgs a = score_args(s);
     a.layer0 = 0;
     a.n_layers = s->cfg.n_layer;
@@ -843,6 +1033,8 @@ kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0, u
     if (static_cast<uint64_t>(layer0) + n_layers > s->cfg.n_layer) return fail(s, KVM_EINVAL, "layers out of range");
     if (!d_terms || ldt < s->n_blocks) return fail(s, KVM_EINVAL, "bad terms buffer");
     DeviceGuard g(s->device);
+    kvm_status r = ensure_query(s, as_stream(stream));
+    if (r != KVM_OK) return r;
     ScoreArgs a = score_args(s);
     a.layer0 = layer0;
     a.n_layers = n_layers;

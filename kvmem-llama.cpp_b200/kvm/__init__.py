@@ -21,6 +21,7 @@ PKG = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "libkvm.so")
 
 TYPE_F16, TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0 = 1, 2, 6, 8
+TYPE_F32, TYPE_BF16 = 0, 30
 TIER_GPU, TIER_CPU, TIER_SSD = 0, 1, 2
 LOC_DEVICE, LOC_HOST = 0, 1
 
@@ -36,7 +37,8 @@ ABI_SYMBOLS = (
     "kvm_score_terms", "kvm_reduce_terms", "kvm_set_scores_from_sum", "kvm_set_scores", "kvm_select",
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
-    "kvm_quantize_rows_noalloc",
+    "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
+    "kvm_meank_zero", "kvm_query_reset", "kvm_query_add",
 )
 
 
@@ -70,6 +72,30 @@ class Source(C.Structure):
     _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("layer_stride", C.c_uint64),
                 ("block_stride", C.c_uint64), ("row_stride", C.c_uint64),
                 ("location", C.c_int32), ("reserved0", C.c_int32)]
+
+
+class Rows(C.Structure):
+    """kvm_rows: a captured ggml activation (token t, head h, dim d) at
+    data + t*nb_tok + h*nb_head + d*nb_dim."""
+    _fields_ = [("data", C.c_void_p), ("type", C.c_int32), ("n_head", C.c_uint32),
+                ("head_dim", C.c_uint32), ("reserved0", C.c_uint32), ("nb_dim", C.c_uint64),
+                ("nb_head", C.c_uint64), ("nb_tok", C.c_uint64)]
+
+
+_TORCH_TYPES = {"torch.float32": TYPE_F32, "torch.float16": TYPE_F16, "torch.bfloat16": TYPE_BF16}
+
+
+def rows_of(t, n_head: int, head_dim: int) -> Rows:
+    """kvm_rows of a torch tensor [tokens, n_head, head_dim] (any strides) or
+    [tokens, n_head*head_dim] (row-major heads)."""
+    ty = _TORCH_TYPES[str(t.dtype)]
+    es = t.element_size()
+    if t.dim() == 3:
+        nb_tok, nb_head, nb_dim = (x * es for x in t.stride())
+    else:
+        nb_tok, nb_dim = t.stride(0) * es, t.stride(1) * es
+        nb_head = head_dim * nb_dim
+    return Rows(t.data_ptr(), ty, n_head, head_dim, 0, nb_dim, nb_head, nb_tok)
 
 
 class Window(C.Structure):
@@ -143,6 +169,12 @@ def lib():
             "kvm_kernel_launches": (u64, [vp]),
             "kvm_quantize_rows": (C.c_int, [vp, i32, vp, u64, u32, vp]),
             "kvm_quantize_rows_noalloc": (C.c_int, [vp, i32, vp, u64, u32, vp]),
+            "kvm_write_mean_k": (C.c_int, [vp, vp, u32, u32, u32, C.POINTER(Rows)]),
+            "kvm_meank_add": (C.c_int, [vp, vp, u32, u32, u32, C.POINTER(Rows)]),
+            "kvm_meank_flush": (C.c_int, [vp, vp, u32, u32, u32, u32]),
+            "kvm_meank_zero": (C.c_int, [vp, vp, u32, u32]),
+            "kvm_query_reset": (C.c_int, [vp, vp]),
+            "kvm_query_add": (C.c_int, [vp, vp, u32, u32, C.POINTER(Rows), vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -279,6 +311,35 @@ class Session:
         qc = np.ascontiguousarray(np.asarray(q_count, dtype=np.uint32))
         self._check(lib().kvm_set_query(self.h, _stream(stream), _ptr(q_sum), qc.ctypes.data),
                     "set_query")
+
+    # ---- device producers (harvest of K summaries and the query)
+    def write_mean_k(self, layer, pos0, n, rows: Rows, stream=None):
+        self._check(lib().kvm_write_mean_k(self.h, _stream(stream), layer, pos0, n, C.byref(rows)),
+                    "write_mean_k")
+
+    def meank_add(self, layer, tok0, n, rows: Rows, stream=None):
+        self._check(lib().kvm_meank_add(self.h, _stream(stream), layer, tok0, n, C.byref(rows)),
+                    "meank_add")
+
+    def meank_flush(self, pos0, n, layer0=0, n_layers=None, stream=None):
+        n_layers = self.cfg.n_layer if n_layers is None else n_layers
+        self._check(lib().kvm_meank_flush(self.h, _stream(stream), layer0, n_layers, pos0, n),
+                    "meank_flush")
+
+    def meank_zero(self, layer0=0, n_layers=None, stream=None):
+        n_layers = self.cfg.n_layer if n_layers is None else n_layers
+        self._check(lib().kvm_meank_zero(self.h, _stream(stream), layer0, n_layers), "meank_zero")
+
+    def query_reset(self, stream=None):
+        self._check(lib().kvm_query_reset(self.h, _stream(stream)), "query_reset")
+
+    def query_add(self, layer, n, rows: Rows, keep=None, stream=None):
+        kp = None
+        if keep is not None:
+            kp = np.ascontiguousarray(np.asarray(keep, dtype=np.uint8))
+            assert kp.size >= n
+        self._check(lib().kvm_query_add(self.h, _stream(stream), layer, n, C.byref(rows),
+                                         None if kp is None else kp.ctypes.data), "query_add")
 
     # ---- stages
     def score(self, d_scores=None, stream=None):

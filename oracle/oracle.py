@@ -171,6 +171,7 @@ def ref():
         R.ref_raw_free.argtypes = [C.c_void_p]
         R.ref_raw_write_mean_k.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
         R.ref_raw_mean_k.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]
+        R.ref_raw_write_mean_sum.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
         R.ref_raw_has_block.restype = C.c_int
         R.ref_raw_has_block.argtypes = [C.c_void_p, C.c_uint32]
         _ref = R
@@ -217,6 +218,59 @@ def mean_k(sum_: np.ndarray, n: int) -> np.ndarray:
     out = np.empty_like(s)
     lib().ora_mean_k(s, n, s.size, out)
     return out
+
+
+def add_rows(acc: np.ndarray, rows: np.ndarray) -> np.ndarray:
+    """acc[j] += rows[t][j] for t in order, in F32 -- the decode accumulator
+    (meank_add_*, src/adapter/llama-kvmem-stagein.cu:269-315) and the query
+    harvest (llama-memory-kvmem.cpp:2164-2171).  Returns the new acc."""
+    out = np.array(acc, dtype=np.float32, copy=True)
+    for r in np.asarray(rows, dtype=np.float32):
+        out = (out + r).astype(np.float32)
+    return out
+
+
+class MeanStore:
+    """The mean-K statistics of kvmem::RawKvStore, restated: per (layer,
+    block) an F32 sum and mean_tokens.
+
+    write_layer_mean_k  follows raw_kv_store.cpp:674-694 with add_mean_f32
+                        (:204-223): a write at block offset 0 restarts the
+                        sum, rows are added in order, mean_tokens = take
+                        (offset 0) or max(mean_tokens, offset+take);
+    write_layer_mean_sum follows :696-720 (one block; sum += the given sum);
+    mean_k               follows :976-996 (sum * (1.0f / mean_tokens))."""
+
+    def __init__(self, n_layer, n_blocks, n_embd, block_tokens):
+        self.T = block_tokens
+        self.sums = np.zeros((n_layer, n_blocks, n_embd), np.float32)
+        self.mean_tok = np.zeros((n_layer, n_blocks), np.uint32)
+
+    def write_layer_mean_k(self, pos0, rows_f32, il):
+        rows = np.asarray(rows_f32, dtype=np.float32)
+        done, n = 0, rows.shape[0]
+        while done < n:
+            pos = pos0 + done
+            bid, off = pos // self.T, pos % self.T
+            take = min(n - done, self.T - off)
+            start = np.zeros_like(self.sums[il, bid]) if off == 0 else self.sums[il, bid]
+            self.sums[il, bid] = add_rows(start, rows[done:done + take])
+            mt = take if off == 0 else max(int(self.mean_tok[il, bid]), off + take)
+            self.mean_tok[il, bid] = mt
+            done += take
+
+    def write_layer_mean_sum(self, pos0, n, il, sum_f32):
+        bid, off = pos0 // self.T, pos0 % self.T
+        take = min(n, self.T - off)
+        start = np.zeros_like(self.sums[il, bid]) if off == 0 else self.sums[il, bid]
+        self.sums[il, bid] = (start + np.asarray(sum_f32, np.float32)).astype(np.float32)
+        self.mean_tok[il, bid] = take if off == 0 else max(int(self.mean_tok[il, bid]), off + take)
+
+    def mean_k(self, bid, il):
+        mt = int(self.mean_tok[il, bid])
+        if mt == 0:
+            return np.zeros(self.sums.shape[2], np.float32)
+        return mean_k(self.sums[il, bid], mt)
 
 
 def score(sums, mean_tok, has_block, q_sum, q_count, n_head_kv, n_head_q, head_dim,
@@ -446,6 +500,10 @@ class RefRaw:
     def write_layer_mean_k(self, pos0, k_rows_f32, il):
         k = np.ascontiguousarray(k_rows_f32, dtype=np.float32)
         ref().ref_raw_write_mean_k(self.h, pos0, k.shape[0], il, k)
+
+    def write_layer_mean_sum(self, pos0, n, il, sum_f32):
+        v = np.ascontiguousarray(sum_f32, dtype=np.float32)
+        ref().ref_raw_write_mean_sum(self.h, pos0, n, il, v)
 
     def mean_k(self, block_id, il):
         out = np.zeros(self.n_embd, dtype=np.float32)

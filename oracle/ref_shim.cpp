@@ -144,6 +144,10 @@ void ref_raw_write_mean_k(void *r, uint32_t pos0, uint32_t n, uint32_t il, const
     static_cast<kvmem::RawKvStore *>(r)->write_layer_mean_k(pos0, n, il, k);
 }
 
+void ref_raw_write_mean_sum(void *r, uint32_t pos0, uint32_t n, uint32_t il, const float *sum) {
+    static_cast<kvmem::RawKvStore *>(r)->write_layer_mean_sum(pos0, n, il, sum);
+}
+
 void ref_raw_mean_k(void *r, uint32_t block_id, uint32_t il, float *out) {
     static_cast<kvmem::RawKvStore *>(r)->mean_k(block_id, il, out);
 }

@@ -10,6 +10,12 @@ Outputs (all small, committed):
   store_golden.json  selection + KvMemPlan sequences produced by the reference's own
                      kvmem::KvMemStore (oracle/_ref/libkvmem_ref.so)
   meank_golden.npz   means produced by the reference's own kvmem::RawKvStore
+  meank_seq_golden.npz  a prefill + decode sequence on kvmem::RawKvStore: uneven
+                     write_layer_mean_k batches across block edges (prefill
+                     harvest), then decode sums flushed with write_layer_mean_sum
+                     from mid-block and block-start positions; the means after it
+
+`python tests/golden/make_golden.py meank_seq` regenerates only the named fixtures.
 """
 import json
 import os
@@ -118,12 +124,64 @@ def make_meank(rng):
                         block_tokens=bt)
 
 
+def meank_seq_ops(rng, L, E, bt):
+    """The operation list of meank_seq_golden: ("k", il, pos0, rows) for
+    write_layer_mean_k and ("s", il, pos0, n, sum) for write_layer_mean_sum."""
+    ops = []
+    prefill = 2 * bt + 9                    # ends mid-block
+    for il in range(L):
+        k = rng.standard_normal((prefill, E)).astype(np.float32) * 4
+        k[:, rng.choice(E, 3, replace=False)] *= 20
+        pos = 0
+        for n in (5, bt - 5 + 3, 17, prefill):   # uneven batches across block edges
+            n = min(n, prefill - pos)
+            if n <= 0:
+                break
+            ops.append(("k", il, pos, k[pos:pos + n]))
+            pos += n
+    # decode: sums of the tokens after the prefill, flushed when the block fills,
+    # then one full block from its start, then a partial block
+    pos = prefill
+    for n in (bt - prefill % bt, bt, 7):
+        for il in range(L):
+            rows = rng.standard_normal((n, E)).astype(np.float32)
+            ops.append(("s", il, pos, n, O.add_rows(np.zeros(E, np.float32), rows)))
+        pos += n
+    return ops, pos
+
+
+def make_meank_seq(rng):
+    L, E, bt = 2, 64, 16
+    ops, end = meank_seq_ops(rng, L, E, bt)
+    raw = O.RefRaw(L, E, bt)
+    for op in ops:
+        if op[0] == "k":
+            raw.write_layer_mean_k(op[2], op[3], op[1])
+        else:
+            raw.write_layer_mean_sum(op[2], op[3], op[1], op[4])
+    nb = (end + bt - 1) // bt
+    means = np.stack([np.stack([raw.mean_k(b, il) for b in range(nb)]) for il in range(L)])
+    arrays = dict(means=means, block_tokens=bt, n_layer=L, n_embd=E, n_ops=len(ops))
+    for i, op in enumerate(ops):
+        if op[0] == "k":
+            arrays[f"op{i}"] = np.array([0, op[1], op[2], op[3].shape[0]], np.int64)
+            arrays[f"rows{i}"] = op[3]
+        else:
+            arrays[f"op{i}"] = np.array([1, op[1], op[2], op[3]], np.int64)
+            arrays[f"rows{i}"] = op[4][None, :]
+    np.savez_compressed(os.path.join(HERE, "meank_seq_golden.npz"), **arrays)
+
+
 if __name__ == "__main__":
     O.build(ref=True)
     if not O.have_ref():
         sys.exit("oracle/_ref/libkvmem_ref.so missing: needs the reference tree")
-    rng = np.random.default_rng(20261201)
-    make_quant(rng)
-    make_store(rng)
-    make_meank(rng)
+    only = set(sys.argv[1:])
+    if not only or only & {"quant", "store", "meank"}:
+        rng = np.random.default_rng(20261201)
+        make_quant(rng)
+        make_store(rng)
+        make_meank(rng)
+    if not only or "meank_seq" in only:
+        make_meank_seq(np.random.default_rng(20261202))
     print("golden fixtures written to", HERE)

@@ -7,9 +7,25 @@ plan, chronological layout and the quantized window bytes.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load_meank_seq():
+    """The meank_seq_golden operation list -- ("k", il, pos0, rows) for
+    write_layer_mean_k and ("s", il, pos0, n, sum) for write_layer_mean_sum --
+    and the npz holding the reference RawKvStore's means after it."""
+    g = np.load(os.path.join(GOLD, "meank_seq_golden.npz"))
+    ops = []
+    for i in range(int(g["n_ops"])):
+        kind, il, pos0, n = (int(x) for x in g[f"op{i}"])
+        rows = g[f"rows{i}"]
+        ops.append(("k", il, pos0, rows) if kind == 0 else ("s", il, pos0, n, rows[0]))
+    return ops, g
 
 
 @dataclass

@@ -130,6 +130,32 @@ def test_mean_k_live_vs_reference(oracle):
     assert not raw.has_block(9)
 
 
+def test_mean_store_sequence_matches_reference_golden(oracle):
+    from kvm_testlib import load_meank_seq
+    ops, g = load_meank_seq()
+    L, E, bt = int(g["n_layer"]), int(g["n_embd"]), int(g["block_tokens"])
+    nb = g["means"].shape[1]
+    ms = oracle.MeanStore(L, nb, E, bt)
+    for op in ops:
+        if op[0] == "k":
+            ms.write_layer_mean_k(op[2], op[3], op[1])
+        else:
+            ms.write_layer_mean_sum(op[2], op[3], op[1], op[4])
+    for il in range(L):
+        for b in range(nb):
+            assert ms.mean_k(b, il).tobytes() == g["means"][il, b].tobytes(), (il, b)
+    # the sequence covers mid-block flushes, block-start flushes and partial blocks
+    kinds = {(op[0], op[2] % bt == 0) for op in ops}
+    assert ("s", False) in kinds and ("s", True) in kinds and ("k", False) in kinds
+
+
+def test_add_rows_is_the_ordered_f32_sum(oracle):
+    rows = np.array([[1e8], [1.0], [-1e8], [1.0]], np.float32)
+    # (((0 + 1e8) + 1) - 1e8) + 1 = 1 in F32 order; a pairwise sum would give 2
+    assert oracle.add_rows(np.zeros(1, np.float32), rows)[0] == np.float32(1.0)
+    assert oracle.add_rows(np.array([-0.0], np.float32), np.array([[-0.0]], np.float32))[0] == 0.0
+
+
 # ------------------------------------------------------ selection + diff ---
 
 def _cfg_from(oracle, c):
