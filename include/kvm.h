@@ -297,6 +297,43 @@ kvm_status kvm_query_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint
 kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum,
                          const uint32_t *q_count);
 
+/* ---------------------------------------------- stage-in transform mode -- */
+
+/*
+ * Optional per-head transforms applied to the F16 rows between the gather and
+ * the quantizer (the reference's quantizing stage-in, llama-kvmem-stagein.cu:
+ * 632-753: RoPE at the original position, then attn_rot, then quantize), so
+ * F16 pre-RoPE history can feed a rotated quantized cache:
+ *   K: NeoX RoPE of the first rope_n_rot dims of every head at the token's
+ *      original position (block_id * block_tokens + row), then the
+ *      Walsh-Hadamard transform of every rot_k chunk of every head;
+ *   V: the Walsh-Hadamard transform of every rot_v chunk.
+ * The RoPE frequencies follow kvmem::rope_neox_apply (kvmem/src/host/
+ * rope.cpp:8-45): theta_i = powf(freq_base, -2i/n_rot) * freq_scale; the
+ * Hadamard transform follows fwht_kernel (llama-kvmem-stagein.cu:104-130):
+ * scale by 1/sqrtf(n) first, then butterflies h = 1, 2, 4, ...  Zero fields
+ * switch a transform off.  rot_k / rot_v must be 64, 128, 256 or 512 and
+ * divide head_dim; rope_n_rot a multiple of 64 up to head_dim.  The window
+ * types must be quantized (Q8_0 / Q4_0 / Q5_0) for a Hadamard transform, as
+ * kvmem_attn_rot_on requires; head_dim must be 64, 128, 256 or 512.
+ */
+typedef struct kvm_transform {
+    uint32_t rot_k;
+    uint32_t rot_v;
+    uint32_t rope_n_rot;
+    uint32_t reserved0;
+    float rope_freq_base;
+    float rope_freq_scale;
+} kvm_transform;
+
+/* Set (or, with NULL, clear) the transforms of later stage-ins. */
+kvm_status kvm_set_transform(kvm_session *s, const kvm_transform *t);
+/* The reference's attn_rot rule (kvmem_attn_rot_on, kvmem_hadamard_nrot_k /
+ * _v, src/adapter/llama-kvmem-quant.h:22-40): the Hadamard size a cache of
+ * `type` gets for K (is_k = 1) or V, 0 when attn_rot is off for it.  The
+ * LLAMA_ATTN_ROT_DISABLE environment switch is the caller's to read. */
+uint32_t kvm_attn_rot_nrot(int32_t type, uint32_t head_dim, int is_k);
+
 /* ----------------------------------------------------- reselection step -- */
 
 /* Scores of every block (f64, score_retrieval); optional copy to d_scores. */

@@ -56,6 +56,13 @@ struct StageinArgs {
     uint32_t tile_out_bytes;
     uint32_t bulk_store;
     uint32_t *status;
+    // transform mode (kvm_set_transform): xform = head_dim / 32 when a
+    // transform is on, 0 for the plain gather + quantize
+    uint32_t xform;
+    uint32_t rot_k;
+    uint32_t rot_v;
+    uint32_t rope_n_rot;
+    const float *theta;            // device [rope_n_rot / 2]
 };
 
 uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens);

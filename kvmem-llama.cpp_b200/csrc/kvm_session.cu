@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
@@ -83,6 +84,8 @@ struct kvm_session {
     uint32_t *d_keep = nullptr;        // kept query token indices
     uint32_t keep_cap = 0;
     std::vector<uint32_t> h_q_count;   // host copy of q_count
+    kvm_transform xf{};                // stage-in transforms (all zero = off)
+    float *d_theta = nullptr;          // RoPE frequencies [head_dim / 2]
     bool q_dirty = false;              // q_sum / q_count changed since the last query prep
     void *d_base = nullptr;            // one allocation for the small arrays
 
@@ -247,6 +250,13 @@ StageinArgs stagein_common(kvm_session *s) {
     const uint32_t out_max = a.rows_per_tile * std::max(s->row_bytes_k, s->row_bytes_v);
     a.tile_out_bytes = (out_max + 15u) & ~15u;
     a.bulk_store = (s->row_bytes_k % 16u == 0 && s->row_bytes_v % 16u == 0 && window_aligned16(s)) ? 1u : 0u;
+    if (s->xf.rot_k || s->xf.rot_v || s->xf.rope_n_rot) {
+        a.xform = s->cfg.head_dim / 32u;
+        a.rot_k = s->xf.rot_k;
+        a.rot_v = s->xf.rot_v;
+        a.rope_n_rot = s->xf.rope_n_rot;
+        a.theta = s->d_theta;
+    }
     a.status = s->d_status;
     return a;
 }
@@ -570,6 +580,7 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->d_stage_sums), sizeof(float) * stage_cap * E},
         {reinterpret_cast<void **>(&s->d_stage_counts), sizeof(uint32_t) * stage_cap},
         {reinterpret_cast<void **>(&s->d_meank), sizeof(float) * L * E},
+        {reinterpret_cast<void **>(&s->d_theta), sizeof(float) * (kMaxHeadDim / 2)},
     };
     size_t total = 0;
     for (auto &it : items) total += (it.bytes + 255u) & ~static_cast<size_t>(255u);
@@ -849,6 +860,59 @@ kvm_status ensure_query(kvm_session *s, cudaStream_t st) {
 }
 
 }  // namespace
+
+uint32_t kvm_attn_rot_nrot(int32_t type, uint32_t head_dim, int is_k) {
+    // kvmem_attn_rot_on: quantized cache, head_dim a multiple of 64
+    if (type != KVM_TYPE_Q8_0 && type != KVM_TYPE_Q4_0 && type != KVM_TYPE_Q5_0) return 0u;
+    if (head_dim < 64u || head_dim % 64u != 0u) return 0u;
+    if (!is_k) return 64u;                              // kvmem_hadamard_nrot_v
+    uint32_t nrot = 64u;                                // kvmem_hadamard_nrot_k
+    do {
+        nrot *= 2u;
+    } while (head_dim % nrot == 0u);
+    return nrot / 2u;
+}
+
+kvm_status kvm_set_transform(kvm_session *s, const kvm_transform *t) {
+    if (!s) return KVM_EINVAL;
+    if (!t) {
+        s->xf = kvm_transform{};
+        return KVM_OK;
+    }
+    const uint32_t D = s->cfg.head_dim;
+    auto rot_ok = [&](uint32_t n) {
+        return n == 0u || ((n == 64u || n == 128u || n == 256u || n == 512u) && D % n == 0u);
+    };
+    if (!rot_ok(t->rot_k) || !rot_ok(t->rot_v))
+        return fail(s, KVM_EINVAL, "rot_k / rot_v must be 0, 64, 128, 256 or 512 and divide head_dim");
+    if (t->rope_n_rot % 64u != 0u || t->rope_n_rot > D)
+        return fail(s, KVM_EINVAL, "rope_n_rot must be a multiple of 64 up to head_dim");
+    const bool on = t->rot_k || t->rot_v || t->rope_n_rot;
+    if (on && !(D == 64u || D == 128u || D == 192u || D == 256u || D == 384u || D == 512u))
+        return fail(s, KVM_EINVAL, "transforms need head_dim 64, 128, 192, 256, 384 or 512");
+    auto quantized = [](int32_t ty) {
+        return ty == KVM_TYPE_Q8_0 || ty == KVM_TYPE_Q4_0 || ty == KVM_TYPE_Q5_0;
+    };
+    if ((t->rot_k && !quantized(s->cfg.type_k)) || (t->rot_v && !quantized(s->cfg.type_v)))
+        return fail(s, KVM_EINVAL, "a Hadamard transform needs a quantized window type");
+    if (t->rope_n_rot) {
+        // kvmem::rope_neox_apply, kvmem/src/host/rope.cpp:18-22
+        const uint32_t half = t->rope_n_rot / 2u;
+        std::vector<float> theta(half);
+        for (uint32_t i = 0; i < half; ++i) {
+            theta[i] = powf(t->rope_freq_base,
+                            -2.0f * static_cast<float>(i) / static_cast<float>(t->rope_n_rot));
+            theta[i] *= t->rope_freq_scale;
+        }
+        DeviceGuard g(s->device);
+        // later stage-ins read the table: wait for earlier ones to finish with it
+        KVM_CUDA(s, cudaDeviceSynchronize(), "transform sync");
+        KVM_CUDA(s, cudaMemcpy(s->d_theta, theta.data(), sizeof(float) * half, cudaMemcpyHostToDevice),
+                 "theta upload");
+    }
+    s->xf = *t;
+    return KVM_OK;
+}
 
 kvm_status kvm_write_mean_k(kvm_session *s, kvm_stream stream, uint32_t layer, uint32_t pos0, uint32_t n,
                             const kvm_rows *k) {

@@ -34,12 +34,13 @@ struct TaskDesc {
     uint8_t *dst;
     uint32_t rows;
     uint32_t kv;
+    uint32_t pos0;     // original position of the tile's first row
     bool valid;
 };
 
 __device__ __forceinline__ TaskDesc decode_task(const StageinArgs &a, uint64_t t,
                                                 uint32_t tiles, uint32_t n_items) {
-    TaskDesc d{nullptr, nullptr, 0u, 0u, false};
+    TaskDesc d{nullptr, nullptr, 0u, 0u, 0u, false};
     const uint64_t per_item = static_cast<uint64_t>(a.n_layer) * a.n_kv * tiles;
     const uint32_t item = static_cast<uint32_t>(t / per_item);
     uint32_t r = static_cast<uint32_t>(t % per_item);
@@ -64,6 +65,7 @@ __device__ __forceinline__ TaskDesc decode_task(const StageinArgs &a, uint64_t t
     if (row0 >= nt) return d;
     d.rows = min(a.rows_per_tile, nt - row0);
     d.kv = kv;
+    d.pos0 = block * a.block_tokens + row0;
     const uint64_t src_index = a.src_by_item ? item : block;
     const uint8_t *sbase = kv ? a.src_v : a.src_k;
     d.src = sbase + layer * a.layer_stride + src_index * a.item_stride + row0 * a.row_stride;
@@ -98,7 +100,7 @@ struct TileSlot {
     uint32_t rows;
     int32_t type;
     uint32_t out_bytes;
-    uint32_t pad;
+    uint32_t meta;     // bit 31: V tile; bits 0-30: original position of row 0
 };
 static_assert(sizeof(TileSlot) == 24, "TileSlot");
 
@@ -106,7 +108,125 @@ static_assert(sizeof(TileSlot) == 24, "TileSlot");
 // then NS input tiles and NS output tiles.
 constexpr uint32_t kStageinHeader = 384;
 
-template <int NS>
+// ------------------------------------------------------- transform mode --
+//
+// One warp per (row, head) of NREG*32 values; value i of the head lives in
+// lane i % 32, register i / 32.  Every float operation is a round-to-nearest
+// intrinsic, so the Hadamard and quantizer steps match the CPU bit for bit;
+// RoPE calls the CUDA sincosf (the reference's GPU kernel does the same) and
+// agrees with the host cosf / sinf to within their last-bit errors.
+
+// A ggml block spread over the warp (value j in lane j) into its bytes.
+__device__ __forceinline__ void quant_warp(int type, float x, uint8_t *blk, int lane) {
+    const unsigned full = 0xffffffffu;
+    if (type == KVM_TYPE_F16) {
+        st_u16(blk + 2 * lane, f16_bits(x));
+        return;
+    }
+    float amax = fabsf(x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(full, amax, o));
+    if (type == KVM_TYPE_Q8_0) {
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        if (lane == 0) st_u16(blk, f16_bits(d));
+        blk[2 + lane] = static_cast<uint8_t>(round_half_away(__fmul_rn(x, id)) & 0xff);
+        return;
+    }
+    const bool q5 = type == KVM_TYPE_Q5_0;
+    // the reference's strict `amax < |v|` scan keeps the first value of
+    // largest magnitude, and +0.0 when every value is zero
+    const unsigned hit = __ballot_sync(full, fabsf(x) == amax);
+    float vmax = __shfl_sync(full, x, __ffs(hit) - 1);
+    if (amax == 0.0f) vmax = 0.0f;
+    const float d = __fdiv_rn(vmax, q5 ? -16.0f : -8.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const uint32_t code = code_q(x, id, q5 ? 16.5f : 8.5f, q5 ? 31 : 15);
+    const uint32_t partner = __shfl_down_sync(full, code, 16);
+    const unsigned qh = __ballot_sync(full, (code >> 4) & 1u);
+    if (lane == 0) {
+        st_u16(blk, f16_bits(d));
+        if (q5) {
+            st_u16(blk + 2, qh & 0xffffu);
+            st_u16(blk + 4, qh >> 16);
+        }
+    }
+    if (lane < 16) blk[(q5 ? 6 : 2) + lane] = static_cast<uint8_t>((code & 15u) | ((partner & 15u) << 4));
+}
+
+template <int NREG>
+__device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
+                                               uint8_t *ob, int warp, int lane) {
+    constexpr uint32_t D = NREG * 32u;
+    const bool is_v = (ts.meta >> 31) != 0u;
+    const uint32_t pos0 = ts.meta & 0x7fffffffu;
+    const uint32_t nrot = is_v ? a.rot_v : a.rot_k;
+    const uint32_t n_rope = is_v ? 0u : a.rope_n_rot;
+    const uint32_t half = n_rope / 2u;
+    const uint32_t H = a.n_embd / D;
+    const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
+    const uint32_t bb = static_cast<uint32_t>(block_bytes(ts.type));
+    const float scale = nrot ? __fdiv_rn(1.0f, __fsqrt_rn(__uint2float_rn(nrot))) : 1.0f;
+    const uint32_t units = ts.rows * H;
+    for (uint32_t u = static_cast<uint32_t>(warp); u < units; u += kStageinConsumerWarps) {
+        const uint32_t row = u / H;
+        const uint32_t h = u - row * H;
+        const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
+        const float pos = __uint2float_rn(pos0 + row);
+        float v[NREG];
+#pragma unroll
+        for (int r = 0; r < NREG; ++r) {
+            const uint32_t i = static_cast<uint32_t>(r) * 32u + static_cast<uint32_t>(lane);
+            float y = __half2float(x[i]);
+            if (i < n_rope) {
+                // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i]
+                const bool lo = i < half;
+                const uint32_t f = lo ? i : i - half;
+                const float other = __half2float(x[lo ? i + half : i - half]);
+                float sn, cs;
+                sincosf(__fmul_rn(pos, a.theta[f]), &sn, &cs);
+                y = lo ? __fsub_rn(__fmul_rn(y, cs), __fmul_rn(other, sn))
+                       : __fadd_rn(__fmul_rn(other, sn), __fmul_rn(y, cs));
+            }
+            v[r] = y;
+        }
+        if (nrot) {
+#pragma unroll
+            for (int r = 0; r < NREG; ++r) v[r] = __fmul_rn(v[r], scale);
+            // butterflies of span 1 .. 16: across lanes
+#pragma unroll
+            for (int hh = 1; hh < 32; hh <<= 1) {
+                const bool upper = (lane & hh) != 0;
+#pragma unroll
+                for (int r = 0; r < NREG; ++r) {
+                    const float p = __shfl_xor_sync(0xffffffffu, v[r], hh);
+                    v[r] = upper ? __fsub_rn(p, v[r]) : __fadd_rn(v[r], p);
+                }
+            }
+            // spans 32 .. nrot/2: across registers of the same lane
+#pragma unroll
+            for (int hr = 1; hr < NREG; hr <<= 1) {
+                if (32u * static_cast<uint32_t>(hr) < nrot) {
+#pragma unroll
+                    for (int r = 0; r < NREG; ++r) {
+                        if ((r & hr) == 0 && (r | hr) < NREG) {
+                            const float p = v[r];
+                            const float q = v[r | hr];
+                            v[r] = __fadd_rn(p, q);
+                            v[r | hr] = __fsub_rn(p, q);
+                        }
+                    }
+                }
+            }
+        }
+        uint8_t *orow = ob + static_cast<size_t>(row) * rb;
+#pragma unroll
+        for (int r = 0; r < NREG; ++r)
+            quant_warp(ts.type, v[r], orow + static_cast<size_t>(h * NREG + r) * bb, lane);
+    }
+}
+
+template <int NS, int NREG>
 __global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -151,6 +271,7 @@ __global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs
                 ts.rows = d.rows;
                 ts.type = d.kv ? a.type_v : a.type_k;
                 ts.out_bytes = d.rows * (d.kv ? a.row_bytes_v : a.row_bytes_k);
+                ts.meta = (d.pos0 & 0x7fffffffu) | (d.kv ? 0x80000000u : 0u);
                 issue_tile_load(a, d, in_buf + s * a.tile_in_bytes, &full[s]);
                 ++issued;
                 return;
@@ -227,6 +348,16 @@ __global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs
         if (ts.rows == 0) break;
         const uint8_t *ib = in_buf + s * a.tile_in_bytes;
         uint8_t *ob = out_buf + s * a.tile_out_bytes;
+        if (NREG > 0) {
+            const bool is_v = (ts.meta >> 31) != 0u;
+            if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
+                transform_tile<(NREG > 0 ? NREG : 1)>(a, ts, ib, ob, warp, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&done[s]);
+                continue;
+            }
+        }
         const uint32_t nqb = ts.rows * qb_per_row;
         for (uint32_t qb = static_cast<uint32_t>(warp * 32 + lane); qb < nqb;
              qb += kStageinConsumerWarps * 32u) {
@@ -379,21 +510,37 @@ static bool attr_once(std::atomic<uint64_t> &done, const void *fn, int bytes) {
 static std::atomic<uint64_t> g_stagein_attr{0};
 static std::atomic<uint64_t> g_permute_attr{0};
 
-cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
+template <int NREG>
+static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap,
+                                    std::atomic<uint64_t> &attr) {
     const size_t smem = stagein_smem_bytes(a);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    if (!attr_once(g_stagein_attr, reinterpret_cast<const void *>(stagein_kernel<kStageinStages>),
-                   200 * 1024))
-        return cudaErrorInvalidValue;
+    const void *fn = reinterpret_cast<const void *>(stagein_kernel<kStageinStages, NREG>);
+    if (!attr_once(attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages>,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages, NREG>,
                                                   kStageinThreads, smem);
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    stagein_kernel<kStageinStages><<<grid, kStageinThreads, smem, stream>>>(a);
+    stagein_kernel<kStageinStages, NREG><<<grid, kStageinThreads, smem, stream>>>(a);
     return cudaGetLastError();
+}
+
+static std::atomic<uint64_t> g_xform_attr[6];
+
+cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
+    switch (a.xform) {
+        case 0: return launch_stagein_t<0>(a, stream, grid_cap, g_stagein_attr);
+        case 2: return launch_stagein_t<2>(a, stream, grid_cap, g_xform_attr[0]);
+        case 4: return launch_stagein_t<4>(a, stream, grid_cap, g_xform_attr[1]);
+        case 6: return launch_stagein_t<6>(a, stream, grid_cap, g_xform_attr[2]);
+        case 8: return launch_stagein_t<8>(a, stream, grid_cap, g_xform_attr[3]);
+        case 12: return launch_stagein_t<12>(a, stream, grid_cap, g_xform_attr[4]);
+        case 16: return launch_stagein_t<16>(a, stream, grid_cap, g_xform_attr[5]);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {

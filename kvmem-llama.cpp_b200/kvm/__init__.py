@@ -38,7 +38,8 @@ ABI_SYMBOLS = (
     "kvm_set_selection_ids", "kvm_diff", "kvm_stagein", "kvm_step", "kvm_wait", "kvm_get_plan",
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
     "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
-    "kvm_meank_zero", "kvm_query_reset", "kvm_query_add",
+    "kvm_meank_zero", "kvm_query_reset", "kvm_query_add", "kvm_set_transform",
+    "kvm_attn_rot_nrot",
 )
 
 
@@ -96,6 +97,17 @@ def rows_of(t, n_head: int, head_dim: int) -> Rows:
         nb_tok, nb_dim = t.stride(0) * es, t.stride(1) * es
         nb_head = head_dim * nb_dim
     return Rows(t.data_ptr(), ty, n_head, head_dim, 0, nb_dim, nb_head, nb_tok)
+
+
+class Transform(C.Structure):
+    """kvm_transform: stage-in RoPE / Walsh-Hadamard settings (0 = off)."""
+    _fields_ = [("rot_k", C.c_uint32), ("rot_v", C.c_uint32), ("rope_n_rot", C.c_uint32),
+                ("reserved0", C.c_uint32), ("rope_freq_base", C.c_float),
+                ("rope_freq_scale", C.c_float)]
+
+
+def attn_rot_nrot(type_: int, head_dim: int, is_k: bool) -> int:
+    return int(lib().kvm_attn_rot_nrot(type_, head_dim, 1 if is_k else 0))
 
 
 class Window(C.Structure):
@@ -175,6 +187,8 @@ def lib():
             "kvm_meank_zero": (C.c_int, [vp, vp, u32, u32]),
             "kvm_query_reset": (C.c_int, [vp, vp]),
             "kvm_query_add": (C.c_int, [vp, vp, u32, u32, C.POINTER(Rows), vp]),
+            "kvm_set_transform": (C.c_int, [vp, C.POINTER(Transform)]),
+            "kvm_attn_rot_nrot": (u32, [i32, u32, C.c_int]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -311,6 +325,15 @@ class Session:
         qc = np.ascontiguousarray(np.asarray(q_count, dtype=np.uint32))
         self._check(lib().kvm_set_query(self.h, _stream(stream), _ptr(q_sum), qc.ctypes.data),
                     "set_query")
+
+    def set_transform(self, rot_k=0, rot_v=0, rope_n_rot=0, rope_freq_base=10000.0,
+                      rope_freq_scale=1.0):
+        """Stage-in transforms for later steps; all zero switches them off."""
+        t = Transform(rot_k, rot_v, rope_n_rot, 0, rope_freq_base, rope_freq_scale)
+        self._check(lib().kvm_set_transform(self.h, C.byref(t)), "set_transform")
+
+    def clear_transform(self):
+        self._check(lib().kvm_set_transform(self.h, None), "set_transform")
 
     # ---- device producers (harvest of K summaries and the query)
     def write_mean_k(self, layer, pos0, n, rows: Rows, stream=None):

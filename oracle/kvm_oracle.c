@@ -301,6 +301,83 @@ int ora_quantize_rows_f16(int type, const uint16_t *src, int64_t n_rows,
     return 0;
 }
 
+/* ------------------------------------------------------------ transforms --
+ * RoPE: kvmem/src/host/rope.cpp:8-45 (theta table, then per token and head
+ * x0*c - x1*s, x0*s + x1*c with c = cos(pos*theta_i), s = sin(pos*theta_i)).
+ * Hadamard: fwht_kernel, src/adapter/llama-kvmem-stagein.cu:104-130.
+ * attn_rot sizes: src/adapter/llama-kvmem-quant.h:22-40.
+ */
+void ora_rope_theta(uint32_t n_rot, float freq_base, float freq_scale, float *theta)
+{
+    for (uint32_t i = 0; i < n_rot / 2u; ++i) {
+        theta[i] = powf(freq_base, -2.0f * (float)i / (float)n_rot);
+        theta[i] *= freq_scale;
+    }
+}
+
+void ora_rope_neox_rows(float *x, int64_t n_tokens, uint32_t n_head, uint32_t head_dim,
+                        uint32_t n_rot, int32_t pos0, const float *theta)
+{
+    const uint32_t half = n_rot / 2u;
+    for (int64_t t = 0; t < n_tokens; ++t) {
+        const float pos = (float)(pos0 + (int32_t)t);
+        for (uint32_t h = 0; h < n_head; ++h) {
+            float *row = x + ((uint64_t)t * n_head + h) * head_dim;
+            for (uint32_t i = 0; i < half; ++i) {
+                const float c = cosf(pos * theta[i]);
+                const float s = sinf(pos * theta[i]);
+                const float x0 = row[i];
+                const float x1 = row[i + half];
+                row[i] = x0 * c - x1 * s;
+                row[i + half] = x0 * s + x1 * c;
+            }
+        }
+    }
+}
+
+void ora_fwht_rows(float *x, int64_t n_rows, uint32_t n_embd, uint32_t nrot)
+{
+    if (nrot == 0 || n_embd % nrot != 0) {
+        return;
+    }
+    const float scale = 1.0f / sqrtf((float)nrot);
+    const int64_t chunks = n_rows * (int64_t)(n_embd / nrot);
+    for (int64_t c = 0; c < chunks; ++c) {
+        float *v = x + c * (int64_t)nrot;
+        for (uint32_t i = 0; i < nrot; ++i) {
+            v[i] = v[i] * scale;
+        }
+        for (uint32_t h = 1; h < nrot; h *= 2) {
+            for (uint32_t i = 0; i < nrot; i += 2 * h) {
+                for (uint32_t j = 0; j < h; ++j) {
+                    const float a = v[i + j];
+                    const float b = v[i + j + h];
+                    v[i + j] = a + b;
+                    v[i + j + h] = a - b;
+                }
+            }
+        }
+    }
+}
+
+uint32_t ora_attn_rot_nrot(int type, uint32_t head_dim, int is_k)
+{
+    if (type != ORA_TYPE_Q8_0 && type != ORA_TYPE_Q4_0 && type != ORA_TYPE_Q5_0) {
+        return 0;
+    }
+    if (head_dim < 64 || head_dim % 64 != 0) {
+        return 0;
+    }
+    if (!is_k) {
+        return 64;
+    }
+    uint32_t nrot = 64;
+    do {
+        nrot *= 2;
+    } while (head_dim % nrot == 0);
+    return nrot / 2;
+}
+
 /* ---------------------------------------------------------------- mean-K --
  * kvmem/src/host/raw_kv_store.cpp:204-223 (add_mean_f32: zero-filled F32
  * accumulator, tokens added in order) and :976-1000 (mean_k: sum * (1.0f/n),

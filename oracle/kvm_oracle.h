@@ -56,6 +56,26 @@ void ora_quantize_q5_0(const float *x, int64_t n, uint8_t *y);
 int ora_quantize_rows_f16(int type, const uint16_t *src, int64_t n_rows,
                           uint32_t n_embd, uint8_t *dst, int n_threads);
 
+/*
+ * Stage-in transforms (the reference's quantizing stage-in,
+ * src/adapter/llama-kvmem-stagein.cu:632-753).
+ *   ora_rope_theta: theta_i = powf(base, -2i/n_rot) * scale, i < n_rot/2
+ *                   (kvmem/src/host/rope.cpp:18-22).
+ *   ora_rope_neox_rows: NeoX RoPE of rows [n_tokens][n_head][head_dim] at
+ *                   positions pos0 + t (rope.cpp:26-43, rope_neox_kernel
+ *                   stagein.cu:160-178); cosf / sinf, no FMA contraction.
+ *   ora_fwht_rows:  Walsh-Hadamard of every nrot chunk of n_rows rows of
+ *                   n_embd floats, fwht_kernel order (stagein.cu:104-130):
+ *                   scale by 1.0f/sqrtf(nrot) first, butterflies h = 1, 2, ...
+ *   ora_attn_rot_nrot: kvmem_attn_rot_on + kvmem_hadamard_nrot_k/_v
+ *                   (src/adapter/llama-kvmem-quant.h:22-40).
+ */
+void ora_rope_theta(uint32_t n_rot, float freq_base, float freq_scale, float *theta);
+void ora_rope_neox_rows(float *x, int64_t n_tokens, uint32_t n_head, uint32_t head_dim,
+                        uint32_t n_rot, int32_t pos0, const float *theta);
+void ora_fwht_rows(float *x, int64_t n_rows, uint32_t n_embd, uint32_t nrot);
+uint32_t ora_attn_rot_nrot(int type, uint32_t head_dim, int is_k);
+
 /* Ordered F32 sum over tokens of F16 K rows (RawKvStore::add_mean_f32). */
 void ora_block_sum_f16(const uint16_t *k, uint32_t n_tokens, uint32_t n_embd,
                        uint64_t row_stride, float *sum);

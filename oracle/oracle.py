@@ -133,6 +133,15 @@ def lib():
         L.ora_set_selection.restype = C.c_int
         L.ora_set_selection.argtypes = [C.POINTER(OraCfg), C.POINTER(_OraBlocks), C.c_uint32,
                                         _u32p, C.c_uint32, C.c_int, C.POINTER(_OraPlan)]
+        L.ora_rope_theta.restype = None
+        L.ora_rope_theta.argtypes = [C.c_uint32, C.c_float, C.c_float, _f32p]
+        L.ora_rope_neox_rows.restype = None
+        L.ora_rope_neox_rows.argtypes = [_f32p, C.c_int64, C.c_uint32, C.c_uint32, C.c_uint32,
+                                         C.c_int32, _f32p]
+        L.ora_fwht_rows.restype = None
+        L.ora_fwht_rows.argtypes = [_f32p, C.c_int64, C.c_uint32, C.c_uint32]
+        L.ora_attn_rot_nrot.restype = C.c_uint32
+        L.ora_attn_rot_nrot.argtypes = [C.c_int, C.c_uint32, C.c_int]
         L.ora_layout.restype = C.c_int
         L.ora_layout.argtypes = [_u32p, C.c_uint32, _i32p, C.c_uint32, _i32p, _u32p, _i32p,
                                  _i32p, C.POINTER(C.c_uint32), _u32p, _i32p, C.POINTER(C.c_uint32)]
@@ -172,6 +181,9 @@ def ref():
         R.ref_raw_write_mean_k.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
         R.ref_raw_mean_k.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]
         R.ref_raw_write_mean_sum.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
+        R.ref_rope_neox.restype = None
+        R.ref_rope_neox.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float, _f32p,
+                                    C.c_uint32, C.c_int32, _f32p]
         R.ref_raw_has_block.restype = C.c_int
         R.ref_raw_has_block.argtypes = [C.c_void_p, C.c_uint32]
         _ref = R
@@ -203,6 +215,50 @@ def quantize_rows_f16(type_: int, rows: np.ndarray, n_threads: int = 1) -> np.nd
     if rc != 0:
         raise ValueError("unsupported type or width")
     return out
+
+
+def rope_theta(n_rot: int, freq_base: float, freq_scale: float = 1.0) -> np.ndarray:
+    th = np.zeros(max(1, n_rot // 2), np.float32)
+    lib().ora_rope_theta(n_rot, freq_base, freq_scale, th)
+    return th[:n_rot // 2]
+
+
+def rope_neox_rows(x: np.ndarray, n_head: int, head_dim: int, n_rot: int, pos0: int,
+                   theta: np.ndarray) -> np.ndarray:
+    """NeoX RoPE of F32 rows [n, n_head*head_dim] at positions pos0 + t."""
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    th = np.ascontiguousarray(theta, dtype=np.float32)
+    lib().ora_rope_neox_rows(y, y.shape[0], n_head, head_dim, n_rot, pos0, th)
+    return y
+
+
+def fwht_rows(x: np.ndarray, nrot: int) -> np.ndarray:
+    """Walsh-Hadamard (fwht_kernel order) of every nrot chunk of F32 rows."""
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    lib().ora_fwht_rows(y, y.shape[0], y.shape[1], nrot)
+    return y
+
+
+def attn_rot_nrot(type_: int, head_dim: int, is_k: bool) -> int:
+    return int(lib().ora_attn_rot_nrot(type_, head_dim, 1 if is_k else 0))
+
+
+def transform_quantize_rows(type_: int, rows_f16: np.ndarray, n_head: int, head_dim: int,
+                            nrot: int = 0, n_rope: int = 0, pos0: int = 0,
+                            theta: np.ndarray | None = None, pre_quant: bool = False):
+    """The quantizing stage-in with transforms: F16 rows -> RoPE(pos0 + t) ->
+    Hadamard -> quantized row bytes [n, row_bytes] (and the F32 values before
+    the quantizer when pre_quant)."""
+    x = np.asarray(rows_f16, dtype=np.float16).astype(np.float32)
+    if n_rope:
+        x = rope_neox_rows(x, n_head, head_dim, n_rope, pos0, theta)
+    if nrot:
+        x = fwht_rows(x, nrot)
+    if type_ == TYPE_F16:
+        out = x.astype(np.float16).view(np.uint8).reshape(x.shape[0], -1)
+    else:
+        out = np.stack([quantize(type_, r) for r in x])
+    return (out, x) if pre_quant else out
 
 
 def block_sum_f16(k: np.ndarray) -> np.ndarray:
@@ -512,6 +568,15 @@ class RefRaw:
 
     def has_block(self, block_id):
         return bool(ref().ref_raw_has_block(self.h, block_id))
+
+
+def ref_rope_neox(k: np.ndarray, n_head: int, head_dim: int, n_rot: int, pos0: int,
+                  freq_base: float, freq_scale: float = 1.0) -> np.ndarray:
+    """The reference's own kvmem::rope_neox_apply on F32 rows [n, n_head*head_dim]."""
+    x = np.ascontiguousarray(k, dtype=np.float32)
+    out = np.zeros_like(x)
+    ref().ref_rope_neox(n_rot, head_dim, n_head, freq_base, freq_scale, x, x.shape[0], pos0, out)
+    return out
 
 
 # -------------------------------------------------------- synthetic inputs --

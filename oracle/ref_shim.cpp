@@ -7,6 +7,7 @@
 // in the product links this.
 #include "kvmem/kvmem_store.hpp"
 #include "kvmem/raw_kv_store.hpp"
+#include "kvmem/rope.hpp"
 
 #include <cstdint>
 #include <cstring>
@@ -150,6 +151,17 @@ void ref_raw_write_mean_sum(void *r, uint32_t pos0, uint32_t n, uint32_t il, con
 
 void ref_raw_mean_k(void *r, uint32_t block_id, uint32_t il, float *out) {
     static_cast<kvmem::RawKvStore *>(r)->mean_k(block_id, il, out);
+}
+
+void ref_rope_neox(uint32_t n_rot, uint32_t head_dim, uint32_t n_head, float freq_base, float freq_scale,
+                   const float *k, uint32_t n_tokens, int32_t pos0, float *out) {
+    kvmem::RopeConfig cfg;
+    cfg.n_rot = n_rot;
+    cfg.n_embd_head = head_dim;
+    cfg.n_head_kv = n_head;
+    cfg.freq_base = freq_base;
+    cfg.freq_scale = freq_scale;
+    kvmem::rope_neox_apply(cfg, k, n_tokens, pos0, out);
 }
 
 int ref_raw_has_block(void *r, uint32_t block_id) {

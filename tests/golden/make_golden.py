@@ -15,6 +15,9 @@ Outputs (all small, committed):
                      harvest), then decode sums flushed with write_layer_mean_sum
                      from mid-block and block-start positions; the means after it
 
+  rope_golden.npz    F32 rows rotated by the reference's own kvmem::rope_neox_apply
+                     (full and partial rotary dims, small and 256K-range positions)
+
 `python tests/golden/make_golden.py meank_seq` regenerates only the named fixtures.
 """
 import json
@@ -172,6 +175,23 @@ def make_meank_seq(rng):
     np.savez_compressed(os.path.join(HERE, "meank_seq_golden.npz"), **arrays)
 
 
+ROPE_CASES = (   # n_head, head_dim, n_rot, pos0, freq_base, freq_scale
+    (2, 128, 128, 0, 1e6, 1.0),
+    (4, 256, 256, 131000, 1e6, 1.0),
+    (2, 128, 64, 262100, 1e4, 0.25),
+)
+
+
+def make_rope(rng):
+    arrays = {}
+    for i, (H, D, n_rot, pos0, base, scale) in enumerate(ROPE_CASES):
+        x = rng.standard_normal((4, H * D)).astype(np.float32) * 3
+        arrays[f"x{i}"] = x
+        arrays[f"out{i}"] = O.ref_rope_neox(x, H, D, n_rot, pos0, base, scale)
+        arrays[f"case{i}"] = np.array([H, D, n_rot, pos0, base, scale], np.float64)
+    np.savez_compressed(os.path.join(HERE, "rope_golden.npz"), n_cases=len(ROPE_CASES), **arrays)
+
+
 if __name__ == "__main__":
     O.build(ref=True)
     if not O.have_ref():
@@ -184,4 +204,6 @@ if __name__ == "__main__":
         make_meank(rng)
     if not only or "meank_seq" in only:
         make_meank_seq(np.random.default_rng(20261202))
+    if not only or "rope" in only:
+        make_rope(np.random.default_rng(20261203))
     print("golden fixtures written to", HERE)

@@ -156,6 +156,58 @@ def test_add_rows_is_the_ordered_f32_sum(oracle):
     assert oracle.add_rows(np.array([-0.0], np.float32), np.array([[-0.0]], np.float32))[0] == 0.0
 
 
+# ------------------------------------------------- stage-in transforms ---
+
+def test_rope_oracle_matches_reference_golden(oracle):
+    """The oracle's NeoX RoPE against kvmem::rope_neox_apply outputs (fixture
+    made by the compiled reference), bit for bit."""
+    g = np.load(os.path.join(GOLD, "rope_golden.npz"))
+    for i in range(int(g["n_cases"])):
+        H, D, n_rot, pos0, base, scale = g[f"case{i}"]
+        H, D, n_rot, pos0 = int(H), int(D), int(n_rot), int(pos0)
+        th = oracle.rope_theta(n_rot, float(np.float32(base)), float(np.float32(scale)))
+        got = oracle.rope_neox_rows(g[f"x{i}"], H, D, n_rot, pos0, th)
+        assert got.tobytes() == g[f"out{i}"].tobytes(), i
+
+
+def test_fwht_oracle_exact_cases_and_inverse(oracle):
+    n = 64
+    e0 = np.zeros((1, n), np.float32)
+    e0[0, 0] = 1.0
+    assert np.all(oracle.fwht_rows(e0, n) == np.float32(0.125))     # first column of H/8
+    ones = np.ones((1, 2 * n), np.float32)
+    y = oracle.fwht_rows(ones, n)                                   # two chunks of 64
+    assert y[0, 0] == 8.0 and y[0, n] == 8.0 and not np.any(np.delete(y[0], [0, n]))
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((5, 512)).astype(np.float32)
+    for nrot in (64, 128, 256, 512):
+        z = oracle.fwht_rows(oracle.fwht_rows(x, nrot), nrot)       # H is orthonormal, H^2 = I
+        assert np.allclose(z, x, atol=1e-5)
+        assert np.allclose(np.linalg.norm(oracle.fwht_rows(x, nrot), axis=1),
+                           np.linalg.norm(x, axis=1), rtol=1e-5)
+
+
+def test_attn_rot_sizes_follow_the_reference_rule(oracle):
+    # kvmem_hadamard_nrot_k: the largest power of two >= 64 dividing head_dim;
+    # V always 64; only quantized caches with head_dim % 64 == 0 rotate
+    want_k = {64: 64, 128: 128, 192: 64, 256: 256, 320: 64, 384: 128, 512: 512}
+    for d, n in want_k.items():
+        assert oracle.attn_rot_nrot(oracle.TYPE_Q8_0, d, True) == n
+        assert oracle.attn_rot_nrot(oracle.TYPE_Q4_0, d, False) == 64
+    assert oracle.attn_rot_nrot(oracle.TYPE_F16, 256, True) == 0
+    assert oracle.attn_rot_nrot(oracle.TYPE_Q8_0, 96, True) == 0
+
+
+def test_attn_rot_rule_of_the_library_matches_oracle(oracle):
+    import kvm
+    kvm.build()
+    L = kvm.lib()
+    for ty in (oracle.TYPE_F16, oracle.TYPE_Q8_0, oracle.TYPE_Q4_0, oracle.TYPE_Q5_0):
+        for d in (32, 64, 96, 128, 192, 256, 320, 384, 512, 1024):
+            for k in (0, 1):
+                assert L.kvm_attn_rot_nrot(ty, d, k) == oracle.attn_rot_nrot(ty, d, bool(k))
+
+
 # ------------------------------------------------------ selection + diff ---
 
 def _cfg_from(oracle, c):
