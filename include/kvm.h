@@ -315,7 +315,7 @@ kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum,
  * switch a transform off.  rot_k / rot_v must be 64, 128, 256 or 512 and
  * divide head_dim; rope_n_rot a multiple of 64 up to head_dim.  The window
  * types must be quantized (Q8_0 / Q4_0 / Q5_0) for a Hadamard transform, as
- * kvmem_attn_rot_on requires; head_dim must be 64, 128, 256 or 512.
+ * kvmem_attn_rot_on requires; head_dim must be a multiple of 32.
  */
 typedef struct kvm_transform {
     uint32_t rot_k;

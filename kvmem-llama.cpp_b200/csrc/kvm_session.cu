@@ -888,8 +888,8 @@ kvm_status kvm_set_transform(kvm_session *s, const kvm_transform *t) {
     if (t->rope_n_rot % 64u != 0u || t->rope_n_rot > D)
         return fail(s, KVM_EINVAL, "rope_n_rot must be a multiple of 64 up to head_dim");
     const bool on = t->rot_k || t->rot_v || t->rope_n_rot;
-    if (on && !(D == 64u || D == 128u || D == 192u || D == 256u || D == 384u || D == 512u))
-        return fail(s, KVM_EINVAL, "transforms need head_dim 64, 128, 192, 256, 384 or 512");
+    if (on && (D % 32u != 0u || D > 1024u))
+        return fail(s, KVM_EINVAL, "transforms need head_dim a multiple of 32, at most 1024");
     auto quantized = [](int32_t ty) {
         return ty == KVM_TYPE_Q8_0 || ty == KVM_TYPE_Q4_0 || ty == KVM_TYPE_Q5_0;
     };

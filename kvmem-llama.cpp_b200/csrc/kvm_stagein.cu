@@ -110,124 +110,168 @@ constexpr uint32_t kStageinHeader = 384;
 
 // ------------------------------------------------------- transform mode --
 //
-// One warp per (row, head) of NREG*32 values; value i of the head lives in
-// lane i % 32, register i / 32.  Every float operation is a round-to-nearest
-// intrinsic, so the Hadamard and quantizer steps match the CPU bit for bit;
-// RoPE calls the CUDA sincosf (the reference's GPU kernel does the same) and
-// agrees with the host cosf / sinf to within their last-bit errors.
+// A lane owns one ggml block -- 32 consecutive values of one head of one row
+// -- and the head_dim/32 lanes of a (row, head) work together: butterflies of
+// span < 32 stay in the lane's registers, larger spans pair lanes (xor of the
+// lane index), and each lane quantizes its own block in the reference's
+// sequential order.  Every float operation is a round-to-nearest intrinsic,
+// so the Hadamard and the quantizers match the CPU bit for bit; RoPE calls the
+// CUDA sincosf (as the reference's GPU kernel does) and agrees with the host
+// cosf / sinf to within their last-bit errors.
 
-// A ggml block spread over the warp (value j in lane j) into its bytes.
-__device__ __forceinline__ void quant_warp(int type, float x, uint8_t *blk, int lane) {
-    const unsigned full = 0xffffffffu;
+// One 32-value block from F32 values, the reference's loops in their order
+// (quant_q8_0 / quant_q4_0, llama-kvmem-stagein.cu:180-233; q5_0 as ggml).
+__device__ __forceinline__ void quant_f32_block(int type, const float (&v)[32], uint8_t *blk) {
     if (type == KVM_TYPE_F16) {
-        st_u16(blk + 2 * lane, f16_bits(x));
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            *reinterpret_cast<uint32_t *>(blk + 2 * j) = f16_bits(v[j]) | (f16_bits(v[j + 1]) << 16);
+        }
         return;
     }
-    float amax = fabsf(x);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(full, amax, o));
     if (type == KVM_TYPE_Q8_0) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        if (lane == 0) st_u16(blk, f16_bits(d));
-        blk[2 + lane] = static_cast<uint8_t>(round_half_away(__fmul_rn(x, id)) & 0xff);
+        st_u16(blk, f16_bits(d));
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const uint32_t q0 = static_cast<uint32_t>(round_half_away(__fmul_rn(v[j], id))) & 0xffu;
+            const uint32_t q1 = static_cast<uint32_t>(round_half_away(__fmul_rn(v[j + 1], id))) & 0xffu;
+            st_u16(blk + 2 + j, q0 | (q1 << 8));
+        }
         return;
     }
     const bool q5 = type == KVM_TYPE_Q5_0;
-    // the reference's strict `amax < |v|` scan keeps the first value of
-    // largest magnitude, and +0.0 when every value is zero
-    const unsigned hit = __ballot_sync(full, fabsf(x) == amax);
-    float vmax = __shfl_sync(full, x, __ffs(hit) - 1);
-    if (amax == 0.0f) vmax = 0.0f;
-    const float d = __fdiv_rn(vmax, q5 ? -16.0f : -8.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const uint32_t code = code_q(x, id, q5 ? 16.5f : 8.5f, q5 ? 31 : 15);
-    const uint32_t partner = __shfl_down_sync(full, code, 16);
-    const unsigned qh = __ballot_sync(full, (code >> 4) & 1u);
-    if (lane == 0) {
-        st_u16(blk, f16_bits(d));
-        if (q5) {
-            st_u16(blk + 2, qh & 0xffffu);
-            st_u16(blk + 4, qh >> 16);
+    float amax = 0.0f, vmax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float m = fabsf(v[j]);
+        if (amax < m) {
+            amax = m;
+            vmax = v[j];
         }
     }
-    if (lane < 16) blk[(q5 ? 6 : 2) + lane] = static_cast<uint8_t>((code & 15u) | ((partner & 15u) << 4));
+    const float d = __fdiv_rn(vmax, q5 ? -16.0f : -8.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float off = q5 ? 16.5f : 8.5f;
+    const int maxq = q5 ? 31 : 15;
+    st_u16(blk, f16_bits(d));
+    uint32_t qh = 0;
+    uint8_t *qs = blk + (q5 ? 6 : 2);
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        const uint32_t a0 = code_q(v[j], id, off, maxq), b0 = code_q(v[j + 16], id, off, maxq);
+        const uint32_t a1 = code_q(v[j + 1], id, off, maxq), b1 = code_q(v[j + 17], id, off, maxq);
+        qh |= ((a0 >> 4) << j) | ((a1 >> 4) << (j + 1)) | ((b0 >> 4) << (j + 16)) | ((b1 >> 4) << (j + 17));
+        st_u16(qs + j, ((a0 & 15u) | ((b0 & 15u) << 4)) | (((a1 & 15u) | ((b1 & 15u) << 4)) << 8));
+    }
+    if (q5) {
+        st_u16(blk + 2, qh & 0xffffu);
+        st_u16(blk + 4, qh >> 16);
+    }
 }
 
-template <int NREG>
+// 32 consecutive F16 values of a tile row, widened.
+__device__ __forceinline__ void load32(const __half *p, float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 r = *reinterpret_cast<const uint4 *>(p + 8 * c);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&r);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const float2 f = __half22float2(h[m]);
+            v[8 * c + 2 * m] = f.x;
+            v[8 * c + 2 * m + 1] = f.y;
+        }
+    }
+}
+
 __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
                                                uint8_t *ob, int warp, int lane) {
-    constexpr uint32_t D = NREG * 32u;
     const bool is_v = (ts.meta >> 31) != 0u;
     const uint32_t pos0 = ts.meta & 0x7fffffffu;
     const uint32_t nrot = is_v ? a.rot_v : a.rot_k;
     const uint32_t n_rope = is_v ? 0u : a.rope_n_rot;
     const uint32_t half = n_rope / 2u;
+    const uint32_t G = a.xform;                    // lanes per (row, head) = head_dim / 32
+    const uint32_t D = G * 32u;
+    const uint32_t per_warp = 32u / G;
     const uint32_t H = a.n_embd / D;
     const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
     const uint32_t bb = static_cast<uint32_t>(block_bytes(ts.type));
     const float scale = nrot ? __fdiv_rn(1.0f, __fsqrt_rn(__uint2float_rn(nrot))) : 1.0f;
+    const uint32_t sub = static_cast<uint32_t>(lane) / G;
+    const uint32_t j = static_cast<uint32_t>(lane) - sub * G;
     const uint32_t units = ts.rows * H;
-    for (uint32_t u = static_cast<uint32_t>(warp); u < units; u += kStageinConsumerWarps) {
-        const uint32_t row = u / H;
-        const uint32_t h = u - row * H;
-        const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
-        const float pos = __uint2float_rn(pos0 + row);
-        float v[NREG];
-#pragma unroll
-        for (int r = 0; r < NREG; ++r) {
-            const uint32_t i = static_cast<uint32_t>(r) * 32u + static_cast<uint32_t>(lane);
-            float y = __half2float(x[i]);
-            if (i < n_rope) {
+    for (uint32_t u0 = static_cast<uint32_t>(warp) * per_warp; u0 < units;
+         u0 += kStageinConsumerWarps * per_warp) {
+        const uint32_t u = u0 + sub;
+        const bool valid = sub < per_warp && u < units;
+        const uint32_t row = valid ? u / H : 0u;
+        const uint32_t h = valid ? u - row * H : 0u;
+        float v[32];
+        if (valid) {
+            const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
+            load32(x + 32u * j, v);
+            const uint32_t i0 = 32u * j;
+            if (i0 < n_rope) {
                 // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i]
-                const bool lo = i < half;
-                const uint32_t f = lo ? i : i - half;
-                const float other = __half2float(x[lo ? i + half : i - half]);
-                float sn, cs;
-                sincosf(__fmul_rn(pos, a.theta[f]), &sn, &cs);
-                y = lo ? __fsub_rn(__fmul_rn(y, cs), __fmul_rn(other, sn))
-                       : __fadd_rn(__fmul_rn(other, sn), __fmul_rn(y, cs));
+                const bool lo = i0 < half;
+                float w[32];
+                load32(x + (lo ? i0 + half : i0 - half), w);
+                const float pos = __uint2float_rn(pos0 + row);
+                const float *th = a.theta + (lo ? i0 : i0 - half);
+#pragma unroll
+                for (int m = 0; m < 32; ++m) {
+                    float sn, cs;
+                    sincosf(__fmul_rn(pos, th[m]), &sn, &cs);
+                    v[m] = lo ? __fsub_rn(__fmul_rn(v[m], cs), __fmul_rn(w[m], sn))
+                              : __fadd_rn(__fmul_rn(w[m], sn), __fmul_rn(v[m], cs));
+                }
             }
-            v[r] = y;
+        } else {
+#pragma unroll
+            for (int m = 0; m < 32; ++m) v[m] = 0.0f;
         }
         if (nrot) {
 #pragma unroll
-            for (int r = 0; r < NREG; ++r) v[r] = __fmul_rn(v[r], scale);
-            // butterflies of span 1 .. 16: across lanes
+            for (int m = 0; m < 32; ++m) v[m] = __fmul_rn(v[m], scale);
+            // spans 1 .. 16 inside the lane (fwht_kernel's h loop, ascending)
 #pragma unroll
             for (int hh = 1; hh < 32; hh <<= 1) {
-                const bool upper = (lane & hh) != 0;
 #pragma unroll
-                for (int r = 0; r < NREG; ++r) {
-                    const float p = __shfl_xor_sync(0xffffffffu, v[r], hh);
-                    v[r] = upper ? __fsub_rn(p, v[r]) : __fadd_rn(v[r], p);
-                }
-            }
-            // spans 32 .. nrot/2: across registers of the same lane
-#pragma unroll
-            for (int hr = 1; hr < NREG; hr <<= 1) {
-                if (32u * static_cast<uint32_t>(hr) < nrot) {
-#pragma unroll
-                    for (int r = 0; r < NREG; ++r) {
-                        if ((r & hr) == 0 && (r | hr) < NREG) {
-                            const float p = v[r];
-                            const float q = v[r | hr];
-                            v[r] = __fadd_rn(p, q);
-                            v[r | hr] = __fsub_rn(p, q);
-                        }
+                for (int m = 0; m < 32; ++m) {
+                    if ((m & hh) == 0) {
+                        const float p = v[m];
+                        const float q = v[m | hh];
+                        v[m] = __fadd_rn(p, q);
+                        v[m | hh] = __fsub_rn(p, q);
                     }
                 }
             }
-        }
-        uint8_t *orow = ob + static_cast<size_t>(row) * rb;
+            // spans 32 .. nrot/2: lane j pairs with lane j ^ (span / 32)
+            for (uint32_t dl = 1; 32u * dl < nrot; dl <<= 1) {
+                const bool upper = (j & dl) != 0u;
 #pragma unroll
-        for (int r = 0; r < NREG; ++r)
-            quant_warp(ts.type, v[r], orow + static_cast<size_t>(h * NREG + r) * bb, lane);
+                for (int m = 0; m < 32; ++m) {
+                    const float p = __shfl_xor_sync(0xffffffffu, v[m], static_cast<int>(dl));
+                    v[m] = upper ? __fsub_rn(p, v[m]) : __fadd_rn(v[m], p);
+                }
+            }
+        }
+        if (valid)
+            quant_f32_block(ts.type, v, ob + static_cast<size_t>(row) * rb + static_cast<size_t>(h * G + j) * bb);
     }
 }
 
-template <int NS, int NREG>
-__global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs a) {
+// Resident CTAs per SM: three for the plain kernel (its shared memory allows
+// three; at most 75 registers a thread), two for the transform variant (16
+// consumer warps to hide its ALU latencies).
+template <int NS, bool XF>
+__global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(StageinArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
@@ -348,10 +392,10 @@ __global__ void __launch_bounds__(kStageinThreads, 1) stagein_kernel(StageinArgs
         if (ts.rows == 0) break;
         const uint8_t *ib = in_buf + s * a.tile_in_bytes;
         uint8_t *ob = out_buf + s * a.tile_out_bytes;
-        if (NREG > 0) {
+        if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
-                transform_tile<(NREG > 0 ? NREG : 1)>(a, ts, ib, ob, warp, lane);
+                transform_tile(a, ts, ib, ob, warp, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done[s]);
@@ -510,37 +554,33 @@ static bool attr_once(std::atomic<uint64_t> &done, const void *fn, int bytes) {
 static std::atomic<uint64_t> g_stagein_attr{0};
 static std::atomic<uint64_t> g_permute_attr{0};
 
-template <int NREG>
+template <bool XF>
 static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap,
                                     std::atomic<uint64_t> &attr) {
     const size_t smem = stagein_smem_bytes(a);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    const void *fn = reinterpret_cast<const void *>(stagein_kernel<kStageinStages, NREG>);
+    const void *fn = reinterpret_cast<const void *>(stagein_kernel<kStageinStages, XF>);
     if (!attr_once(attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages, NREG>,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages, XF>,
                                                   kStageinThreads, smem);
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    stagein_kernel<kStageinStages, NREG><<<grid, kStageinThreads, smem, stream>>>(a);
+    stagein_kernel<kStageinStages, XF><<<grid, kStageinThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
-static std::atomic<uint64_t> g_xform_attr[6];
+static std::atomic<uint64_t> g_xform_attr{0};
 
 cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
-    switch (a.xform) {
-        case 0: return launch_stagein_t<0>(a, stream, grid_cap, g_stagein_attr);
-        case 2: return launch_stagein_t<2>(a, stream, grid_cap, g_xform_attr[0]);
-        case 4: return launch_stagein_t<4>(a, stream, grid_cap, g_xform_attr[1]);
-        case 6: return launch_stagein_t<6>(a, stream, grid_cap, g_xform_attr[2]);
-        case 8: return launch_stagein_t<8>(a, stream, grid_cap, g_xform_attr[3]);
-        case 12: return launch_stagein_t<12>(a, stream, grid_cap, g_xform_attr[4]);
-        case 16: return launch_stagein_t<16>(a, stream, grid_cap, g_xform_attr[5]);
-        default: return cudaErrorInvalidValue;
-    }
+    if (a.xform == 0) return launch_stagein_t<false>(a, stream, grid_cap, g_stagein_attr);
+    // lanes of a (row, head) must tile the warp's xor pairs: head_dim / 32 in
+    // 1 .. 32 and, for every Hadamard size, a multiple of size / 32
+    if (a.xform > 32u || (a.rot_k && a.xform % (a.rot_k / 32u)) || (a.rot_v && a.xform % (a.rot_v / 32u)))
+        return cudaErrorInvalidValue;
+    return launch_stagein_t<true>(a, stream, grid_cap, g_xform_attr);
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
