@@ -375,6 +375,26 @@ kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh);
  * the cold blocks with the quantize kernel through the HBM staging ring. */
 kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
                        const kvm_window *win);
+/*
+ * Stage-out (harvest) of resident blocks: the packed window rows of blocks
+ * ids[0..n) -- harvest_gpu_v with kvmem_stageout_enqueue / _submit,
+ * src/adapter/llama-memory-kvmem.cpp:2318-2410, llama-kvmem-stagein.cu:842-963.
+ * Block ids[j] lands at dst + j * kvm_stageout_item_bytes(s): for every layer
+ * l, at + l * block_tokens * (row_bytes_k + row_bytes_v), its n_tokens K rows
+ * then (at + block_tokens * row_bytes_k) its V rows; bytes past a partial
+ * block's rows are unspecified.  Window slots come from the device block
+ * table, so the call needs no plan read-back.  dst is device memory (one
+ * gather kernel) or host memory (pinned for asynchrony: chunks are packed in
+ * the HBM staging ring and copied out on a second stream while the next chunk
+ * is packed).  resident (host, optional) receives per block 1 when it had a
+ * window slot and was copied, 0 when not (its bytes unspecified).  Everything
+ * is stream-ordered on `stream`: dst and resident are complete once it is.
+ */
+kvm_status kvm_stageout(kvm_session *s, kvm_stream stream, const uint32_t *ids, uint32_t n,
+                        const kvm_window *win, void *dst, uint8_t *resident);
+/* Bytes one block occupies in a kvm_stageout destination. */
+uint64_t kvm_stageout_item_bytes(const kvm_session *s);
+
 /* score -> select -> diff -> stage-in in one call. */
 kvm_status kvm_step(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,
                     uint32_t n_mandatory, const kvm_source *src, const kvm_window *win);

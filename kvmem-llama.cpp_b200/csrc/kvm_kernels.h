@@ -69,6 +69,30 @@ uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens);
 size_t stagein_smem_bytes(const StageinArgs &a);
 cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap);
 
+// ------------------------------------------------------------ stage-out --
+struct StageoutArgs {
+    const uint32_t *ids;           // device block ids of this launch's items
+    uint32_t n;                    // items in this launch
+    uint32_t item0;                // index of ids[0] in the caller's list (resident flags)
+    const int32_t *gpu_slot;       // block table
+    const uint32_t *n_tokens;
+    uint32_t n_blocks;
+    uint32_t n_slots;
+    uint32_t n_layer;
+    uint32_t block_tokens;
+    uint8_t *const *win_k;         // device arrays [n_layer]
+    uint8_t *const *win_v;
+    uint32_t row_bytes_k;
+    uint32_t row_bytes_v;
+    uint8_t *dst;                  // item j at dst + j * item_bytes
+    uint64_t item_bytes;
+    uint8_t *resident;             // optional device flags, [item0 + j]
+    uint32_t bulk;                 // 1: every address and size 16-byte aligned
+    uint32_t *status;
+};
+
+cudaError_t launch_stageout(const StageoutArgs &a, cudaStream_t stream);
+
 // -------------------------------------------------------------- permute --
 struct PermuteArgs {
     const uint32_t *n_moves_dev;

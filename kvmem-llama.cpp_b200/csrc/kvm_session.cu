@@ -102,6 +102,10 @@ struct kvm_session {
     static constexpr int kRingSlots = 4;
     cudaEvent_t ring_copied[kRingSlots] = {};
     cudaEvent_t ring_free[kRingSlots] = {};
+    cudaEvent_t out_gathered[kRingSlots] = {};   // stage-out: slot packed (on the caller's stream)
+    cudaEvent_t out_done[kRingSlots] = {};       // stage-out: slot copied out (on copy_stream)
+    uint32_t *d_out_ids = nullptr;               // stage-out block list
+    uint8_t *d_out_flags = nullptr;              // stage-out resident flags
     cudaEvent_t ev[7] = {};   // 0-4 step stages, 5 plan read-back, 6 ring start
     bool timed = false;
 
@@ -459,6 +463,8 @@ void kvm_session_destroy(kvm_session *s) {
         for (auto &e : s->pin_ev) if (e) cudaEventDestroy(e);
         for (auto &e : s->ring_copied) if (e) cudaEventDestroy(e);
         for (auto &e : s->ring_free) if (e) cudaEventDestroy(e);
+        for (auto &e : s->out_gathered) if (e) cudaEventDestroy(e);
+        for (auto &e : s->out_done) if (e) cudaEventDestroy(e);
         for (auto &e : s->ev) if (e) cudaEventDestroy(e);
         if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
     }
@@ -581,6 +587,8 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->d_stage_counts), sizeof(uint32_t) * stage_cap},
         {reinterpret_cast<void **>(&s->d_meank), sizeof(float) * L * E},
         {reinterpret_cast<void **>(&s->d_theta), sizeof(float) * (kMaxHeadDim / 2)},
+        {reinterpret_cast<void **>(&s->d_out_ids), sizeof(uint32_t) * nb},
+        {reinterpret_cast<void **>(&s->d_out_flags), nb},
     };
     size_t total = 0;
     for (auto &it : items) total += (it.bytes + 255u) & ~static_cast<size_t>(255u);
@@ -613,6 +621,8 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
     for (int i = 0; i < kvm_session::kRingSlots; ++i) {
         e = cudaEventCreateWithFlags(&s->ring_copied[i], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ring_free[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->out_gathered[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->out_done[i], cudaEventDisableTiming);
         if (e != cudaSuccess) return cleanup(e, "event");
     }
     for (auto &ev : s->ev) {
@@ -1232,6 +1242,98 @@ kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
     a.row_stride = src->row_stride;
     KVM_CUDA(s, launch_stagein(a, st, 0), "stage-in launch");
     s->launches++;
+    return KVM_OK;
+}
+
+uint64_t kvm_stageout_item_bytes(const kvm_session *s) {
+    return s ? static_cast<uint64_t>(s->cfg.n_layer) * s->cfg.block_tokens * (s->row_bytes_k + s->row_bytes_v)
+             : 0u;
+}
+
+kvm_status kvm_stageout(kvm_session *s, kvm_stream stream, const uint32_t *ids, uint32_t n,
+                        const kvm_window *win, void *dst, uint8_t *resident) {
+    if (!s) return KVM_EINVAL;
+    if (n == 0) return KVM_OK;
+    if (!ids || !dst) return fail(s, KVM_EINVAL, "null block list or destination");
+    if (n > s->max_blocks) return fail(s, KVM_EINVAL, "at most max_blocks (%u) blocks per call", s->max_blocks);
+    if (!win || !win->d_k || !win->d_v) return fail(s, KVM_EINVAL, "null window");
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    kvm_status r = upload_window(s, st, win);
+    if (r != KVM_OK) return r;
+    r = upload_small(s, st, s->d_out_ids, ids, sizeof(uint32_t) * n);
+    if (r != KVM_OK) return r;
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, dst) != cudaSuccess) {
+        (void)cudaGetLastError();
+        pa.type = cudaMemoryTypeUnregistered;
+    }
+    const bool on_device = pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged;
+    const uint64_t item_bytes = kvm_stageout_item_bytes(s);
+    StageoutArgs a{};
+    a.gpu_slot = s->bt.gpu_slot;
+    a.n_tokens = s->bt.n_tokens;
+    a.n_blocks = s->n_blocks;
+    a.n_slots = s->n_slots;
+    a.n_layer = s->cfg.n_layer;
+    a.block_tokens = s->cfg.block_tokens;
+    a.win_k = s->d_win;
+    a.win_v = s->d_win + s->cfg.n_layer;
+    a.row_bytes_k = s->row_bytes_k;
+    a.row_bytes_v = s->row_bytes_v;
+    a.item_bytes = item_bytes;
+    a.resident = s->d_out_flags;
+    a.status = s->d_status;
+    const bool rows16 = s->row_bytes_k % 16u == 0 && s->row_bytes_v % 16u == 0 && window_aligned16(s);
+    if (on_device) {
+        a.ids = s->d_out_ids;
+        a.n = n;
+        a.item0 = 0;
+        a.dst = static_cast<uint8_t *>(dst);
+        a.bulk = rows16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 ? 1u : 0u;
+        KVM_CUDA(s, launch_stageout(a, st), "stage-out launch");
+        s->launches++;
+    } else {
+        // host destination: pack chunks into the HBM ring on `st`, copy each
+        // slot out on the copy stream while the next one is packed
+        const uint64_t slot_cap = s->ring_bytes / kvm_session::kRingSlots;
+        if (item_bytes > slot_cap)
+            return fail(s, KVM_ENOMEM, "staging ring slot (%llu B) smaller than one block (%llu B)",
+                        static_cast<unsigned long long>(slot_cap), static_cast<unsigned long long>(item_bytes));
+        if (!s->d_ring) {
+            KVM_CUDA(s, cudaStreamSynchronize(st), "ring allocation sync");
+            KVM_CUDA(s, cudaMalloc(&s->d_ring, s->ring_bytes), "staging ring allocation");
+        }
+        const uint32_t per_slot = static_cast<uint32_t>(slot_cap / item_bytes);
+        a.bulk = rows16 ? 1u : 0u;
+        uint8_t *out = static_cast<uint8_t *>(dst);
+        int last = 0;
+        uint32_t chunk = 0;
+        for (uint32_t i0 = 0; i0 < n; i0 += per_slot, ++chunk) {
+            const uint32_t m = std::min(per_slot, n - i0);
+            const int rs = static_cast<int>(chunk % kvm_session::kRingSlots);
+            uint8_t *ring = s->d_ring + static_cast<uint64_t>(rs) * slot_cap;
+            // the slot's previous copy-out must be done before it is packed again
+            KVM_CUDA(s, cudaStreamWaitEvent(st, s->out_done[rs], 0), "ring slot wait");
+            a.ids = s->d_out_ids + i0;
+            a.n = m;
+            a.item0 = i0;
+            a.dst = ring;
+            KVM_CUDA(s, launch_stageout(a, st), "stage-out launch");
+            s->launches++;
+            KVM_CUDA(s, cudaEventRecord(s->out_gathered[rs], st), "stage-out packed");
+            KVM_CUDA(s, cudaStreamWaitEvent(s->copy_stream, s->out_gathered[rs], 0), "stage-out packed wait");
+            KVM_CUDA(s, cudaMemcpyAsync(out + static_cast<uint64_t>(i0) * item_bytes, ring, m * item_bytes,
+                                        cudaMemcpyDeviceToHost, s->copy_stream),
+                     "stage-out D2H");
+            KVM_CUDA(s, cudaEventRecord(s->out_done[rs], s->copy_stream), "stage-out copied");
+            last = rs;
+        }
+        // work queued on `st` after this call sees the copies done
+        KVM_CUDA(s, cudaStreamWaitEvent(st, s->out_done[last], 0), "stage-out join");
+    }
+    if (resident)
+        KVM_CUDA(s, cudaMemcpyAsync(resident, s->d_out_flags, n, cudaMemcpyDeviceToHost, st), "resident flags");
     return KVM_OK;
 }
 

@@ -1,0 +1,137 @@
+// kvm_stageout.cu -- stage-out (harvest) of packed window rows.
+//
+// Replaces the reference's harvest gather (harvest_gpu_v ->
+// kvmem_stageout_enqueue / kvmem_stageout_submit,
+// src/adapter/llama-memory-kvmem.cpp:2318-2410,
+// src/adapter/llama-kvmem-stagein.cu:842-963): for a list of blocks, every
+// layer's K and V rows (n_tokens rows from the block's window slot, read from
+// the device block table so no host round trip is needed) are packed into a
+// contiguous destination -- item j at dst + j*item_bytes, layer l at
+// + l*T*(row_bytes_k + row_bytes_v), K rows then V rows.
+//
+// stageout_kernel: a one-warp CTA whose elected lane moves 16 KiB pieces with
+// TMA bulk copies -- cp.async.bulk global->shared completing on an mbarrier,
+// then cp.async.bulk shared->global -- double-buffered so the store of one
+// piece overlaps the load of the next; six or seven such CTAs per SM keep
+// ~200 KiB in flight.  A byte-copy path serves destinations or rows that are
+// not 16-byte aligned.
+#include "kvm_internal.cuh"
+#include "kvm_kernels.h"
+
+#include <atomic>
+
+namespace kvm {
+
+namespace {
+
+constexpr uint32_t kPiece = 16u * 1024u;
+constexpr int kOutStages = 2;
+constexpr uint32_t kOutSmem = 128u + kOutStages * kPiece;
+
+struct Piece {
+    const uint8_t *src;
+    uint8_t *dst;
+    uint32_t bytes;
+};
+
+// Unit u = ((j * L + l) * 2 + kv) * pieces + p.  bytes == 0: nothing to move.
+__device__ __forceinline__ Piece decode_piece(const StageoutArgs &a, uint64_t u, uint32_t pieces) {
+    Piece pc{nullptr, nullptr, 0u};
+    const uint32_t p = static_cast<uint32_t>(u % pieces);
+    uint64_t r = u / pieces;
+    const uint32_t kv = static_cast<uint32_t>(r & 1u);
+    r >>= 1;
+    const uint32_t l = static_cast<uint32_t>(r % a.n_layer);
+    const uint32_t j = static_cast<uint32_t>(r / a.n_layer);
+    const uint32_t b = a.ids[j];
+    const bool ok = b < a.n_blocks;
+    const int32_t slot = ok ? a.gpu_slot[b] : -1;
+    const bool res = slot >= 0 && static_cast<uint32_t>(slot) < a.n_slots;
+    if (p == 0 && l == 0 && kv == 0 && a.resident) a.resident[a.item0 + j] = res ? 1u : 0u;
+    if (!res) return pc;
+    const uint32_t nt = min(a.n_tokens[b], a.block_tokens);
+    const uint32_t rb = kv ? a.row_bytes_v : a.row_bytes_k;
+    const uint32_t total = nt * rb;
+    const uint32_t off = p * kPiece;
+    if (off >= total) return pc;
+    pc.bytes = min(kPiece, total - off);
+    const uint8_t *base = kv ? a.win_v[l] : a.win_k[l];
+    pc.src = base + static_cast<uint64_t>(slot) * a.block_tokens * rb + off;
+    pc.dst = a.dst + static_cast<uint64_t>(j) * a.item_bytes +
+             static_cast<uint64_t>(l) * a.block_tokens * (a.row_bytes_k + a.row_bytes_v) +
+             (kv ? static_cast<uint64_t>(a.block_tokens) * a.row_bytes_k : 0ull) + off;
+    return pc;
+}
+
+__global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *buf = smem + 128;
+    const uint32_t pieces = (a.block_tokens * max(a.row_bytes_k, a.row_bytes_v) + kPiece - 1u) / kPiece;
+    const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
+    const int lane = threadIdx.x;
+    if (!a.bulk) {
+        // unaligned rows or destination: every lane copies bytes
+        for (uint64_t u = blockIdx.x; u < total; u += gridDim.x) {
+            const Piece pc = decode_piece(a, u, pieces);
+            for (uint32_t i = lane; i < pc.bytes; i += 32u) pc.dst[i] = pc.src[i];
+        }
+        return;
+    }
+    if (lane != 0) return;
+    for (int s = 0; s < kOutStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    uint32_t k = 0;
+    bool ok = true;
+    for (uint64_t u = blockIdx.x; u < total; u += gridDim.x) {
+        const Piece pc = decode_piece(a, u, pieces);
+        if (pc.bytes == 0) continue;
+        const uint32_t s = k % kOutStages;
+        // the store that last read stage s was issued kOutStages pieces ago
+        if (k >= static_cast<uint32_t>(kOutStages)) bulk_wait_read<kOutStages - 1>();
+        mbar_arrive_expect_tx(&full[s], pc.bytes);
+        bulk_g2s(buf + s * kPiece, pc.src, pc.bytes, &full[s]);
+        if (!mbar_wait_bounded(&full[s], (k / kOutStages) & 1u)) {
+            set_status(a.status, kErrTimeout);
+            ok = false;
+            break;
+        }
+        bulk_s2g(pc.dst, buf + s * kPiece, pc.bytes);
+        bulk_commit();
+        ++k;
+    }
+    if (!ok) {
+        // bounded wait for the load still landing in this CTA's shared memory
+        const uint32_t s = k % kOutStages;
+        (void)mbar_wait_bounded(&full[s], (k / kOutStages) & 1u);
+    }
+    bulk_wait_all<0>();
+}
+
+}  // namespace
+
+cudaError_t launch_stageout(const StageoutArgs &a, cudaStream_t stream) {
+    if (a.n == 0) return cudaSuccess;
+    static std::atomic<uint64_t> attr{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!(attr.load(std::memory_order_acquire) & (1ull << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(stageout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kOutSmem));
+        if (e != cudaSuccess) return e;
+        attr.fetch_or(1ull << dev, std::memory_order_acq_rel);
+    }
+    int per_sm = 1, sms = 148;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stageout_kernel, 32, kOutSmem);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (per_sm < 1) per_sm = 1;
+    const uint32_t pieces = (a.block_tokens * (a.row_bytes_k > a.row_bytes_v ? a.row_bytes_k : a.row_bytes_v) +
+                             kPiece - 1u) / kPiece;
+    const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
+    uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
+    if (grid > total) grid = total;
+    stageout_kernel<<<static_cast<uint32_t>(grid), 32, kOutSmem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace kvm

@@ -39,7 +39,7 @@ ABI_SYMBOLS = (
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
     "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
     "kvm_meank_zero", "kvm_query_reset", "kvm_query_add", "kvm_set_transform",
-    "kvm_attn_rot_nrot",
+    "kvm_attn_rot_nrot", "kvm_stageout", "kvm_stageout_item_bytes",
 )
 
 
@@ -189,6 +189,8 @@ def lib():
             "kvm_query_add": (C.c_int, [vp, vp, u32, u32, C.POINTER(Rows), vp]),
             "kvm_set_transform": (C.c_int, [vp, C.POINTER(Transform)]),
             "kvm_attn_rot_nrot": (u32, [i32, u32, C.c_int]),
+            "kvm_stageout": (C.c_int, [vp, vp, vp, u32, C.POINTER(Window), vp, vp]),
+            "kvm_stageout_item_bytes": (u64, [vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -413,6 +415,23 @@ class Session:
         win = self._window(k_bases, v_bases)
         self._check(lib().kvm_stagein(self.h, _stream(stream), C.byref(src), C.byref(win)),
                     "stagein")
+
+    @property
+    def stageout_item_bytes(self) -> int:
+        return int(lib().kvm_stageout_item_bytes(self.h))
+
+    def stageout(self, ids, k_bases, v_bases, dst, stream=None, want_resident=False):
+        """Packed window rows of blocks `ids` into dst (device pointer / tensor or
+        host array); returns the resident flags when asked (after a wait)."""
+        idv = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
+        win = self._window(k_bases, v_bases)
+        res = np.zeros(max(1, idv.size), np.uint8) if want_resident else None
+        self._check(lib().kvm_stageout(self.h, _stream(stream), idv.ctypes.data, idv.size, C.byref(win),
+                                        _ptr(dst), None if res is None else res.ctypes.data), "stageout")
+        if res is not None:
+            self.wait(stream=stream)
+            return res[:idv.size]
+        return None
 
     def step(self, src: Source, k_bases, v_bases, mandatory=(), stream=None):
         m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))

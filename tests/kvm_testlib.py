@@ -72,7 +72,7 @@ class Rig:
         return [self.win_v[l].data_ptr() for l in range(self.shape.n_layer)]
 
 
-def make_rig(shape: Shape, seed: int = 0, device: int = 0, outlier_channels=None):
+def make_rig(shape: Shape, seed: int = 0, device: int = 0, outlier_channels=None, **cfg_extra):
     import torch
     import kvm
     import oracle as O
@@ -82,7 +82,7 @@ def make_rig(shape: Shape, seed: int = 0, device: int = 0, outlier_channels=None
         block_tokens=T, select_budget=shape.budget_blocks * T, gen_reserve=shape.gen_blocks * T,
         sink_blocks=shape.sink_blocks, recent_blocks=shape.recent_blocks, n_layer=L,
         n_head_kv=shape.n_head_kv, head_dim=shape.head_dim, n_head_q=shape.n_head_q,
-        max_blocks=B + 8, type_k=shape.type_k, type_v=shape.type_v)
+        max_blocks=B + 8, type_k=shape.type_k, type_v=shape.type_v, **cfg_extra)
     sess = kvm.Session(cfg, device)
     dev = torch.device("cuda", device)
     k = O.synth_f16(rng, (L, B, T, E), E, outlier_channels=outlier_channels)
