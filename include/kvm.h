@@ -362,6 +362,16 @@ kvm_status kvm_set_scores(kvm_session *s, kvm_stream stream, const double *score
  * (walked from its end, newest first). */
 kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,
                       uint32_t n_mandatory);
+/* KvMemStore::pick_semantic_groups (kvmem/src/host/kvmem_store.cpp:625-756)
+ * in place of kvm_select: the same sink / mandatory / recent pins, then whole
+ * groups -- spans[2g], spans[2g+1] a half-open token span (host array),
+ * scores[g] its f64 score (host or device) -- in score-descending,
+ * group-descending order; a group is admitted with every block it overlaps
+ * or skipped when they do not fit; the rest of the budget stays unused.
+ * At most 8192 groups. */
+kvm_status kvm_select_groups(kvm_session *s, kvm_stream stream, const uint32_t *spans,
+                             const double *scores, uint32_t n_groups,
+                             const uint32_t *mandatory, uint32_t n_mandatory);
 /* Use a caller-chosen selection instead of kvm_select (any order, duplicates
  * and out-of-range ids are dropped like set_selection does). */
 kvm_status kvm_set_selection_ids(kvm_session *s, kvm_stream stream, const uint32_t *ids,

@@ -248,6 +248,27 @@ struct SelectArgs {
 
 cudaError_t launch_select(const SelectArgs &a, cudaStream_t stream);
 
+// pick_semantic_groups
+constexpr uint32_t kMaxGroups = 8192;
+struct GroupSelectArgs {
+    const uint32_t *spans;         // [n_groups][2] half-open token spans
+    const double *scores;          // [n_groups]
+    uint32_t n_groups;
+    uint32_t n_blocks;
+    uint32_t budget;
+    uint32_t sink;
+    uint32_t recent;
+    uint32_t block_tokens;
+    uint32_t covered_tokens;       // tokens registered (last block's start + its tokens)
+    const uint32_t *mandatory;
+    uint32_t n_mandatory;
+    uint32_t *selected;
+    PlanHeader *hdr;
+};
+
+size_t group_select_smem(uint32_t n_groups, uint32_t n_blocks);
+cudaError_t launch_group_select(const GroupSelectArgs &a, cudaStream_t stream);
+
 // Sort ascending + dedupe + drop >= n of a caller selection (device, n <= cap).
 cudaError_t launch_canon_ids(const uint32_t *ids, uint32_t n_ids, uint32_t n_blocks,
                              uint32_t *selected, PlanHeader *hdr, cudaStream_t stream);

@@ -20,6 +20,8 @@
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
+#include <atomic>
+
 namespace kvm {
 
 __device__ __forceinline__ uint64_t score_key(double s) {
@@ -203,6 +205,145 @@ cudaError_t launch_canon_ids(const uint32_t *ids, uint32_t n_ids, uint32_t n_blo
     if (smem > 48u * 1024u)
         cudaFuncSetAttribute(canon_ids_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     canon_ids_kernel<<<1, kSelectThreads, smem, stream>>>(ids, n_ids, n_blocks, selected, hdr);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------ semantic groups --
+//
+// KvMemStore::pick_semantic_groups (kvmem/src/host/kvmem_store.cpp:625-756):
+// the same sink / mandatory / recent pins as pick_topk_blocks, then whole
+// groups (half-open token spans, each covering every block it overlaps) in
+// the order score desc, group id desc; a group whose not-yet-kept blocks do
+// not fit in the remaining budget is skipped, never admitted in part; stop
+// once the budget is full.  Blocks a group shares with kept ones are charged
+// once.  The remaining budget is left unused, as in the reference.
+//
+// One CTA: candidates are built in parallel and sorted (bitonic, shared
+// memory) on (score key + 1, group id) descending -- invalid spans get key 0
+// and sink to the end; NaN scores rank below every number (the reference's
+// comparator is undefined on NaN).  Warp 0 then walks the sorted groups in
+// order; each group's new-block count and marking use the whole warp.
+__global__ void __launch_bounds__(kSelectThreads) group_select_kernel(GroupSelectArgs a) {
+    extern __shared__ __align__(16) uint8_t gsm[];
+    __shared__ uint32_t scratch[40];
+    __shared__ uint32_t s_kc;
+    __shared__ uint32_t s_valid;
+    const uint32_t n = a.n_blocks;
+    const uint32_t budget = a.budget;
+    const uint32_t tid = threadIdx.x;
+    if (n == 0) {
+        if (tid == 0) a.hdr->n_selected = 0;
+        return;
+    }
+    if (budget == 0 || n <= budget) {
+        for (uint32_t i = tid; i < n; i += kSelectThreads) a.selected[i] = i;
+        if (tid == 0) a.hdr->n_selected = n;
+        return;
+    }
+    uint32_t P = 1;
+    while (P < a.n_groups) P <<= 1;
+    uint64_t *key = reinterpret_cast<uint64_t *>(gsm);
+    uint32_t *grp = reinterpret_cast<uint32_t *>(gsm + 8u * P);
+    uint8_t *kept = gsm + 12u * P;
+    for (uint32_t i = tid; i < n; i += kSelectThreads) kept[i] = 0;
+    if (tid == 0) s_valid = 0;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t kc = 0;
+        const uint32_t sink = min(a.sink, n);
+        for (uint32_t i = 0; i < sink && kc < budget; ++i)
+            if (!kept[i]) { kept[i] = 1; ++kc; }
+        for (uint32_t i = a.n_mandatory; i > 0 && kc < budget; --i) {
+            const uint32_t id = a.mandatory[i - 1];
+            if (id < n && !kept[id]) { kept[id] = 1; ++kc; }
+        }
+        const uint32_t recent = min(a.recent, n);
+        for (uint32_t i = 0; i < recent && kc < budget; ++i) {
+            const uint32_t id = n - 1 - i;
+            if (!kept[id]) { kept[id] = 1; ++kc; }
+        }
+        s_kc = kc;
+    }
+    const uint32_t bt = max(1u, a.block_tokens);
+    for (uint32_t g = tid; g < P; g += kSelectThreads) {
+        uint64_t k = 0ull;
+        if (g < a.n_groups) {
+            const uint32_t begin = a.spans[2u * g];
+            const uint32_t end = a.spans[2u * g + 1u];
+            if (end > begin && begin < a.covered_tokens && begin / bt < n) {
+                k = score_key(a.scores[g]) + 1ull;
+                atomicAdd(&s_valid, 1u);
+            }
+        }
+        key[g] = k;
+        grp[g] = g;
+    }
+    __syncthreads();
+    // bitonic sort, descending on (key, group)
+    for (uint32_t size = 2; size <= P; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = tid; i < P / 2u; i += kSelectThreads) {
+                const uint32_t lo = 2u * stride * (i / stride) + (i % stride);
+                const uint32_t hi = lo + stride;
+                const bool desc = (lo & size) == 0u;
+                const uint64_t kl = key[lo], kh = key[hi];
+                const uint32_t gl = grp[lo], gh = grp[hi];
+                const bool lo_first = kl > kh || (kl == kh && gl > gh);   // lo ranks ahead
+                if (lo_first != desc) {
+                    key[lo] = kh;
+                    key[hi] = kl;
+                    grp[lo] = gh;
+                    grp[hi] = gl;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (tid < 32) {
+        const uint32_t lane = tid;
+        uint32_t kc = s_kc;
+        const uint32_t nv = s_valid;
+        for (uint32_t c = 0; c < nv && kc < budget; ++c) {
+            const uint32_t g = grp[c];
+            const uint32_t begin = a.spans[2u * g];
+            const uint32_t end = min(a.spans[2u * g + 1u], a.covered_tokens);
+            const uint32_t first = begin / bt;
+            const uint32_t last = min((end - 1u) / bt, n - 1u);
+            uint32_t fresh = 0;
+            for (uint32_t id0 = first; id0 <= last; id0 += 32u) {
+                const uint32_t id = id0 + lane;
+                fresh += __popc(__ballot_sync(0xffffffffu, id <= last && !kept[id]));
+            }
+            if (fresh > budget - kc) continue;
+            for (uint32_t id = first + lane; id <= last; id += 32u) kept[id] = 1;
+            __syncwarp();
+            kc += fresh;
+        }
+    }
+    __syncthreads();
+    const uint32_t total = compact_flags(kept, n, a.selected, scratch);
+    if (tid == 0) a.hdr->n_selected = total;
+}
+
+size_t group_select_smem(uint32_t n_groups, uint32_t n_blocks) {
+    uint32_t P = 1;
+    while (P < n_groups) P <<= 1;
+    return 12u * static_cast<size_t>(P) + ((n_blocks + 15u) & ~15u);
+}
+
+cudaError_t launch_group_select(const GroupSelectArgs &a, cudaStream_t stream) {
+    const size_t smem = group_select_smem(a.n_groups, a.n_blocks);
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    static std::atomic<uint64_t> attr{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!(attr.load(std::memory_order_acquire) & (1ull << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(group_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr.fetch_or(1ull << dev, std::memory_order_acq_rel);
+    }
+    group_select_kernel<<<1, kSelectThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

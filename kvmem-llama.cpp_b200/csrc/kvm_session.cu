@@ -106,6 +106,8 @@ struct kvm_session {
     cudaEvent_t out_done[kRingSlots] = {};       // stage-out: slot copied out (on copy_stream)
     uint32_t *d_out_ids = nullptr;               // stage-out block list
     uint8_t *d_out_flags = nullptr;              // stage-out resident flags
+    uint32_t *d_group_spans = nullptr;           // semantic-group spans [kMaxGroups][2]
+    double *d_group_scores = nullptr;            // semantic-group scores [kMaxGroups]
     cudaEvent_t ev[7] = {};   // 0-4 step stages, 5 plan read-back, 6 ring start
     bool timed = false;
 
@@ -589,6 +591,8 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->d_theta), sizeof(float) * (kMaxHeadDim / 2)},
         {reinterpret_cast<void **>(&s->d_out_ids), sizeof(uint32_t) * nb},
         {reinterpret_cast<void **>(&s->d_out_flags), nb},
+        {reinterpret_cast<void **>(&s->d_group_spans), sizeof(uint32_t) * 2 * kMaxGroups},
+        {reinterpret_cast<void **>(&s->d_group_scores), sizeof(double) * kMaxGroups},
     };
     size_t total = 0;
     for (auto &it : items) total += (it.bytes + 255u) & ~static_cast<size_t>(255u);
@@ -1173,6 +1177,55 @@ kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandato
     a.selected = s->plan.selected;
     a.hdr = s->plan.hdr;
     KVM_CUDA(s, launch_select(a, st), "select launch");
+    s->launches++;
+    s->have_selection = true;
+    return KVM_OK;
+}
+
+kvm_status kvm_select_groups(kvm_session *s, kvm_stream stream, const uint32_t *spans, const double *scores,
+                             uint32_t n_groups, const uint32_t *mandatory, uint32_t n_mandatory) {
+    if (!s) return KVM_EINVAL;
+    if (n_groups > kMaxGroups) return fail(s, KVM_EINVAL, "at most %u groups", kMaxGroups);
+    if (n_groups && (!spans || !scores)) return fail(s, KVM_EINVAL, "null spans or scores");
+    if (n_mandatory > s->max_blocks) return fail(s, KVM_EINVAL, "too many mandatory blocks");
+    if (n_mandatory && !mandatory) return fail(s, KVM_EINVAL, "null mandatory");
+    if (group_select_smem(n_groups, s->n_blocks) > 200u * 1024u)
+        return fail(s, KVM_EINVAL, "too many groups for %u blocks", s->n_blocks);
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    kvm_status r = upload_small(s, st, s->d_mandatory, mandatory, sizeof(uint32_t) * n_mandatory);
+    if (r != KVM_OK) return r;
+    r = upload_small(s, st, s->d_group_spans, spans, sizeof(uint32_t) * 2 * n_groups);
+    if (r != KVM_OK) return r;
+    if (n_groups) {
+        cudaPointerAttributes pa{};
+        if (cudaPointerGetAttributes(&pa, scores) != cudaSuccess) {
+            (void)cudaGetLastError();
+            pa.type = cudaMemoryTypeUnregistered;
+        }
+        if (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) {
+            KVM_CUDA(s, cudaMemcpyAsync(s->d_group_scores, scores, sizeof(double) * n_groups,
+                                        cudaMemcpyDeviceToDevice, st), "group scores copy");
+        } else {
+            r = upload_small(s, st, s->d_group_scores, scores, sizeof(double) * n_groups);
+            if (r != KVM_OK) return r;
+        }
+    }
+    GroupSelectArgs a{};
+    a.spans = s->d_group_spans;
+    a.scores = s->d_group_scores;
+    a.n_groups = n_groups;
+    a.n_blocks = s->n_blocks;
+    a.budget = s->budget_blocks;
+    a.sink = s->cfg.sink_blocks;
+    a.recent = s->cfg.recent_blocks;
+    a.block_tokens = s->cfg.block_tokens;
+    a.covered_tokens = s->total_tokens;
+    a.mandatory = s->d_mandatory;
+    a.n_mandatory = n_mandatory;
+    a.selected = s->plan.selected;
+    a.hdr = s->plan.hdr;
+    KVM_CUDA(s, launch_group_select(a, st), "group select launch");
     s->launches++;
     s->have_selection = true;
     return KVM_OK;

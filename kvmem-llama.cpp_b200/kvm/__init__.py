@@ -39,7 +39,7 @@ ABI_SYMBOLS = (
     "kvm_get_scores", "kvm_get_timings", "kvm_kernel_launches", "kvm_quantize_rows",
     "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
     "kvm_meank_zero", "kvm_query_reset", "kvm_query_add", "kvm_set_transform",
-    "kvm_attn_rot_nrot", "kvm_stageout", "kvm_stageout_item_bytes",
+    "kvm_attn_rot_nrot", "kvm_stageout", "kvm_stageout_item_bytes", "kvm_select_groups",
 )
 
 
@@ -191,6 +191,7 @@ def lib():
             "kvm_attn_rot_nrot": (u32, [i32, u32, C.c_int]),
             "kvm_stageout": (C.c_int, [vp, vp, vp, u32, C.POINTER(Window), vp, vp]),
             "kvm_stageout_item_bytes": (u64, [vp]),
+            "kvm_select_groups": (C.c_int, [vp, vp, vp, vp, u32, vp, u32]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -400,6 +401,21 @@ class Session:
         self._check(lib().kvm_set_selection_ids(self.h, _stream(stream),
                                                  m.ctypes.data if m.size else None, m.size),
                     "set_selection_ids")
+
+    def select_groups(self, spans, scores, mandatory=(), stream=None):
+        """pick_semantic_groups: spans [g][2] half-open token spans, scores [g] f64
+        (numpy array or device tensor)."""
+        sp = np.ascontiguousarray(np.asarray(spans, dtype=np.uint32).reshape(-1, 2))
+        if hasattr(scores, "data_ptr"):
+            sc_ptr, n = scores.data_ptr(), scores.numel()
+        else:
+            sc = np.ascontiguousarray(np.asarray(scores, dtype=np.float64))
+            sc_ptr, n = sc.ctypes.data, sc.size
+        assert n == sp.shape[0]
+        m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
+        self._check(lib().kvm_select_groups(self.h, _stream(stream), sp.ctypes.data if n else None,
+                                             sc_ptr if n else None, n, m.ctypes.data if m.size else None,
+                                             m.size), "select_groups")
 
     def diff(self, force_raw_refresh=False, stream=None):
         self._check(lib().kvm_diff(self.h, _stream(stream), int(bool(force_raw_refresh))), "diff")

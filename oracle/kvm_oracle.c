@@ -535,6 +535,111 @@ static int better_cmp(const void *pa, const void *pb)
     return a > b ? -1 : (a < b ? 1 : 0);
 }
 
+/* Candidate order of pick_semantic_groups (kvmem_store.cpp:712-716): score
+ * descending, then group index descending. */
+typedef struct ora_group_cand {
+    uint32_t group, first, last;
+    double score;
+} ora_group_cand;
+
+static int group_cmp(const void *pa, const void *pb)
+{
+    const ora_group_cand *a = (const ora_group_cand *)pa;
+    const ora_group_cand *b = (const ora_group_cand *)pb;
+    if (a->score != b->score) {
+        return a->score > b->score ? -1 : 1;
+    }
+    return a->group > b->group ? -1 : (a->group < b->group ? 1 : 0);
+}
+
+uint32_t ora_pick_semantic_groups(const ora_cfg *cfg, uint32_t n, uint64_t covered_tokens,
+                                  const uint32_t *spans, const double *scores,
+                                  uint32_t n_groups, const uint32_t *mandatory,
+                                  uint32_t n_mandatory, uint32_t *out)
+{
+    if (n == 0) {
+        return 0;
+    }
+    const uint32_t budget = cfg->budget_blocks;
+    if (budget == 0 || n <= budget) {
+        for (uint32_t i = 0; i < n; ++i) {
+            out[i] = i;
+        }
+        return n;
+    }
+    uint8_t *kept = (uint8_t *)calloc(n, 1);
+    uint32_t kept_count = 0;
+#define ORA_KEEP(id_)                                                    \
+    do {                                                                 \
+        const uint32_t id__ = (id_);                                     \
+        if (id__ < n && !kept[id__]) {                                   \
+            kept[id__] = 1;                                              \
+            ++kept_count;                                                \
+        }                                                                \
+    } while (0)
+    const uint32_t sink = cfg->sink_blocks < n ? cfg->sink_blocks : n;
+    const uint32_t recent = cfg->recent_blocks < n ? cfg->recent_blocks : n;
+    for (uint32_t i = 0; i < sink && kept_count < budget; ++i) {
+        ORA_KEEP(i);
+    }
+    for (uint32_t i = n_mandatory; i > 0 && kept_count < budget; --i) {
+        ORA_KEEP(mandatory[i - 1]);
+    }
+    for (uint32_t i = 0; i < recent && kept_count < budget; ++i) {
+        ORA_KEEP(n - 1 - i);
+    }
+    const uint32_t bt = cfg->block_tokens ? cfg->block_tokens : 1;
+    ora_group_cand *cand = (ora_group_cand *)malloc(sizeof(ora_group_cand) * (n_groups ? n_groups : 1));
+    uint32_t nc = 0;
+    for (uint32_t g = 0; g < n_groups; ++g) {
+        const uint32_t begin = spans[2 * g];
+        const uint32_t end = spans[2 * g + 1];
+        if (end <= begin || begin >= covered_tokens) {
+            continue;
+        }
+        const uint32_t capped = end < covered_tokens ? end : (uint32_t)covered_tokens;
+        const uint32_t first = begin / bt;
+        uint32_t last = (capped - 1) / bt;
+        if (first >= n) {
+            continue;
+        }
+        if (last > n - 1) {
+            last = n - 1;
+        }
+        cand[nc].group = g;
+        cand[nc].first = first;
+        cand[nc].last = last;
+        cand[nc].score = scores[g];
+        ++nc;
+    }
+    qsort(cand, nc, sizeof(ora_group_cand), group_cmp);
+    for (uint32_t c = 0; c < nc; ++c) {
+        uint32_t fresh = 0;
+        for (uint32_t id = cand[c].first; id <= cand[c].last; ++id) {
+            fresh += kept[id] ? 0u : 1u;
+        }
+        if (fresh > budget - kept_count) {
+            continue;
+        }
+        for (uint32_t id = cand[c].first; id <= cand[c].last; ++id) {
+            ORA_KEEP(id);
+        }
+        if (kept_count == budget) {
+            break;
+        }
+    }
+#undef ORA_KEEP
+    uint32_t m = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (kept[i]) {
+            out[m++] = i;
+        }
+    }
+    free(cand);
+    free(kept);
+    return m;
+}
+
 uint32_t ora_pick_topk(const ora_cfg *cfg, const double *scores, uint32_t n,
                        const uint32_t *mandatory, uint32_t n_mandatory,
                        uint32_t *out)

@@ -149,6 +149,16 @@ uint32_t ora_pick_topk(const ora_cfg *cfg, const double *scores, uint32_t n,
                        uint32_t *out);
 
 /* KvMemStore::set_selection. Returns 0, or -1 where the reference throws. */
+/*
+ * KvMemStore::pick_semantic_groups (kvmem/src/host/kvmem_store.cpp:625-756).
+ * spans: [n_groups][2] half-open token spans; covered_tokens: tokens of the
+ * store (last block's start + its n_tokens).  Selected ids ascending in out.
+ */
+uint32_t ora_pick_semantic_groups(const ora_cfg *cfg, uint32_t n, uint64_t covered_tokens,
+                                  const uint32_t *spans, const double *scores,
+                                  uint32_t n_groups, const uint32_t *mandatory,
+                                  uint32_t n_mandatory, uint32_t *out);
+
 int ora_set_selection(const ora_cfg *cfg, ora_blocks *b, uint32_t n,
                       const uint32_t *ids, uint32_t n_ids,
                       int force_raw_refresh, ora_plan *plan);

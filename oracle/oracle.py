@@ -130,6 +130,9 @@ def lib():
                                 C.c_uint32, C.c_uint32, C.c_uint32, _f64p, C.c_void_p, C.c_int]
         L.ora_pick_topk.restype = C.c_uint32
         L.ora_pick_topk.argtypes = [C.POINTER(OraCfg), _f64p, C.c_uint32, _u32p, C.c_uint32, _u32p]
+        L.ora_pick_semantic_groups.restype = C.c_uint32
+        L.ora_pick_semantic_groups.argtypes = [C.POINTER(OraCfg), C.c_uint32, C.c_uint64, _u32p, _f64p,
+                                               C.c_uint32, _u32p, C.c_uint32, _u32p]
         L.ora_set_selection.restype = C.c_int
         L.ora_set_selection.argtypes = [C.POINTER(OraCfg), C.POINTER(_OraBlocks), C.c_uint32,
                                         _u32p, C.c_uint32, C.c_int, C.POINTER(_OraPlan)]
@@ -166,6 +169,9 @@ def ref():
         R.ref_set_retrieval_scores.argtypes = [C.c_void_p, _f64p, C.c_uint32]
         R.ref_pick_topk.restype = C.c_uint32
         R.ref_pick_topk.argtypes = [C.c_void_p, _u32p, C.c_uint32, _u32p]
+        R.ref_pick_semantic_groups.restype = C.c_uint32
+        R.ref_pick_semantic_groups.argtypes = [C.c_void_p, _u32p, _f64p, C.c_uint32, _u32p, C.c_uint32,
+                                               _u32p]
         R.ref_set_selection.restype = C.c_int
         R.ref_set_selection.argtypes = [C.c_void_p, _u32p, C.c_uint32, C.c_int,
                                         _u32p, C.POINTER(C.c_uint32), _u32p, C.POINTER(C.c_uint32),
@@ -366,6 +372,17 @@ def pick_topk(cfg: OraCfg, scores: np.ndarray, mandatory=()) -> np.ndarray:
     return out[:k].copy()
 
 
+def pick_semantic_groups(cfg: OraCfg, n_blocks: int, covered_tokens: int, spans, scores,
+                         mandatory=()) -> np.ndarray:
+    """KvMemStore::pick_semantic_groups restated; spans [g][2] half-open token spans."""
+    sp = np.ascontiguousarray(np.asarray(spans, dtype=np.uint32).reshape(-1, 2))
+    sc = np.ascontiguousarray(np.asarray(scores, dtype=np.float64))
+    m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
+    out = np.zeros(max(1, n_blocks), dtype=np.uint32)
+    k = lib().ora_pick_semantic_groups(C.byref(cfg), n_blocks, covered_tokens, sp, sc, sc.size, m, m.size, out)
+    return out[:k].copy()
+
+
 @dataclass
 class Blocks:
     """Block table (KvMemBlock fields used by the path), one entry per block."""
@@ -500,6 +517,14 @@ class RefStore:
         m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
         out = np.zeros(max(1, self.block_count()), dtype=np.uint32)
         k = ref().ref_pick_topk(self.h, m, m.size, out)
+        return out[:k].copy()
+
+    def pick_semantic_groups(self, spans, scores, mandatory=()):
+        sp = np.ascontiguousarray(np.asarray(spans, dtype=np.uint32).reshape(-1, 2))
+        sc = np.ascontiguousarray(np.asarray(scores, dtype=np.float64))
+        m = np.ascontiguousarray(np.asarray(mandatory, dtype=np.uint32))
+        out = np.zeros(max(1, self.block_count()), dtype=np.uint32)
+        k = ref().ref_pick_semantic_groups(self.h, sp, sc, sc.size, m, m.size, out)
         return out[:k].copy()
 
     def set_selection(self, ids, force_raw_refresh=False) -> Plan:

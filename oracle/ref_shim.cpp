@@ -65,6 +65,17 @@ uint32_t ref_pick_topk(void *s, const uint32_t *mand, uint32_t n_mand, uint32_t 
     return static_cast<uint32_t>(sel.size());
 }
 
+uint32_t ref_pick_semantic_groups(void *s, const uint32_t *spans, const double *scores, uint32_t n_groups,
+                                  const uint32_t *mand, uint32_t n_mand, uint32_t *out) {
+    std::vector<std::pair<uint32_t, uint32_t>> g(n_groups);
+    for (uint32_t i = 0; i < n_groups; ++i) g[i] = {spans[2 * i], spans[2 * i + 1]};
+    std::vector<double> sc(scores, scores + n_groups);
+    std::vector<uint32_t> m(mand, mand + n_mand);
+    auto sel = static_cast<kvmem::KvMemStore *>(s)->pick_semantic_groups(g, sc, m);
+    std::memcpy(out, sel.data(), sel.size() * sizeof(uint32_t));
+    return static_cast<uint32_t>(sel.size());
+}
+
 // Plan arrays must hold block_count() entries.  Returns 0, or -1 on a throw.
 int ref_set_selection(void *s, const uint32_t *ids, uint32_t n_ids, int force_raw,
                       uint32_t *stage_in, uint32_t *n_stage_in,

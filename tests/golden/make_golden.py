@@ -15,6 +15,8 @@ Outputs (all small, committed):
                      harvest), then decode sums flushed with write_layer_mean_sum
                      from mid-block and block-start positions; the means after it
 
+  groups_golden.json  pick_semantic_groups selections of the reference's own
+                     kvmem::KvMemStore for seeded random spans, scores, pins
   rope_golden.npz    F32 rows rotated by the reference's own kvmem::rope_neox_apply
                      (full and partial rotary dims, small and 256K-range positions)
 
@@ -192,6 +194,41 @@ def make_rope(rng):
     np.savez_compressed(os.path.join(HERE, "rope_golden.npz"), n_cases=len(ROPE_CASES), **arrays)
 
 
+def groups_case(rng):
+    """One seeded pick_semantic_groups case (config, spans, scores, pins)."""
+    T = int(rng.choice([16, 32, 64, 128]))
+    n = int(rng.integers(1, 160))
+    cfg = dict(block_tokens=T, budget_blocks=int(rng.integers(0, n + 5)),
+               sink_blocks=int(rng.integers(0, 4)), recent_blocks=int(rng.integers(0, 4)))
+    total = n * T - int(rng.integers(0, T))
+    G = int(rng.integers(0, 48))
+    b0 = rng.integers(0, total + 3 * T, G)
+    spans = np.stack([b0, b0 + rng.integers(-5, 6 * T, G)], 1).clip(0).astype(np.uint32)
+    if rng.integers(0, 3) == 0:
+        scores = rng.choice([0.0, -0.0, 1.0, 2.0], G)          # ties, signed zeros
+    else:
+        scores = rng.standard_normal(G)
+    mand = rng.integers(0, n + 3, int(rng.integers(0, 5))).astype(np.uint32)
+    return cfg, total, spans, scores, mand
+
+
+def make_groups(rng):
+    cases = []
+    for _ in range(80):
+        cfg, total, spans, scores, mand = groups_case(rng)
+        rs = O.RefStore(block_tokens=cfg["block_tokens"],
+                        select_budget=cfg["budget_blocks"] * cfg["block_tokens"],
+                        sink_blocks=cfg["sink_blocks"], recent_blocks=cfg["recent_blocks"])
+        rs.register_append(total)
+        sel = rs.pick_semantic_groups(spans, scores, mand)
+        cases.append(dict(cfg=cfg, total_tokens=total, spans=spans.tolist(),
+                          scores=[float(x) for x in scores], signbits=[bool(np.signbit(x)) for x in scores],
+                          mandatory=mand.tolist(), selected=sel.tolist()))
+    with open(os.path.join(HERE, "groups_golden.json"), "w") as f:
+        json.dump(dict(source="kvmem::KvMemStore::pick_semantic_groups compiled from CrKcel/kvmem-llama.cpp kvmem/",
+                       cases=cases), f, separators=(",", ":"))
+
+
 if __name__ == "__main__":
     O.build(ref=True)
     if not O.have_ref():
@@ -206,4 +243,6 @@ if __name__ == "__main__":
         make_meank_seq(np.random.default_rng(20261202))
     if not only or "rope" in only:
         make_rope(np.random.default_rng(20261203))
+    if not only or "groups" in only:
+        make_groups(np.random.default_rng(20261204))
     print("golden fixtures written to", HERE)

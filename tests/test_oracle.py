@@ -156,6 +156,67 @@ def test_add_rows_is_the_ordered_f32_sum(oracle):
     assert oracle.add_rows(np.array([-0.0], np.float32), np.array([[-0.0]], np.float32))[0] == 0.0
 
 
+# ------------------------------------------------------- semantic groups ---
+
+def _group_case_scores(c):
+    return np.array([-0.0 if (x == 0.0 and sb) else x for x, sb in zip(c["scores"], c["signbits"])],
+                    np.float64)
+
+
+def test_semantic_groups_reference_inline_cases(oracle):
+    """The expectations of kvmem/tests/kvmem_store_test.cpp for
+    pick_semantic_groups (whole-group admission, shared boundary charged once,
+    newest mandatory ids kept under budget pressure)."""
+    # four variable-length groups, budget 8, sink 1, recent 1 (:1020-1058)
+    sel = oracle.pick_semantic_groups(oracle.make_cfg(32, 8, 1, 1), 20, 32 * 20,
+                                      [(32, 128), (131, 251), (256, 352), (384, 448)],
+                                      [1.0, 10.0, 9.0, 2.0])
+    assert sel.size <= 8 and {0, 19, 4, 5, 6, 7} <= set(sel.tolist())
+    assert not ({8, 9, 10} & set(sel.tolist()))
+    # two groups sharing block 2, mandatory {7} (:1060-1080)
+    sel = oracle.pick_semantic_groups(oracle.make_cfg(64, 4, 0, 0), 8, 64 * 8,
+                                      [(64, 138), (138, 256)], [2.0, 1.0], [7])
+    assert sel.tolist() == [1, 2, 3, 7]
+    # sink {0} + mandatory {1,2,3,4} > budget 4: newest mandatory ids (:480-503)
+    sel = oracle.pick_semantic_groups(oracle.make_cfg(32, 4, 1, 2), 10, 320, [(160, 224)], [1.0],
+                                      [1, 2, 3, 4])
+    assert sel.tolist() == [0, 2, 3, 4]
+
+
+def test_semantic_groups_match_reference_golden(oracle):
+    g = json.load(open(os.path.join(GOLD, "groups_golden.json")))
+    for i, c in enumerate(g["cases"]):
+        cfg = c["cfg"]
+        n = (c["total_tokens"] + cfg["block_tokens"] - 1) // cfg["block_tokens"]
+        sel = oracle.pick_semantic_groups(
+            oracle.make_cfg(cfg["block_tokens"], cfg["budget_blocks"], cfg["sink_blocks"],
+                            cfg["recent_blocks"]),
+            n, c["total_tokens"], np.array(c["spans"], np.uint32).reshape(-1, 2),
+            _group_case_scores(c), c["mandatory"])
+        assert sel.tolist() == c["selected"], i
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(HERE), "oracle", "_ref",
+                                                    "libkvmem_ref.so")),
+                    reason="reference library not built here")
+def test_semantic_groups_live_vs_reference(oracle):
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import groups_case
+    rng = np.random.default_rng(99)
+    for _ in range(400):
+        cfg, total, spans, scores, mand = groups_case(rng)
+        rs = oracle.RefStore(block_tokens=cfg["block_tokens"],
+                             select_budget=cfg["budget_blocks"] * cfg["block_tokens"],
+                             sink_blocks=cfg["sink_blocks"], recent_blocks=cfg["recent_blocks"])
+        rs.register_append(total)
+        want = rs.pick_semantic_groups(spans, scores, mand)
+        got = oracle.pick_semantic_groups(
+            oracle.make_cfg(cfg["block_tokens"], cfg["budget_blocks"], cfg["sink_blocks"],
+                            cfg["recent_blocks"]), rs.block_count(), total, spans, scores, mand)
+        assert np.array_equal(got, want)
+
+
 # ------------------------------------------------- stage-in transforms ---
 
 def test_rope_oracle_matches_reference_golden(oracle):
