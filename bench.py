@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--profile-case", choices=("score",), default=None,
                     help="small profiling case: the scorer alone over config-2 summaries "
                          "(134 MB on the device, no history)")
-    ap.add_argument("--mode", choices=("sessions", "layer-split", "incremental", "multi-session"),
+    ap.add_argument("--mode", choices=("sessions", "layer-split", "incremental", "multi-session",
+                                       "kernels"),
                     default="sessions",
                     help="sessions: one independent config-2 session per GPU (the bench line); "
                          "layer-split: one 1M-token session (8192 blocks) whose 16 layers are "
@@ -62,7 +63,9 @@ def parse():
                          "incremental: config 4, 40 overlapping reselections of a 1M-token "
                          "session without a window reset; "
                          "multi-session: config 5, 64 sessions of 131072 tokens split over the "
-                         "GPUs, each on its own stream")
+                         "GPUs, each on its own stream; "
+                         "kernels: the producers, stage-in transform modes, stage-out and "
+                         "semantic-group selection at config-2 sizes (one GPU)")
     ap.add_argument("--combine", choices=("allgather", "allreduce"), default="allgather")
     ap.add_argument("--config", type=int, choices=(1, 2), default=2,
                     help="2: BASELINE configs[1] (16 layers, the bench line); "
@@ -912,6 +915,111 @@ def run_layer_split(args):
     dist.destroy_process_group()
 
 
+def _time_ms(torch, fn, reps=5, warm=2, stream=None):
+    """Min over reps of the CUDA-event time of fn() on the current stream."""
+    out = []
+    for i in range(warm + reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= warm:
+            out.append(a.elapsed_time(b))
+    return min(out)
+
+
+def run_kernels(args):
+    """The kernels around the step at config-2 sizes, each timed alone with CUDA
+    events (inputs larger than L2 where the kernel streams):
+      summarize      mean-K of 16 layers x 2048 blocks of F16 K (4.3 GB read);
+      write_mean_k   one prefill ubatch (2048 tokens) of one layer per call, 16
+                     calls captured in a CUDA graph (no host launch cost);
+      stage-in       the config-2 cold-window stage-in plain, with attn_rot
+                     (Hadamard 256 on K, 64 on V) and with RoPE + attn_rot;
+      stage-out      the 256 selected blocks (1.14 GB) to HBM and to pinned host;
+      select_groups  8192 groups over the 2048 blocks."""
+    import torch
+    import kvm
+    peak, peak_src = load_peak()
+    dev = torch.device("cuda", 0)
+    c = dict(CFG2)
+    L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    hk, hv = gen_history(torch, c, args.seed, dev)
+    sess = _make_session(kvm, c, B, 0)
+    sess.register_append(B * T)
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    out = {"metric": "auxiliary kernels at config-2 sizes", "n_gpus": 1, "data": "synthetic",
+           "peak_hbm_gbs": peak, "peak_source": peak_src}
+    # ---- producers
+    ms = _time_ms(torch, lambda: sess.summarize(src))
+    byt = L * B * T * E * 2
+    out["summarize"] = {"ms": round(ms, 4), "GBs": round(byt / ms / 1e6, 1),
+                        "frac": round(byt / ms / 1e6 / peak, 3), "bytes": byt}
+    rows = [kvm.rows_of(hk[l, :16].reshape(16 * T, E), c["n_head_kv"], c["head_dim"]) for l in range(L)]
+    for l in range(L):
+        sess.write_mean_k(l, 0, 16 * T, rows[l])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for l in range(L):
+            sess.write_mean_k(l, 0, 16 * T, rows[l])
+    ms = _time_ms(torch, g.replay)
+    byt = L * 16 * T * E * 2
+    out["write_mean_k_ubatch"] = {"calls": L, "tokens_per_call": 16 * T, "ms": round(ms, 4),
+                                  "us_per_call": round(1e3 * ms / L, 2), "GBs": round(byt / ms / 1e6, 1)}
+    del g
+    sess.summarize(src)
+    # ---- stage-in with transforms (cold window every time)
+    wk, wv, kb, vb = _window(torch, c, sess.n_slots, dev)
+    q = gen_queries(torch, c, 1, args.seed, dev)[0]
+    sess.set_query(q.data_ptr(), np.ones(L, np.uint32))
+    step_b = algo_bytes(c, 256)[1]
+    xf = {}
+    for name, t in (("plain", None), ("attn_rot", dict(rot_k=256, rot_v=64)),
+                    ("rope_attn_rot", dict(rot_k=256, rot_v=64, rope_n_rot=256, rope_freq_base=1e6))):
+        if t:
+            sess.set_transform(**t)
+        else:
+            sess.clear_transform()
+
+        # one cold-window plan; repeating the stage-in re-stages the same 256 blocks
+        sess.reset_window()
+        sess.score()
+        sess.select()
+        sess.diff()
+        ms = _time_ms(torch, lambda: sess.stagein(src, kb, vb))
+        xf[name] = {"stagein_ms": round(ms, 4), "GBs": round(step_b / ms / 1e6, 1),
+                    "frac": round(step_b / ms / 1e6 / peak, 3)}
+    sess.clear_transform()
+    out["stagein_transforms"] = xf
+    # ---- stage-out
+    sess.reset_window()
+    sess.step(src, kb, vb)
+    sel = sess.plan()["selected"]
+    item = sess.stageout_item_bytes
+    dd = torch.empty(len(sel) * item, dtype=torch.uint8, device=dev)
+    hp = torch.empty(len(sel) * item, dtype=torch.uint8).pin_memory()
+    so = {"blocks": int(len(sel)), "bytes": int(len(sel) * item)}
+    for name, buf in (("hbm", dd), ("pinned_host", hp)):
+        ms = _time_ms(torch, lambda: sess.stageout(sel, kb, vb, buf))
+        so[name] = {"ms": round(ms, 4), "GBs_packed": round(len(sel) * item / ms / 1e6, 1)}
+    so["hbm"]["frac_rw"] = round(2 * len(sel) * item / (so["hbm"]["ms"] * 1e6) / peak, 3)
+    out["stageout"] = so
+    # ---- semantic groups
+    rng = np.random.default_rng(args.seed)
+    b0 = rng.integers(0, B * T, 8192)
+    spans = np.stack([b0, b0 + rng.integers(1, 4 * T, 8192)], 1).astype(np.uint32)
+    scores = torch.from_numpy(rng.standard_normal(8192)).to(dev)
+    ms = _time_ms(torch, lambda: sess.select_groups(spans, scores))
+    out["select_groups_8192"] = {"ms": round(ms, 4)}
+    out["gpu_launches_total"] = int(sess.kernel_launches)
+    print(json.dumps(out), flush=True)
+    sess.close()
+
+
 def main():
     args = parse()
     if args.mode == "layer-split":
@@ -920,6 +1028,8 @@ def main():
         run_incremental(args)
     elif args.mode == "multi-session":
         run_multi_session(args)
+    elif args.mode == "kernels":
+        run_kernels(args)
     elif args.profile_case == "score":
         run_profile_score(args)
     elif args.impl == "reference":

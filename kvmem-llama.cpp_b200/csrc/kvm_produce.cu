@@ -195,13 +195,28 @@ __global__ void __launch_bounds__(kStagedThreads) mean_k_staged_kernel(MeanKArgs
     const uint32_t take = p1 - p0;
     const uint8_t *rows = a.src + l * a.nb_layer + static_cast<uint64_t>(p0 - a.pos0) * a.nb_row;
     if (VEC) {
+        // eight independent 16-byte loads in flight per thread, then their stores
         const uint32_t segs = nc / G;
-        for (uint32_t r = threadIdx.x; r < take * segs; r += kStagedThreads) {
-            const uint32_t t = r / segs;
-            const uint32_t e = c0 + (r - t * segs) * G;
-            const uint8_t *p = rows + t * a.nb_row + (e / a.head_dim) * a.nb_head + (e % a.head_dim) * a.nb_dim;
-            *reinterpret_cast<uint4 *>(slab + (static_cast<size_t>(t) * C + (e - c0)) * ES) =
-                __ldcs(reinterpret_cast<const uint4 *>(p));
+        const uint32_t n_seg = take * segs;
+        constexpr uint32_t U = 8;
+        for (uint32_t r0 = threadIdx.x; r0 < n_seg; r0 += U * kStagedThreads) {
+            uint4 v[U];
+            uint32_t at[U];
+#pragma unroll
+            for (uint32_t k = 0; k < U; ++k) {
+                const uint32_t r = r0 + k * kStagedThreads;
+                at[k] = 0xffffffffu;
+                if (r < n_seg) {
+                    const uint32_t t = r / segs;
+                    const uint32_t e = c0 + (r - t * segs) * G;
+                    const uint8_t *p = rows + t * a.nb_row + (e / a.head_dim) * a.nb_head + (e % a.head_dim) * a.nb_dim;
+                    v[k] = __ldcs(reinterpret_cast<const uint4 *>(p));
+                    at[k] = t * C + (e - c0);
+                }
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < U; ++k)
+                if (at[k] != 0xffffffffu) *reinterpret_cast<uint4 *>(slab + static_cast<size_t>(at[k]) * ES) = v[k];
         }
     } else {
         for (uint32_t r = threadIdx.x; r < take * nc; r += kStagedThreads) {
@@ -220,6 +235,7 @@ __global__ void __launch_bounds__(kStagedThreads) mean_k_staged_kernel(MeanKArgs
         const size_t idx = sum_index(a.sum, l, c0 + c, b);
         float acc = off == 0 ? 0.0f : a.sum.sum_t[idx];
         const uint8_t *q = slab + static_cast<size_t>(c) * ES;
+#pragma unroll 8
         for (uint32_t t = 0; t < take; ++t) acc = __fadd_rn(acc, load_elem(q + static_cast<size_t>(t) * C * ES, TYPE));
         a.sum.sum_t[idx] = acc;
     }

@@ -299,23 +299,39 @@ __global__ void __launch_bounds__(kSelectThreads) group_select_kernel(GroupSelec
             __syncthreads();
         }
     }
+    // the sorted groups' block ranges, packed into the key slots
+    const uint32_t nv = s_valid;
+    uint32_t *range = reinterpret_cast<uint32_t *>(key);
+    for (uint32_t c = tid; c < nv; c += kSelectThreads) {
+        const uint32_t g = grp[c];
+        const uint32_t begin = a.spans[2u * g];
+        const uint32_t end = min(a.spans[2u * g + 1u], a.covered_tokens);
+        range[2u * c] = begin / bt;
+        range[2u * c + 1u] = min((end - 1u) / bt, n - 1u);
+    }
+    __syncthreads();
     if (tid < 32) {
         const uint32_t lane = tid;
         uint32_t kc = s_kc;
-        const uint32_t nv = s_valid;
         for (uint32_t c = 0; c < nv && kc < budget; ++c) {
-            const uint32_t g = grp[c];
-            const uint32_t begin = a.spans[2u * g];
-            const uint32_t end = min(a.spans[2u * g + 1u], a.covered_tokens);
-            const uint32_t first = begin / bt;
-            const uint32_t last = min((end - 1u) / bt, n - 1u);
+            const uint32_t first = range[2u * c];
+            const uint32_t last = range[2u * c + 1u];
+            if (last - first >= budget - kc) {
+                // more blocks than the remaining budget: fits only if enough are kept
+                uint32_t fresh = 0;
+                for (uint32_t id0 = first; id0 <= last; id0 += 32u) {
+                    const uint32_t id = id0 + lane;
+                    fresh += __popc(__ballot_sync(0xffffffffu, id <= last && !kept[id]));
+                }
+                if (fresh > budget - kc) continue;
+            }
             uint32_t fresh = 0;
             for (uint32_t id0 = first; id0 <= last; id0 += 32u) {
                 const uint32_t id = id0 + lane;
-                fresh += __popc(__ballot_sync(0xffffffffu, id <= last && !kept[id]));
+                const bool add = id <= last && !kept[id];
+                fresh += __popc(__ballot_sync(0xffffffffu, add));
+                if (add) kept[id] = 1;
             }
-            if (fresh > budget - kc) continue;
-            for (uint32_t id = first + lane; id <= last; id += 32u) kept[id] = 1;
             __syncwarp();
             kc += fresh;
         }
