@@ -9,10 +9,13 @@
 // stagein_kernel: persistent CTAs walk (cold block, layer, K|V, row tile)
 // tasks.  One elected thread streams each F16 tile (rows x n_embd halves,
 // contiguous) into shared memory with cp.async.bulk (TMA bulk copy, completed
-// on an mbarrier) NSTAGE tiles ahead; all threads quantize the tile into a
-// shared-memory output buffer (4 lanes per ggml block), then the elected
-// thread writes the tile's quantized rows (contiguous in the window) back with
-// one cp.async.bulk shared->global store.  Every wait is bounded.
+// on an mbarrier) NSTAGE tiles ahead; the consumer warps quantize the tile
+// into a shared-memory output buffer (one thread per ggml block), then the
+// elected thread writes the tile's quantized rows (contiguous in the window)
+// back with one cp.async.bulk shared->global store.  An input buffer is
+// refilled as soon as its tile is consumed; its output buffer is handed back
+// to the consumers separately (ofree barrier) once the store has read it, so
+// the loads run NSTAGE-1 tiles ahead of the quantizers.  Every wait is bounded.
 //
 // permute_kernel: moves retained blocks from their old slot to their new slot
 // in place.  Each CTA owns a byte column of the slot span for one (layer, K|V)
@@ -104,8 +107,8 @@ struct TileSlot {
 };
 static_assert(sizeof(TileSlot) == 24, "TileSlot");
 
-// Shared memory: [0,128) barriers (full[NS], done[NS]); [128,384) tile slots;
-// then NS input tiles and NS output tiles.
+// Shared memory: [0,128) barriers (full[NS], done[NS], ofree[NS]); [128,384)
+// tile slots; then NS input tiles and NS output tiles.
 constexpr uint32_t kStageinHeader = 384;
 
 // ------------------------------------------------------- transform mode --
@@ -275,6 +278,7 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
+    uint64_t *ofree = done + NS;   // phase k of ofree[s]: the store of tile s + k*NS has read out[s]
     TileSlot *slot = reinterpret_cast<TileSlot *>(smem + 128);
     uint8_t *in_buf = smem + kStageinHeader;
     uint8_t *out_buf = in_buf + NS * a.tile_in_bytes;
@@ -292,6 +296,7 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&done[s], kStageinConsumerWarps);
+            mbar_init(&ofree[s], 1);
         }
         fence_mbar_init();
     }
@@ -330,7 +335,6 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
         __syncwarp();   // slot[] written by lane 0 is read by every producer lane
         issued = __shfl_sync(0xffffffffu, issued, 0);
         ended = __shfl_sync(0xffffffffu, ended ? 1 : 0, 0) != 0;
-        const uint32_t lag = a.bulk_store ? 1u : 0u;
         bool bad = false;
         for (uint32_t j = 0; j < issued; ++j) {
             const uint32_t s = j % NS;
@@ -354,11 +358,16 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
                     *reinterpret_cast<uint16_t *>(ts.dst + o) =
                         *reinterpret_cast<const uint16_t *>(ob + o);
                 __syncwarp();
+                if (lane == 0) mbar_arrive(&ofree[s]);
             }
-            if (j >= lag && lane == 0 && !ended) {
-                // the stage of tile j - lag is free once its store has read it
-                if (a.bulk_store) bulk_wait_read<1>();
-                arm_next();
+            if (lane == 0) {
+                // the consumers are done with in[s]: refill it right away; the
+                // output buffer is released separately through ofree[]
+                if (!ended) arm_next();
+                if (a.bulk_store && j >= 1) {
+                    bulk_wait_read<1>();                  // the store of tile j - 1 has read its buffer
+                    mbar_arrive(&ofree[(j - 1) % NS]);
+                }
             }
             __syncwarp();
             issued = __shfl_sync(0xffffffffu, issued, 0);
@@ -390,6 +399,11 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
         }
         const TileSlot ts = slot[s];
         if (ts.rows == 0) break;
+        // out[s] was last written for tile j - NS: its store must have read it
+        if (j >= static_cast<uint32_t>(NS) && !mbar_wait_bounded(&ofree[s], ((j / NS) - 1u) & 1u)) {
+            set_status(a.status, kErrTimeout);
+            break;
+        }
         const uint8_t *ib = in_buf + s * a.tile_in_bytes;
         uint8_t *ob = out_buf + s * a.tile_out_bytes;
         if (XF) {
