@@ -98,11 +98,17 @@ __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_h
     for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) {
         const uint32_t h = i / head_dim;
         const uint32_t d = i % head_dim;
+        // the group members' values are loaded together, then added in order
+        const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
         float qh = 0.0f;
-        for (uint32_t gi = 0; gi < g; ++gi) {
-            const uint32_t qh_i = h * g + gi;
-            if (qh_i >= n_head_q) break;
-            qh = __fadd_rn(qh, qs[static_cast<size_t>(qh_i) * head_dim + d]);
+        for (uint32_t g0 = 0; g0 < n_in; g0 += 8u) {
+            float x[8];
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k)
+                x[k] = g0 + k < n_in ? qs[static_cast<size_t>(h * g + g0 + k) * head_dim + d] : 0.0f;
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k)
+                if (g0 + k < n_in) qh = __fadd_rn(qh, x[k]);
         }
         const float v = __fmul_rn(qh, invq);
         qv[i] = v;
@@ -114,6 +120,7 @@ __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_h
     for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
         float nq = 0.0f;
         const float *v = qv_s + static_cast<size_t>(h) * head_dim;
+#pragma unroll 16
         for (uint32_t d = 0; d < head_dim; ++d) nq = __fadd_rn(nq, __fmul_rn(v[d], v[d]));
         q.nq[static_cast<size_t>(l) * n_head_kv + h] = nq;
     }
@@ -319,20 +326,46 @@ cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_
     const size_t smem = static_cast<size_t>(n_head_kv) * head_dim * sizeof(float);
     if (smem > 48u * 1024u)
         cudaFuncSetAttribute(query_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    query_prep_kernel<<<n_layer, 256, smem, stream>>>(q, n_head_kv, n_head_q, head_dim);
+    query_prep_kernel<<<n_layer, 1024, smem, stream>>>(q, n_head_kv, n_head_q, head_dim);
     return cudaGetLastError();
+}
+
+// The hardware fills an SM with as many resident CTAs as its shared memory
+// allows before it uses the next one, so a one-wave grid smaller than the
+// GPU's capacity lands unevenly (measured: busiest SM active 83K cycles, the
+// least busy 42K, of 89K).  Padding each CTA's shared memory caps residency at
+// ceil(units / SMs) and so spreads the wave over every SM.
+static size_t score_smem_for(uint32_t units, size_t smem_min) {
+    static size_t cache_smem[64] = {};
+    static uint32_t cache_units[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return smem_min;
+    if (cache_units[dev] == units && cache_smem[dev] >= smem_min) return cache_smem[dev];
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int want = static_cast<int>((units + static_cast<uint32_t>(sms) - 1u) / static_cast<uint32_t>(sms));
+    size_t smem = smem_min;
+    int occ = 0;
+    for (int it = 0; it < 512; ++it) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, score_kernel, kScoreThreads, smem) != cudaSuccess)
+            return smem_min;
+        if (occ <= want || smem >= 200u * 1024u) break;
+        smem += 256u;
+    }
+    if (occ < want) smem = smem_min;       // never cap below one wave
+    cache_units[dev] = units;
+    cache_smem[dev] = smem;
+    return smem;
 }
 
 cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
     if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
-    const size_t smem = 128u + ((a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u)) +
-                        static_cast<size_t>(kScoreStages) * kScoreChannels * kScoreBlocks * sizeof(float);
-    if (smem > 48u * 1024u) {
-        cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-    }
+    const size_t smem_min = 128u + ((a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u)) +
+                            static_cast<size_t>(kScoreStages) * kScoreChannels * kScoreBlocks * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
     dim3 grid((a.n_blocks + kScoreBlocks - 1u) / kScoreBlocks, a.n_head_kv, a.n_layers);
+    const size_t smem = score_smem_for(grid.x * grid.y * grid.z, smem_min);
     score_kernel<<<grid, kScoreThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
