@@ -14,10 +14,9 @@ constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 produ
 constexpr int kStageinStages = 3;
 constexpr int kPermuteThreads = 256;
 constexpr int kScoreBlocks = 64;                   // blocks per scorer CTA (one thread each)
-constexpr int kScoreChannels = 16;                 // channel rows per pipeline stage
-constexpr int kScoreStages = 3;
+constexpr int kScoreBatch = 64;                    // channel loads in flight per scorer thread
 constexpr uint32_t kSumGroup = 64;                 // blocks per summary tile (== kScoreBlocks)
-constexpr int kScoreThreads = kScoreBlocks + 32;   // + 1 TMA producer warp
+constexpr int kScoreThreads = kScoreBlocks;        // one thread per block
 constexpr int kSelectThreads = 1024;
 constexpr int kDiffThreads = 1024;
 
@@ -221,9 +220,8 @@ struct ScoreArgs {
     uint32_t ldt;
     float *rbuf;           // [layer][n_head_kv][ldb] per-head results
     uint32_t *status;
-    // combine (only when n_layers == all layers of the session)
+    // combine_kernel: scores too (only when n_layers == all layers of the session)
     int combine;
-    uint32_t *counters;    // [ceil(ldb/kScoreBlocks)]
     double *scores;        // [ldb]
 };
 

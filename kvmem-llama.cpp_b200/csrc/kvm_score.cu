@@ -6,16 +6,17 @@
 //     r = dot / (sqrt(nq) * sqrt(nk) + 1e-6f)
 //   per (block, layer): layer = sum of r over heads in order (double), term = layer / H_kv
 //   per block: score = (sum of terms over layers with a query, in layer order) / n_active
-// The summaries are stored channel-major ([layer][channel][block]) so that a
-// warp of threads, one per block, reads 128 contiguous bytes per channel while
-// each thread keeps the reference's sequential channel order -- coalesced
-// streaming without changing the float rounding of a single block's score.
-// A tree (warp-shuffle) reduction over channels would round differently, and
-// a near-tie at the top-k boundary could then flip the selection.
+// The summaries are stored channel-major in 64-block tiles
+// ([layer][64-block group][channel][64]) so that a warp of threads, one per
+// block, reads 128 contiguous bytes per channel while each thread keeps the
+// reference's sequential channel order -- coalesced streaming without
+// changing the float rounding of a single block's score.  A tree
+// (warp-shuffle) reduction over channels would round differently, and a
+// near-tie at the top-k boundary could then flip the selection.
 //
-// The layer/head combine is done by the last CTA of each block group to
-// finish (threadfence + atomic counter, no waiting), so one launch produces
-// the final scores.
+// The head/layer combine is a second, per-block kernel.  Doing it in the last
+// CTA of each block group (threadfence + atomic counter) put a serial tail of
+// L2 round trips after the last unit: 17 us of a 53 us scorer.
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
@@ -129,20 +130,15 @@ __global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_h
 // ---------------------------------------------------------------- scorer --
 
 // One CTA = (group of kScoreBlocks blocks, one KV head, one layer): D*256
-// contiguous bytes of the tiled summary tensor.  A producer warp streams them
-// in kScoreChannels-row chunks (one cp.async.bulk each) through a
-// kScoreStages-deep ring; each consumer thread owns one block and walks the
+// contiguous bytes of the tiled summary tensor.  Each thread owns one block
+// and keeps kScoreBatch coalesced channel loads in flight, then walks the
 // channels in the reference's order.  Small units (2048 at config 2) and
 // small CTAs (~14 per SM) make one balanced wave.  Per-head results go to rbuf; the last CTA of a
 // block range (over heads x layers) forms the per-layer terms in head order
 // and, when combining, the final scores in layer order.
 __global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + kScoreStages;
-    float *q_s = reinterpret_cast<float *>(smem + 128);
-    float *ring = reinterpret_cast<float *>(smem + 128 + ((a.head_dim * sizeof(float) + 127u) & ~127u));
-    __shared__ uint32_t s_last;
+    float *q_s = reinterpret_cast<float *>(smem);
     const uint32_t H = a.n_head_kv;
     const uint32_t D = a.head_dim;
     const uint32_t ldb = a.sum.ldb;
@@ -153,69 +149,35 @@ __global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a) {
     const uint32_t nb = min(static_cast<uint32_t>(kScoreBlocks), a.n_blocks - b0);
     const bool active = a.q_count[l] > 0;
     const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-    if (tid == 0) {
-        for (int s = 0; s < kScoreStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kScoreBlocks / 32);
-        }
-        fence_mbar_init();
-    }
     for (uint32_t i = tid; i < D; i += blockDim.x)
         q_s[i] = active ? a.qv[(static_cast<size_t>(l) * H + h) * D + i] : 0.0f;
     __syncthreads();
-    const uint32_t n_chunks = active ? (D + kScoreChannels - 1) / kScoreChannels : 0u;
-    bool ok = true;
-    if (warp == kScoreBlocks / 32) {
-        // ------------------------------------------------------- producer
-        if (lane == 0) {
-            // rows h*D .. h*D+D-1 of tile (l, g): contiguous, kSumGroup floats each
-            const float *col0 = a.sum.sum_t + sum_index(a.sum, l, h * D, b0);
-            for (uint32_t k = 0; k < n_chunks; ++k) {
-                const uint32_t s = k % kScoreStages;
-                if (k >= static_cast<uint32_t>(kScoreStages) &&
-                    !mbar_wait_bounded(&empty[s], ((k / kScoreStages) - 1u) & 1u)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t rows = min(static_cast<uint32_t>(kScoreChannels), D - k * kScoreChannels);
-                const uint32_t bytes = rows * kSumGroup * 4u;
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(ring + s * kScoreChannels * kScoreBlocks,
-                         col0 + static_cast<size_t>(k) * kScoreChannels * kSumGroup, bytes, &full[s]);
-            }
-            if (!ok) set_status(a.status, kErrTimeout);
-        }
-    } else {
-        // ------------------------------------------------------ consumers
+    {
+        // One thread per block.  Channel c of the unit is the 256-byte row
+        // h*D + c of tile (l, g): a warp's 32 loads of one channel are one
+        // 128-byte line.  kScoreBatch channels are loaded at once, then added
+        // in the reference's channel order.
         const uint32_t b = b0 + tid;
-        const float inv = (active && static_cast<uint32_t>(tid) < nb)
-                              ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
+        const bool mine = active && static_cast<uint32_t>(tid) < nb;
+        const float inv = mine ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
         float dot = 0.0f;
         float nk = 0.0f;
-        for (uint32_t k = 0; k < n_chunks; ++k) {
-            const uint32_t s = k % kScoreStages;
-            if (!mbar_wait_bounded(&full[s], (k / kScoreStages) & 1u)) {
-                set_status(a.status, kErrTimeout);
-                ok = false;
-                break;
-            }
-            const uint32_t rows = min(static_cast<uint32_t>(kScoreChannels), D - k * kScoreChannels);
-            if (inv != 0.0f) {
-                const float *col = ring + s * kScoreChannels * kScoreBlocks + tid;
-                const float *q = q_s + k * kScoreChannels;
+        if (inv != 0.0f) {
+            const float *col = a.sum.sum_t + sum_index(a.sum, l, h * D, b0) + tid;
+            for (uint32_t c0 = 0; c0 < D; c0 += kScoreBatch) {
+                float x[kScoreBatch];
 #pragma unroll
-                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreChannels); ++r) {
-                    if (r < rows) {
-                        const float mk = __fmul_rn(col[r * kScoreBlocks], inv);
-                        dot = __fadd_rn(dot, __fmul_rn(q[r], mk));
+                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreBatch); ++r)
+                    x[r] = c0 + r < D ? __ldcs(col + static_cast<size_t>(c0 + r) * kSumGroup) : 0.0f;
+#pragma unroll
+                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreBatch); ++r) {
+                    if (c0 + r < D) {
+                        const float mk = __fmul_rn(x[r], inv);
+                        dot = __fadd_rn(dot, __fmul_rn(q_s[c0 + r], mk));
                         nk = __fadd_rn(nk, __fmul_rn(mk, mk));
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
         }
         if (static_cast<uint32_t>(tid) < nb) {
             float rr = 0.0f;
@@ -227,59 +189,71 @@ __global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a) {
             a.rbuf[(static_cast<size_t>(l) * H + h) * ldb + b] = rr;
         }
     }
-    // ---- last CTA of this block group combines heads (and layers)
-    if (warp < kScoreBlocks / 32 && static_cast<uint32_t>(tid) < nb) __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t want = gridDim.y * gridDim.z - 1u;
-        s_last = atomicAdd(&a.counters[g], 1u) == want ? 1u : 0u;
+}
+
+// x / d in double; a power-of-two d divides exactly by scaling, so the
+// product with its reciprocal is the same value as the quotient.
+__device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
+    if ((d & (d - 1u)) == 0u) return __dmul_rn(x, 1.0 / static_cast<double>(d));
+    return __ddiv_rn(x, static_cast<double>(d));
+}
+
+// Combine of the scorer's per-head results (llama-memory-kvmem.cpp:2881-2912):
+// the layer term is the sum over heads in head order (double) divided by
+// n_head_kv; the score is the sum of the active layers' terms in layer order
+// divided by their number, 0 for a block without statistics.  A CTA covers
+// kCombineBlocks blocks x kCombineLanes layer lanes: each thread forms the
+// terms of its layers (their head values loaded together, coalesced across
+// the blocks), parks them in shared memory, and one thread per block then
+// adds them in layer order.
+constexpr uint32_t kCombineBlocks = 32;
+constexpr uint32_t kCombineLanes = 8;
+
+__global__ void __launch_bounds__(kCombineBlocks * kCombineLanes) combine_kernel(ScoreArgs a) {
+    extern __shared__ double term_s[];                 // [n_layers][kCombineBlocks]
+    const uint32_t tb = threadIdx.x % kCombineBlocks;
+    const uint32_t ly = threadIdx.x / kCombineBlocks;
+    const uint32_t bb = blockIdx.x * kCombineBlocks + tb;
+    const uint32_t H = a.n_head_kv;
+    const uint32_t ldb = a.sum.ldb;
+    const bool mine = bb < a.n_blocks;
+    if (mine) {
+        for (uint32_t li = ly; li < a.n_layers; li += kCombineLanes) {
+            const uint32_t ll = a.layer0 + li;
+            const float *rb = a.rbuf + static_cast<size_t>(ll) * H * ldb + bb;
+            double term = 0.0;
+            if (a.q_count[ll] > 0) {
+                double layer = 0.0;
+                for (uint32_t h0 = 0; h0 < H; h0 += 8u) {
+                    float x[8];
+#pragma unroll
+                    for (uint32_t k = 0; k < 8u; ++k)
+                        x[k] = h0 + k < H ? rb[static_cast<size_t>(h0 + k) * ldb] : 0.0f;
+#pragma unroll
+                    for (uint32_t k = 0; k < 8u; ++k)
+                        if (h0 + k < H) layer = __dadd_rn(layer, static_cast<double>(x[k]));
+                }
+                term = div_exact_pow2(layer, H > 1u ? H : 1u);
+            }
+            a.terms[static_cast<size_t>(ll) * a.ldt + bb] = term;
+            term_s[li * kCombineBlocks + tb] = term;
+        }
     }
+    if (!a.combine) return;
     __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // Stage the group's per-head results a layer chunk at a time through the
-    // (now idle) ring with coalesced 256-byte row loads by every thread, then
-    // let each block's thread add them in head order and layer order.
-    const uint32_t ring_floats = kScoreStages * kScoreChannels * kScoreBlocks;
-    const uint32_t chunk = max(1u, ring_floats / (H * kScoreBlocks));
-    const uint32_t bb = b0 + tid;
-    const bool mine = tid < kScoreBlocks && static_cast<uint32_t>(tid) < nb;
-    const double hk = static_cast<double>(H > 1u ? H : 1u);
+    if (ly != 0 || !mine) return;
     double acc = 0.0;
     uint32_t nlay = 0;
-    for (uint32_t c0 = a.layer0; c0 < a.layer0 + a.n_layers; c0 += chunk) {
-        const uint32_t nl = min(chunk, a.layer0 + a.n_layers - c0);
-        const uint32_t nvals = nl * H * kScoreBlocks;
-        __syncthreads();
-        for (uint32_t i = tid; i < nvals; i += blockDim.x) {
-            const uint32_t row = i / kScoreBlocks;            // (layer - c0) * H + head
-            const uint32_t col = i % kScoreBlocks;
-            ring[i] = __ldcg(a.rbuf + (static_cast<size_t>(c0) * H + row) * ldb + b0 + col);
-        }
-        __syncthreads();
-        if (mine) {
-            for (uint32_t li = 0; li < nl; ++li) {
-                const uint32_t ll = c0 + li;
-                double term = 0.0;
-                if (a.q_count[ll] > 0) {
-                    double layer = 0.0;
-                    for (uint32_t hh = 0; hh < H; ++hh)
-                        layer = __dadd_rn(layer, static_cast<double>(ring[(li * H + hh) * kScoreBlocks + tid]));
-                    term = __ddiv_rn(layer, hk);
-                    acc = __dadd_rn(acc, term);
-                    ++nlay;
-                }
-                a.terms[static_cast<size_t>(ll) * a.ldt + bb] = term;
-            }
+    for (uint32_t li = 0; li < a.n_layers; ++li) {
+        if (a.q_count[a.layer0 + li] > 0) {
+            acc = __dadd_rn(acc, term_s[li * kCombineBlocks + tb]);
+            ++nlay;
         }
     }
-    if (mine && a.combine) {
-        bool has = false;
-        for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
-            has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
-        a.scores[bb] = (has && nlay) ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
-    }
-    if (tid == 0) a.counters[g] = 0u;
+    bool has = false;
+    for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
+        has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
+    a.scores[bb] = (has && nlay) ? div_exact_pow2(acc, nlay) : 0.0;
 }
 
 __global__ void reduce_terms_kernel(const double *__restrict__ terms, uint32_t n_layers,
@@ -360,13 +334,22 @@ static size_t score_smem_for(uint32_t units, size_t smem_min) {
 
 cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
     if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
-    const size_t smem_min = 128u + ((a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u)) +
-                            static_cast<size_t>(kScoreStages) * kScoreChannels * kScoreBlocks * sizeof(float);
+    const size_t smem_min = (a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u);
     cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     dim3 grid((a.n_blocks + kScoreBlocks - 1u) / kScoreBlocks, a.n_head_kv, a.n_layers);
     const size_t smem = score_smem_for(grid.x * grid.y * grid.z, smem_min);
     score_kernel<<<grid, kScoreThreads, smem, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t csmem = static_cast<size_t>(a.n_layers) * kCombineBlocks * sizeof(double);
+    if (csmem > 48u * 1024u) {
+        e = cudaFuncSetAttribute(combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(csmem));
+        if (e != cudaSuccess) return e;
+    }
+    combine_kernel<<<(a.n_blocks + kCombineBlocks - 1u) / kCombineBlocks, kCombineBlocks * kCombineLanes,
+                     csmem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -67,7 +67,6 @@ struct kvm_session {
     float *d_rbuf = nullptr;           // per-head scorer results [L][H][ldb]
     double *d_scores = nullptr;
     double *d_acc = nullptr;
-    uint32_t *d_counters = nullptr;
     BlockTable bt{};
     PlanArrays plan{};
     uint32_t *d_mandatory = nullptr;
@@ -557,7 +556,6 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->d_rbuf), sizeof(float) * L * c.n_head_kv * ldb},
         {reinterpret_cast<void **>(&s->d_scores), sizeof(double) * ldb},
         {reinterpret_cast<void **>(&s->d_acc), sizeof(double) * ldb},
-        {reinterpret_cast<void **>(&s->d_counters), sizeof(uint32_t) * n_groups * 2},
         {reinterpret_cast<void **>(&s->bt.n_tokens), sizeof(uint32_t) * nb},
         {reinterpret_cast<void **>(&s->bt.tier), nb},
         {reinterpret_cast<void **>(&s->bt.gpu_slot), sizeof(int32_t) * nb},
@@ -1082,7 +1080,6 @@ static ScoreArgs score_args(kvm_session *s) {
     a.ldt = s->sum.ldb;
     a.rbuf = s->d_rbuf;
     a.status = s->d_status;
-    a.counters = s->d_counters;
     a.scores = s->d_scores;
     return a;
 }

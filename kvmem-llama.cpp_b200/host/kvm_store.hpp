@@ -6,7 +6,8 @@
 // reselection path, so an adapter written against kvmem::KvMemStore (such as
 // llama_memory_kvmem, src/adapter/llama-memory-kvmem.cpp) can swap the type:
 //   register_append, block_count, total_tokens, budget_blocks,
-//   set_retrieval_scores, pick_topk_blocks(mandatory), set_selection(ids),
+//   set_retrieval_scores, pick_topk_blocks(mandatory), pick_semantic_groups,
+//   set_selection(ids),
 //   set_block_tier, set_block_gpu_slot, clear_working_set.
 // The block table lives on the device: pick_topk_blocks and set_selection run
 // the selector / diff kernels and read their results back (one bounded wait
@@ -20,6 +21,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "kvm.h"
@@ -132,6 +134,30 @@ public:
 
     std::vector<uint32_t> pick_topk_blocks(const std::vector<uint32_t> &mandatory = {}) {
         check(kvm_select(s_, stream_, mandatory.data(), static_cast<uint32_t>(mandatory.size())));
+        std::vector<uint32_t> sel(std::max<uint32_t>(1u, block_count()));
+        kvm_plan p{};
+        p.capacity = static_cast<uint32_t>(sel.size());
+        p.selected = sel.data();
+        check(kvm_get_plan(s_, stream_, &p, timeout_ms_));
+        sel.resize(p.n_selected);
+        return sel;
+    }
+
+    // KvMemStore::pick_semantic_groups (kvmem_store.cpp:625-756): whole
+    // variable-length groups of half-open token spans under the block budget.
+    std::vector<uint32_t> pick_semantic_groups(const std::vector<std::pair<uint32_t, uint32_t>> &groups,
+                                               const std::vector<double> &group_scores,
+                                               const std::vector<uint32_t> &mandatory_blocks = {}) {
+        if (groups.size() != group_scores.size())
+            throw std::runtime_error("KVMem semantic group spans/scores size mismatch");
+        std::vector<uint32_t> spans(2 * groups.size());
+        for (size_t i = 0; i < groups.size(); ++i) {
+            spans[2 * i] = groups[i].first;
+            spans[2 * i + 1] = groups[i].second;
+        }
+        check(kvm_select_groups(s_, stream_, spans.data(), group_scores.data(),
+                                static_cast<uint32_t>(groups.size()), mandatory_blocks.data(),
+                                static_cast<uint32_t>(mandatory_blocks.size())));
         std::vector<uint32_t> sel(std::max<uint32_t>(1u, block_count()));
         kvm_plan p{};
         p.capacity = static_cast<uint32_t>(sel.size());
