@@ -152,6 +152,46 @@ static void test_topk_all_fit_and_empty() {
     CHECK(plan.total_window_tokens == 0);
 }
 
+// kvmem_store_test.cpp:1017-1053
+static void test_round_groups_are_selected_whole() {
+    KvMemStore s(base(32, 8, 1, 1));
+    s.register_append(32 * 20);
+    const std::vector<std::pair<uint32_t, uint32_t>> groups{
+        {32, 32 * 4}, {32 * 4 + 3, 32 * 8 - 5}, {32 * 8, 32 * 11}, {32 * 12, 32 * 14}};
+    const auto selected = s.pick_semantic_groups(groups, {1.0, 10.0, 9.0, 2.0});
+    CHECK(selected.size() <= 8);
+    CHECK(has(selected, 0) && has(selected, 19));
+    for (uint32_t id = 4; id <= 7; ++id) CHECK(has(selected, id));
+    for (uint32_t id = 8; id <= 10; ++id) CHECK(!has(selected, id));
+}
+
+// kvmem_store_test.cpp:1055-1076
+static void test_round_groups_charge_shared_boundary_once() {
+    KvMemStore s(base(64, 4, 0, 0));
+    s.register_append(64 * 8);
+    const std::vector<std::pair<uint32_t, uint32_t>> groups{{64, 64 * 2 + 10}, {64 * 2 + 10, 64 * 4}};
+    const auto selected = s.pick_semantic_groups(groups, {2.0, 1.0}, {7});
+    CHECK(selected.size() == 4);
+    for (uint32_t id : {1u, 2u, 3u, 7u}) CHECK(has(selected, id));
+}
+
+// kvmem_store_test.cpp:479-503 (the semantic half)
+static void test_semantic_mandatory_overflow_trims_newest() {
+    KvMemStore s(base(32, 4, 1, 2));
+    s.register_append(32 * 10);
+    const auto sem = s.pick_semantic_groups({{32 * 5, 32 * 7}}, {1.0}, {1, 2, 3, 4});
+    CHECK(sem.size() == 4);
+    for (uint32_t id : {0u, 2u, 3u, 4u}) CHECK(has(sem, id));
+    CHECK(!has(sem, 1));
+    bool threw = false;
+    try {
+        s.pick_semantic_groups({{0, 32}}, {});
+    } catch (const std::runtime_error &) {
+        threw = true;
+    }
+    CHECK(threw);
+}
+
 // A shape the device path cannot serve is rejected with std::invalid_argument,
 // the exception type the reference uses for bad configurations.
 static void test_invalid_config_throws() {
@@ -174,6 +214,9 @@ int main() {
     test_mandatory_overlap_deduplicates_and_recent_is_best_effort();
     test_mandatory_hard_union_overflow_trims_newest();
     test_topk_all_fit_and_empty();
+    test_round_groups_are_selected_whole();
+    test_round_groups_charge_shared_boundary_once();
+    test_semantic_mandatory_overflow_trims_newest();
     test_invalid_config_throws();
     if (g_fail) {
         std::printf("%d check(s) failed\n", g_fail);
