@@ -27,7 +27,7 @@ namespace kvm {
 
 __global__ void __launch_bounds__(kDiffThreads) diff_kernel(DiffArgs a) {
     extern __shared__ uint8_t fl[];
-    __shared__ uint32_t scratch[40];
+    __shared__ uint4 scratch4[kDiffThreads / 32 + 1];
     const uint32_t n = a.n_blocks;
     uint8_t *now = fl;
     uint8_t *was = fl + (n ? n : 1u);
@@ -59,9 +59,11 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(DiffArgs a) {
         overlap += (w && now[i]) ? 1u : 0u;
         n_out += (bt.tier[i] == KVM_TIER_GPU && (!now[i] || ffr)) ? 1u : 0u;
     }
-    uint32_t tot_out;
-    uint32_t off_out = block_exclusive_scan<kDiffThreads>(n_out, scratch, &tot_out);
-    const uint32_t tot_overlap = block_sum<kDiffThreads>(overlap, scratch);
+    uint4 tot1;
+    const uint4 off1 = block_exclusive_scan4<kDiffThreads>(make_uint4(n_out, overlap, 0u, 0u), scratch4, &tot1);
+    uint32_t off_out = off1.x;
+    const uint32_t tot_out = tot1.x;
+    const uint32_t tot_overlap = tot1.y;
     for (uint32_t i = lo; i < hi; ++i) {
         if (bt.tier[i] == KVM_TIER_GPU && (!now[i] || ffr)) {
             a.plan.stage_out[off_out++] = i;
@@ -83,11 +85,10 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(DiffArgs a) {
         if (resident) n_mv += bt.gpu_slot[id] != static_cast<int32_t>(s) ? 1u : 0u;
         else ++n_cold;
     }
-    uint32_t tot_tok, tot_in, tot_mv, tot_cold;
-    uint32_t wpos = block_exclusive_scan<kDiffThreads>(tok, scratch, &tot_tok);
-    uint32_t off_in = block_exclusive_scan<kDiffThreads>(n_in, scratch, &tot_in);
-    uint32_t off_mv = block_exclusive_scan<kDiffThreads>(n_mv, scratch, &tot_mv);
-    uint32_t off_cold = block_exclusive_scan<kDiffThreads>(n_cold, scratch, &tot_cold);
+    uint4 tot2;
+    const uint4 off2 = block_exclusive_scan4<kDiffThreads>(make_uint4(tok, n_in, n_mv, n_cold), scratch4, &tot2);
+    uint32_t wpos = off2.x, off_in = off2.y, off_mv = off2.z, off_cold = off2.w;
+    const uint32_t tot_tok = tot2.x, tot_in = tot2.y, tot_mv = tot2.z, tot_cold = tot2.w;
     uint32_t stable = 0, moved = 0, reused = 0, err = 0;
     for (uint32_t s = slo; s < shi; ++s) {
         const uint32_t id = sel[s];
@@ -158,10 +159,9 @@ __global__ void __launch_bounds__(kDiffThreads) diff_kernel(DiffArgs a) {
         bt.baked_pos[id] = static_cast<int64_t>(wpos);
         wpos += ntok;
     }
-    const uint32_t tot_stable = block_sum<kDiffThreads>(stable, scratch);
-    const uint32_t tot_moved = block_sum<kDiffThreads>(moved, scratch);
-    const uint32_t tot_reused = block_sum<kDiffThreads>(reused, scratch);
-    const uint32_t tot_err = block_sum<kDiffThreads>(err, scratch);
+    uint4 tot3;
+    (void)block_exclusive_scan4<kDiffThreads>(make_uint4(stable, moved, reused, err), scratch4, &tot3);
+    const uint32_t tot_stable = tot3.x, tot_moved = tot3.y, tot_reused = tot3.z, tot_err = tot3.w;
     // every selected block's old slot was read above; now install the layout
     for (uint32_t i = lo; i < hi; ++i) {
         if (now[i]) continue;

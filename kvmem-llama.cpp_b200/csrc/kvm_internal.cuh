@@ -206,6 +206,47 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *s
     return warp_prefix + x - v;
 }
 
+// Four independent exclusive prefix sums in one pass (same contract as
+// block_exclusive_scan, component-wise).  `scratch` holds >= NT/32 + 1 uint4.
+__device__ __forceinline__ uint4 u4_add(uint4 a, uint4 b) {
+    return make_uint4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__device__ __forceinline__ uint4 u4_shfl_up(uint4 v, int o) {
+    return make_uint4(__shfl_up_sync(0xffffffffu, v.x, o), __shfl_up_sync(0xffffffffu, v.y, o),
+                      __shfl_up_sync(0xffffffffu, v.z, o), __shfl_up_sync(0xffffffffu, v.w, o));
+}
+
+template <int NT>
+__device__ __forceinline__ uint4 block_exclusive_scan4(uint4 v, uint4 *scratch, uint4 *total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    uint4 x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint4 y = u4_shfl_up(x, o);
+        if (lane >= o) x = u4_add(x, y);
+    }
+    if (lane == 31) scratch[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        constexpr int NW = NT / 32;
+        uint4 w = lane < NW ? scratch[lane] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint4 y = u4_shfl_up(w, o);
+            if (lane >= o) w = u4_add(w, y);
+        }
+        if (lane < NW) scratch[lane] = w;
+        if (lane == NW - 1) scratch[NW] = w;
+    }
+    __syncthreads();
+    const uint4 wp = warp > 0 ? scratch[warp - 1] : make_uint4(0u, 0u, 0u, 0u);
+    *total = scratch[NT / 32];
+    __syncthreads();
+    return make_uint4(wp.x + x.x - v.x, wp.y + x.y - v.y, wp.z + x.z - v.z, wp.w + x.w - v.w);
+}
+
 // Block-wide sum of one value per thread (all threads get the result).
 template <int NT>
 __device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t *scratch) {

@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
     __shared__ uint32_t s_remaining;
     __shared__ uint64_t s_prefix;
     __shared__ uint64_t s_mask;
+    __shared__ uint32_t s_done;
     const uint32_t n = a.n_blocks;
     const uint32_t budget = a.budget;
     const uint32_t tid = threadIdx.x;
@@ -93,21 +94,52 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
             if (!kept[i]) kept[i] = 2;
         __syncthreads();
     } else if (need > 0) {
+        // Each thread owns the contiguous ids [lo, hi); up to kKeysCached keys
+        // stay in registers across the passes.
+        constexpr uint32_t kKeysCached = 8;
+        const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
+        const uint32_t lo = min(n, tid * per);
+        const uint32_t hi = min(n, lo + per);
+        const bool cached = per <= kKeysCached;
+        uint64_t kc[kKeysCached];
+        uint32_t live = 0;                        // bit j: id lo + j is a candidate
+#pragma unroll
+        for (uint32_t j = 0; j < kKeysCached; ++j) {
+            kc[j] = 0ull;
+            if (cached && lo + j < hi && !kept[lo + j]) {
+                kc[j] = score_key(a.scores[lo + j]);
+                live |= 1u << j;
+            }
+        }
+        auto key_of = [&](uint32_t j) -> uint64_t {
+            if (cached) {
+                uint64_t k = 0ull;
+#pragma unroll
+                for (uint32_t q = 0; q < kKeysCached; ++q)
+                    if (q == j) k = kc[q];
+                return k;
+            }
+            return score_key(a.scores[lo + j]);
+        };
+        auto is_live = [&](uint32_t j) -> bool {
+            return cached ? ((live >> j) & 1u) != 0u : !kept[lo + j];
+        };
         if (tid == 0) {
             s_prefix = 0ull;
             s_mask = 0ull;
             s_remaining = need;
+            s_done = 0u;
         }
         __syncthreads();
-        for (int pass = 0; pass < 8; ++pass) {
+        for (int pass = 0; pass < 8 && !s_done; ++pass) {
             const int shift = 56 - 8 * pass;
             for (uint32_t i = tid; i < 256u; i += kSelectThreads) hist[i] = 0u;
             __syncthreads();
             const uint64_t prefix = s_prefix;
             const uint64_t mask = s_mask;
-            for (uint32_t i = tid; i < n; i += kSelectThreads) {
-                if (kept[i]) continue;
-                const uint64_t k = score_key(a.scores[i]);
+            for (uint32_t j = 0; j < hi - lo; ++j) {
+                if (!is_live(j)) continue;
+                const uint64_t k = key_of(j);
                 if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
             }
             __syncthreads();
@@ -124,8 +156,8 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
                     if (lane >= static_cast<uint32_t>(o)) cum += y;
                 }
                 const uint32_t ex = cum - local;
-                const bool mine = ex < rem && rem <= cum;
-                if (mine) {
+                const bool hit = ex < rem && rem <= cum;
+                if (hit) {
                     uint32_t acc = ex;
                     for (int j = 0; j < 8; ++j) {
                         const uint32_t bin = 255u - 8u * lane - j;
@@ -134,6 +166,9 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
                             s_remaining = rem - acc;
                             s_prefix = prefix | (static_cast<uint64_t>(bin) << shift);
                             s_mask = mask | (255ull << shift);
+                            // the whole bin is needed: every candidate with this
+                            // prefix is taken, no further digit matters
+                            if (acc + hc == rem) s_done = 1u;
                             break;
                         }
                         acc += hc;
@@ -142,28 +177,26 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
             }
             __syncthreads();
         }
-        // take every candidate above the threshold key, and the `rem`
+        // take every candidate above the threshold prefix, and the `rem`
         // highest-id candidates equal to it
         const uint64_t thr = s_prefix;
+        const uint64_t msk = s_mask;
         const uint32_t rem = s_remaining;
-        const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
-        const uint32_t lo = min(n, tid * per);
-        const uint32_t hi = min(n, lo + per);
         uint32_t eq = 0;
-        for (uint32_t i = lo; i < hi; ++i)
-            if (!kept[i] && score_key(a.scores[i]) == thr) ++eq;
+        for (uint32_t j = 0; j < hi - lo; ++j)
+            if (is_live(j) && (key_of(j) & msk) == thr) ++eq;
         uint32_t total_eq;
         const uint32_t before = block_exclusive_scan<kSelectThreads>(eq, scratch, &total_eq);
         uint32_t seen = before;   // equal candidates with id < i, running
-        for (uint32_t i = lo; i < hi; ++i) {
-            if (kept[i]) continue;
-            const uint64_t k = score_key(a.scores[i]);
+        for (uint32_t j = 0; j < hi - lo; ++j) {
+            if (!is_live(j)) continue;
+            const uint64_t k = key_of(j) & msk;
             if (k > thr) {
-                kept[i] = 2;
+                kept[lo + j] = 2;
             } else if (k == thr) {
                 ++seen;
                 const uint32_t above = total_eq - seen;   // equal candidates with id > i
-                if (above < rem) kept[i] = 2;
+                if (above < rem) kept[lo + j] = 2;
             }
         }
         __syncthreads();

@@ -541,8 +541,6 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
     // one allocation for everything small (256-byte aligned sub-buffers)
     struct Item { void **p; size_t bytes; };
     const size_t nb = c.max_blocks;
-    const uint32_t bpc = 32u;
-    const size_t n_groups = (ldb + bpc - 1u) / bpc;
     const size_t stage_cap = std::min<size_t>(nb, 1024);
     s->stage_sums_cap = stage_cap;
     std::vector<Item> items = {
