@@ -117,6 +117,30 @@ typedef struct kvm_source {
 } kvm_source;
 
 /*
+ * Packed (already quantized) K/V rows of the stored history: what the
+ * reference's RawKvStore keeps after the harvest (write_layer_k_gpu /
+ * write_layer_v_gpu, fed by harvest_gpu_v) and what kvm_stageout writes.  The
+ * n_tokens rows of block b, layer l are contiguous, row_bytes_k apart, at
+ *     k + l*k_layer_stride + b*k_block_stride
+ * (V alike with the v_ strides and row_bytes_v).  A kvm_stageout destination
+ * whose ids were 0, 1, 2, ... is such a source with
+ *     k = dst, v = dst + block_tokens*row_bytes_k,
+ *     k_layer_stride = v_layer_stride = block_tokens*(row_bytes_k + row_bytes_v),
+ *     k_block_stride = v_block_stride = kvm_stageout_item_bytes(s).
+ * `location` as in kvm_source.
+ */
+typedef struct kvm_packed_source {
+    const void *k;
+    const void *v;
+    uint64_t k_layer_stride;
+    uint64_t k_block_stride;
+    uint64_t v_layer_stride;
+    uint64_t v_block_stride;
+    int32_t  location;
+    int32_t  reserved0;
+} kvm_packed_source;
+
+/*
  * The bounded window (llama.cpp KV cache tensors, owned by the caller).
  * d_k[l] / d_v[l] are device base pointers of layer l's K / V cache; token t
  * of slot s lives at base + (s*block_tokens + t) * ggml_row_size(type, E).
@@ -404,6 +428,16 @@ kvm_status kvm_stageout(kvm_session *s, kvm_stream stream, const uint32_t *ids, 
                         const kvm_window *win, void *dst, uint8_t *resident);
 /* Bytes one block occupies in a kvm_stageout destination. */
 uint64_t kvm_stageout_item_bytes(const kvm_session *s);
+
+/* kvm_stagein from packed rows, the reference's stage-in as it runs today
+ * (write_block_to_gpu -> kvmem_stagein_enqueue_v / kvmem_stagein_flush,
+ * llama-memory-kvmem.cpp:2726-2791, llama-kvmem-stagein.cu:632-753, 820-840):
+ * the retained blocks are moved to their new slots, then the cold blocks' rows
+ * are copied into theirs unchanged (no quantization: they are already in the
+ * window's types).  A host source goes through the HBM staging ring, each
+ * chunk's H2D overlapping the previous chunk's copy. */
+kvm_status kvm_stagein_packed(kvm_session *s, kvm_stream stream, const kvm_packed_source *src,
+                              const kvm_window *win);
 
 /* score -> select -> diff -> stage-in in one call. */
 kvm_status kvm_step(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,

@@ -92,6 +92,36 @@ struct StageoutArgs {
 
 cudaError_t launch_stageout(const StageoutArgs &a, cudaStream_t stream);
 
+// stage-in of packed rows: cold items [item0, item0 + n) of cold_block / cold_to
+struct PackedInArgs {
+    const uint32_t *cold_block;
+    const int32_t *cold_to;
+    const uint32_t *n_items_dev;   // device count (NULL: use n_items_host)
+    uint32_t n_items_host;
+    uint32_t item0;
+    uint32_t max_items;
+    uint32_t src_by_item;          // 1: source index = item - item0 (staging ring)
+    const uint8_t *src_k;
+    const uint8_t *src_v;
+    uint64_t k_layer_stride;
+    uint64_t k_block_stride;
+    uint64_t v_layer_stride;
+    uint64_t v_block_stride;
+    const uint32_t *n_tokens;
+    uint32_t max_blocks;
+    uint32_t n_slots;
+    uint32_t n_layer;
+    uint32_t block_tokens;
+    uint8_t *const *win_k;
+    uint8_t *const *win_v;
+    uint32_t row_bytes_k;
+    uint32_t row_bytes_v;
+    uint32_t bulk;                 // 1: every address and size 16-byte aligned
+    uint32_t *status;
+};
+
+cudaError_t launch_packed_stagein(const PackedInArgs &a, cudaStream_t stream);
+
 // -------------------------------------------------------------- permute --
 struct PermuteArgs {
     const uint32_t *n_moves_dev;

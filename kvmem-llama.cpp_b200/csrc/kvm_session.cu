@@ -309,13 +309,8 @@ kvm_status source_check(kvm_session *s, const kvm_source *src) {
     return KVM_OK;
 }
 
-// Stage-in of cold blocks from pinned host memory: read the cold list back,
-// then per chunk of blocks copy the F16 spans into an HBM ring slot on the
-// copy stream and quantize that slot on `st` once its copy is done.
-kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *src) {
-    const uint32_t L = s->cfg.n_layer;
-    const uint32_t T = s->cfg.block_tokens;
-    // read back the header and the cold list
+// The plan's cold list on the host (one bounded wait for the header).
+kvm_status read_cold_list(kvm_session *s, cudaStream_t st, std::vector<uint32_t> &cold) {
     cudaEvent_t ev_ready = s->ev[5];
     PlanHeader *hh = reinterpret_cast<PlanHeader *>(s->h_plan);
     KVM_CUDA(s, cudaMemcpyAsync(hh, s->plan.hdr, sizeof(PlanHeader), cudaMemcpyDeviceToHost, st), "hdr read");
@@ -323,10 +318,118 @@ kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *
     kvm_status r = wait_event(s, ev_ready, 30000);
     if (r != KVM_OK) return r;
     const uint32_t n_cold = std::min(hh->n_cold, s->max_blocks);
+    cold.resize(n_cold);
+    if (n_cold)
+        KVM_CUDA(s, cudaMemcpy(cold.data(), s->plan.cold_block, n_cold * sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost), "cold read");
+    return KVM_OK;
+}
+
+kvm_status ensure_ring(kvm_session *s, cudaStream_t st) {
+    if (s->d_ring) return KVM_OK;
+    // first host-source transfer: the ring is only needed on these paths
+    KVM_CUDA(s, cudaStreamSynchronize(st), "ring allocation sync");
+    KVM_CUDA(s, cudaMalloc(&s->d_ring, s->ring_bytes), "staging ring allocation");
+    return KVM_OK;
+}
+
+PackedInArgs packed_common(kvm_session *s) {
+    PackedInArgs a{};
+    a.cold_block = s->plan.cold_block;
+    a.cold_to = s->plan.cold_to;
+    a.max_items = s->max_blocks;
+    a.n_tokens = s->bt.n_tokens;
+    a.max_blocks = s->max_blocks;
+    a.n_slots = s->n_slots;
+    a.n_layer = s->cfg.n_layer;
+    a.block_tokens = s->cfg.block_tokens;
+    a.win_k = s->d_win;
+    a.win_v = s->d_win + s->cfg.n_layer;
+    a.row_bytes_k = s->row_bytes_k;
+    a.row_bytes_v = s->row_bytes_v;
+    a.status = s->d_status;
+    return a;
+}
+
+// Packed stage-in from pinned host memory: per chunk of cold blocks, H2D of
+// their rows into a ring slot on the copy stream, then the copy kernel into
+// the window slots on `st`.
+kvm_status packed_from_host(kvm_session *s, cudaStream_t st, const kvm_packed_source *src) {
+    const uint32_t L = s->cfg.n_layer;
+    const uint32_t T = s->cfg.block_tokens;
+    std::vector<uint32_t> cold;
+    kvm_status r = read_cold_list(s, st, cold);
+    if (r != KVM_OK) return r;
+    const uint32_t n_cold = static_cast<uint32_t>(cold.size());
     if (n_cold == 0) return KVM_OK;
-    std::vector<uint32_t> cold(n_cold);
-    KVM_CUDA(s, cudaMemcpy(cold.data(), s->plan.cold_block, n_cold * sizeof(uint32_t),
-                           cudaMemcpyDeviceToHost), "cold read");
+    const uint64_t span_k = static_cast<uint64_t>(T) * s->row_bytes_k;
+    const uint64_t span_v = static_cast<uint64_t>(T) * s->row_bytes_v;
+    const uint64_t item_bytes = static_cast<uint64_t>(L) * (span_k + span_v);
+    const uint64_t slot_cap = s->ring_bytes / kvm_session::kRingSlots;
+    if (item_bytes > slot_cap)
+        return fail(s, KVM_ENOMEM, "staging ring slot (%llu B) smaller than one block (%llu B)",
+                    static_cast<unsigned long long>(slot_cap), static_cast<unsigned long long>(item_bytes));
+    r = ensure_ring(s, st);
+    if (r != KVM_OK) return r;
+    const uint32_t per_slot = static_cast<uint32_t>(slot_cap / item_bytes);
+    PackedInArgs a = packed_common(s);
+    a.src_by_item = 1;
+    a.k_layer_stride = span_k;
+    a.k_block_stride = item_bytes;
+    a.v_layer_stride = span_v;
+    a.v_block_stride = item_bytes;
+    a.bulk = (s->row_bytes_k % 16u == 0 && s->row_bytes_v % 16u == 0 && window_aligned16(s)) ? 1u : 0u;
+    KVM_CUDA(s, cudaEventRecord(s->ev[6], st), "ring start");
+    KVM_CUDA(s, cudaStreamWaitEvent(s->copy_stream, s->ev[6], 0), "ring start wait");
+    const uint8_t *hk = static_cast<const uint8_t *>(src->k);
+    const uint8_t *hv = static_cast<const uint8_t *>(src->v);
+    uint32_t chunk = 0;
+    for (uint32_t i0 = 0; i0 < n_cold; i0 += per_slot, ++chunk) {
+        const uint32_t m = std::min(per_slot, n_cold - i0);
+        const int rs = static_cast<int>(chunk % kvm_session::kRingSlots);
+        uint8_t *ring = s->d_ring + static_cast<uint64_t>(rs) * slot_cap;
+        if (chunk >= static_cast<uint32_t>(kvm_session::kRingSlots))
+            KVM_CUDA(s, cudaStreamWaitEvent(s->copy_stream, s->ring_free[rs], 0), "ring free wait");
+        for (uint32_t j = 0; j < m; ++j) {
+            const uint32_t b = cold[i0 + j];
+            if (b >= s->n_blocks) return fail(s, KVM_EDEVICE, "cold block %u out of range", b);
+            const uint32_t nt = std::min(s->h_n_tokens[b], T);
+            if (nt == 0) continue;
+            uint8_t *dk = ring + static_cast<uint64_t>(j) * item_bytes;
+            KVM_CUDA(s, cudaMemcpy2DAsync(dk, span_k, hk + static_cast<uint64_t>(b) * src->k_block_stride,
+                                          src->k_layer_stride, static_cast<size_t>(nt) * s->row_bytes_k, L,
+                                          cudaMemcpyHostToDevice, s->copy_stream),
+                     "packed ring H2D (K)");
+            KVM_CUDA(s, cudaMemcpy2DAsync(dk + L * span_k, span_v, hv + static_cast<uint64_t>(b) * src->v_block_stride,
+                                          src->v_layer_stride, static_cast<size_t>(nt) * s->row_bytes_v, L,
+                                          cudaMemcpyHostToDevice, s->copy_stream),
+                     "packed ring H2D (V)");
+        }
+        KVM_CUDA(s, cudaEventRecord(s->ring_copied[rs], s->copy_stream), "ring copied");
+        KVM_CUDA(s, cudaStreamWaitEvent(st, s->ring_copied[rs], 0), "ring copied wait");
+        a.src_k = ring;
+        a.src_v = ring + L * span_k;
+        a.item0 = i0;
+        a.n_items_host = m;
+        a.n_items_dev = nullptr;
+        KVM_CUDA(s, launch_packed_stagein(a, st), "packed stage-in launch");
+        s->launches++;
+        KVM_CUDA(s, cudaEventRecord(s->ring_free[rs], st), "ring free");
+    }
+    return KVM_OK;
+}
+
+// Stage-in of cold blocks from pinned host memory: read the cold list back,
+// then per chunk of blocks copy the F16 spans into an HBM ring slot on the
+// copy stream and quantize that slot on `st` once its copy is done.
+kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *src) {
+    const uint32_t L = s->cfg.n_layer;
+    const uint32_t T = s->cfg.block_tokens;
+    std::vector<uint32_t> cold;
+    kvm_status r = read_cold_list(s, st, cold);
+    if (r != KVM_OK) return r;
+    const uint32_t n_cold = static_cast<uint32_t>(cold.size());
+    if (n_cold == 0) return KVM_OK;
     const uint64_t span = static_cast<uint64_t>(T) * s->n_embd * 2u;   // one (layer, K|V) of a block
     const uint64_t item_bytes = 2ull * L * span;
     const uint32_t per_slot = static_cast<uint32_t>(
@@ -335,11 +438,8 @@ kvm_status stagein_from_host(kvm_session *s, cudaStream_t st, const kvm_source *
         return fail(s, KVM_ENOMEM, "staging ring (%zu B) smaller than one block (%llu B) per slot",
                     s->ring_bytes, static_cast<unsigned long long>(item_bytes));
     const uint64_t slot_bytes = item_bytes * per_slot;
-    if (!s->d_ring) {
-        // first host-source stage-in: the ring is only needed on this path
-        KVM_CUDA(s, cudaStreamSynchronize(st), "ring allocation sync");
-        KVM_CUDA(s, cudaMalloc(&s->d_ring, s->ring_bytes), "staging ring allocation");
-    }
+    r = ensure_ring(s, st);
+    if (r != KVM_OK) return r;
     StageinArgs a = stagein_common(s);
     a.src_by_item = 1;
     a.layer_stride = span;
@@ -1289,6 +1389,38 @@ kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
     a.item_stride = src->block_stride;
     a.row_stride = src->row_stride;
     KVM_CUDA(s, launch_stagein(a, st, 0), "stage-in launch");
+    s->launches++;
+    return KVM_OK;
+}
+
+kvm_status kvm_stagein_packed(kvm_session *s, kvm_stream stream, const kvm_packed_source *src,
+                              const kvm_window *win) {
+    if (!s) return KVM_EINVAL;
+    if (!s->have_plan) return fail(s, KVM_ESTATE, "kvm_stagein_packed needs a plan (kvm_diff)");
+    if (!win || !win->d_k || !win->d_v) return fail(s, KVM_EINVAL, "null window");
+    if (!src || !src->k || !src->v) return fail(s, KVM_EINVAL, "null source");
+    if (src->location != KVM_LOC_DEVICE && src->location != KVM_LOC_HOST)
+        return fail(s, KVM_EINVAL, "bad source location");
+    DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    kvm_status r = upload_window(s, st, win);
+    if (r != KVM_OK) return r;
+    r = launch_moves(s, st);
+    if (r != KVM_OK) return r;
+    if (src->location == KVM_LOC_HOST) return packed_from_host(s, st, src);
+    PackedInArgs a = packed_common(s);
+    a.n_items_dev = &s->plan.hdr->n_cold;
+    a.src_k = static_cast<const uint8_t *>(src->k);
+    a.src_v = static_cast<const uint8_t *>(src->v);
+    a.k_layer_stride = src->k_layer_stride;
+    a.k_block_stride = src->k_block_stride;
+    a.v_layer_stride = src->v_layer_stride;
+    a.v_block_stride = src->v_block_stride;
+    const uint64_t m = reinterpret_cast<uintptr_t>(src->k) | reinterpret_cast<uintptr_t>(src->v) |
+                       src->k_layer_stride | src->k_block_stride | src->v_layer_stride | src->v_block_stride;
+    a.bulk = ((m & 15u) == 0 && s->row_bytes_k % 16u == 0 && s->row_bytes_v % 16u == 0 && window_aligned16(s))
+                 ? 1u : 0u;
+    KVM_CUDA(s, launch_packed_stagein(a, st), "packed stage-in launch");
     s->launches++;
     return KVM_OK;
 }

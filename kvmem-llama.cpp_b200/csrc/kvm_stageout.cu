@@ -1,4 +1,5 @@
-// kvm_stageout.cu -- stage-out (harvest) of packed window rows.
+// kvm_stageout.cu -- stage-out (harvest) of packed window rows, and stage-in
+// of packed rows back into the window.
 //
 // Replaces the reference's harvest gather (harvest_gpu_v ->
 // kvmem_stageout_enqueue / kvmem_stageout_submit,
@@ -15,6 +16,12 @@
 // piece overlaps the load of the next; six or seven such CTAs per SM keep
 // ~200 KiB in flight.  A byte-copy path serves destinations or rows that are
 // not 16-byte aligned.
+//
+// packed_stagein_kernel: the reverse copy for kvm_stagein_packed (the
+// reference's stage-in as it runs today: write_block_to_gpu ->
+// kvmem_stagein_enqueue_v / kvmem_stagein_flush): each cold block's packed
+// rows, from a block-indexed source or a staging-ring chunk, into its window
+// slot, with the same bulk-copy loop.
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
@@ -63,17 +70,20 @@ __device__ __forceinline__ Piece decode_piece(const StageoutArgs &a, uint64_t u,
     return pc;
 }
 
-__global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
+// The copy loop of one CTA over units blockIdx.x, +gridDim.x, ... < total:
+// decode(u) names a piece (bytes == 0: nothing to move).  Lane 0 moves pieces
+// with bulk copies through two shared-memory buffers; without `bulk` every
+// lane copies bytes.
+template <typename Decode>
+__device__ __forceinline__ void copy_pieces(uint64_t total, bool bulk, uint32_t *status,
+                                            const Decode &decode) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint8_t *buf = smem + 128;
-    const uint32_t pieces = (a.block_tokens * max(a.row_bytes_k, a.row_bytes_v) + kPiece - 1u) / kPiece;
-    const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
     const int lane = threadIdx.x;
-    if (!a.bulk) {
-        // unaligned rows or destination: every lane copies bytes
+    if (!bulk) {
         for (uint64_t u = blockIdx.x; u < total; u += gridDim.x) {
-            const Piece pc = decode_piece(a, u, pieces);
+            const Piece pc = decode(u);
             for (uint32_t i = lane; i < pc.bytes; i += 32u) pc.dst[i] = pc.src[i];
         }
         return;
@@ -84,7 +94,7 @@ __global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
     uint32_t k = 0;
     bool ok = true;
     for (uint64_t u = blockIdx.x; u < total; u += gridDim.x) {
-        const Piece pc = decode_piece(a, u, pieces);
+        const Piece pc = decode(u);
         if (pc.bytes == 0) continue;
         const uint32_t s = k % kOutStages;
         // the store that last read stage s was issued kOutStages pieces ago
@@ -92,7 +102,7 @@ __global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
         mbar_arrive_expect_tx(&full[s], pc.bytes);
         bulk_g2s(buf + s * kPiece, pc.src, pc.bytes, &full[s]);
         if (!mbar_wait_bounded(&full[s], (k / kOutStages) & 1u)) {
-            set_status(a.status, kErrTimeout);
+            set_status(status, kErrTimeout);
             ok = false;
             break;
         }
@@ -108,29 +118,108 @@ __global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
     bulk_wait_all<0>();
 }
 
+__device__ __forceinline__ uint32_t pieces_per_span(uint32_t block_tokens, uint32_t rbk, uint32_t rbv) {
+    return (block_tokens * (rbk > rbv ? rbk : rbv) + kPiece - 1u) / kPiece;
+}
+
+__global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
+    const uint32_t pieces = pieces_per_span(a.block_tokens, a.row_bytes_k, a.row_bytes_v);
+    const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
+    copy_pieces(total, a.bulk != 0u, a.status, [&](uint64_t u) { return decode_piece(a, u, pieces); });
+}
+
+// Unit u = ((j * L + l) * 2 + kv) * pieces + p over the cold items of this
+// launch: block cold_block[item0 + j]'s rows go to window slot cold_to[...].
+__device__ __forceinline__ Piece decode_packed_in(const PackedInArgs &a, uint32_t n_items, uint64_t u,
+                                                  uint32_t pieces) {
+    Piece pc{nullptr, nullptr, 0u};
+    const uint32_t p = static_cast<uint32_t>(u % pieces);
+    uint64_t r = u / pieces;
+    const uint32_t kv = static_cast<uint32_t>(r & 1u);
+    r >>= 1;
+    const uint32_t l = static_cast<uint32_t>(r % a.n_layer);
+    const uint32_t j = static_cast<uint32_t>(r / a.n_layer);
+    if (j >= n_items) return pc;
+    const uint32_t idx = a.item0 + j;
+    const uint32_t b = a.cold_block[idx];
+    const int32_t slot = a.cold_to[idx];
+    if (b >= a.max_blocks) {
+        if (p == 0 && l == 0 && kv == 0) set_status(a.status, kErrIndex);
+        return pc;
+    }
+    if (slot < 0 || static_cast<uint32_t>(slot) >= a.n_slots) {
+        if (p == 0 && l == 0 && kv == 0) set_status(a.status, kErrSlot);
+        return pc;
+    }
+    const uint32_t rb = kv ? a.row_bytes_v : a.row_bytes_k;
+    const uint32_t total = min(a.n_tokens[b], a.block_tokens) * rb;
+    const uint32_t off = p * kPiece;
+    if (off >= total) return pc;
+    pc.bytes = min(kPiece, total - off);
+    const uint64_t si = a.src_by_item ? j : b;
+    pc.src = (kv ? a.src_v : a.src_k) + l * (kv ? a.v_layer_stride : a.k_layer_stride) +
+             si * (kv ? a.v_block_stride : a.k_block_stride) + off;
+    pc.dst = (kv ? a.win_v[l] : a.win_k[l]) + static_cast<uint64_t>(slot) * a.block_tokens * rb + off;
+    return pc;
+}
+
+__global__ void __launch_bounds__(32) packed_stagein_kernel(PackedInArgs a) {
+    const uint32_t n_items = min(a.n_items_dev ? *a.n_items_dev : a.n_items_host, a.max_items);
+    const uint32_t pieces = pieces_per_span(a.block_tokens, a.row_bytes_k, a.row_bytes_v);
+    const uint64_t total = static_cast<uint64_t>(n_items) * a.n_layer * 2u * pieces;
+    copy_pieces(total, a.bulk != 0u, a.status,
+                [&](uint64_t u) { return decode_packed_in(a, n_items, u, pieces); });
+}
+
 }  // namespace
 
-cudaError_t launch_stageout(const StageoutArgs &a, cudaStream_t stream) {
-    if (a.n == 0) return cudaSuccess;
-    static std::atomic<uint64_t> attr{0};
+// The copy kernels' shared-memory opt-in, once per device.
+static cudaError_t copy_smem_once(const void *kernel, std::atomic<uint64_t> &attr) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!(attr.load(std::memory_order_acquire) & (1ull << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(stageout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kOutSmem));
         if (e != cudaSuccess) return e;
         attr.fetch_or(1ull << dev, std::memory_order_acq_rel);
     }
-    int per_sm = 1, sms = 148;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stageout_kernel, 32, kOutSmem);
+    return cudaSuccess;
+}
+
+static uint32_t copy_grid(const void *kernel, uint64_t total) {
+    int dev = 0, per_sm = 1, sms = 148;
+    cudaGetDevice(&dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32, kOutSmem);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (per_sm < 1) per_sm = 1;
+    uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
+    if (grid > total) grid = total;
+    return grid ? static_cast<uint32_t>(grid) : 1u;
+}
+
+cudaError_t launch_stageout(const StageoutArgs &a, cudaStream_t stream) {
+    if (a.n == 0) return cudaSuccess;
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = copy_smem_once(reinterpret_cast<const void *>(stageout_kernel), attr);
+    if (e != cudaSuccess) return e;
     const uint32_t pieces = (a.block_tokens * (a.row_bytes_k > a.row_bytes_v ? a.row_bytes_k : a.row_bytes_v) +
                              kPiece - 1u) / kPiece;
     const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
-    uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
-    if (grid > total) grid = total;
-    stageout_kernel<<<static_cast<uint32_t>(grid), 32, kOutSmem, stream>>>(a);
+    stageout_kernel<<<copy_grid(reinterpret_cast<const void *>(stageout_kernel), total), 32, kOutSmem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_packed_stagein(const PackedInArgs &a, cudaStream_t stream) {
+    static std::atomic<uint64_t> attr{0};
+    cudaError_t e = copy_smem_once(reinterpret_cast<const void *>(packed_stagein_kernel), attr);
+    if (e != cudaSuccess) return e;
+    const uint32_t pieces = (a.block_tokens * (a.row_bytes_k > a.row_bytes_v ? a.row_bytes_k : a.row_bytes_v) +
+                             kPiece - 1u) / kPiece;
+    const uint32_t items = a.n_items_dev ? a.max_items : a.n_items_host;
+    const uint64_t total = static_cast<uint64_t>(items) * a.n_layer * 2u * pieces;
+    if (total == 0) return cudaSuccess;
+    packed_stagein_kernel<<<copy_grid(reinterpret_cast<const void *>(packed_stagein_kernel), total), 32, kOutSmem,
+                            stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -40,6 +40,7 @@ ABI_SYMBOLS = (
     "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
     "kvm_meank_zero", "kvm_query_reset", "kvm_query_add", "kvm_set_transform",
     "kvm_attn_rot_nrot", "kvm_stageout", "kvm_stageout_item_bytes", "kvm_select_groups",
+    "kvm_stagein_packed",
 )
 
 
@@ -108,6 +109,14 @@ class Transform(C.Structure):
 
 def attn_rot_nrot(type_: int, head_dim: int, is_k: bool) -> int:
     return int(lib().kvm_attn_rot_nrot(type_, head_dim, 1 if is_k else 0))
+
+
+class PackedSource(C.Structure):
+    """kvm_packed_source: already-quantized rows, block b layer l at
+    k + l*k_layer_stride + b*k_block_stride (V alike)."""
+    _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("k_layer_stride", C.c_uint64),
+                ("k_block_stride", C.c_uint64), ("v_layer_stride", C.c_uint64),
+                ("v_block_stride", C.c_uint64), ("location", C.c_int32), ("reserved0", C.c_int32)]
 
 
 class Window(C.Structure):
@@ -192,6 +201,7 @@ def lib():
             "kvm_stageout": (C.c_int, [vp, vp, vp, u32, C.POINTER(Window), vp, vp]),
             "kvm_stageout_item_bytes": (u64, [vp]),
             "kvm_select_groups": (C.c_int, [vp, vp, vp, vp, u32, vp, u32]),
+            "kvm_stagein_packed": (C.c_int, [vp, vp, C.POINTER(PackedSource), C.POINTER(Window)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -431,6 +441,21 @@ class Session:
         win = self._window(k_bases, v_bases)
         self._check(lib().kvm_stagein(self.h, _stream(stream), C.byref(src), C.byref(win)),
                     "stagein")
+
+    def stagein_packed(self, src: PackedSource, k_bases, v_bases, stream=None):
+        win = self._window(k_bases, v_bases)
+        self._check(lib().kvm_stagein_packed(self.h, _stream(stream), C.byref(src), C.byref(win)),
+                    "stagein_packed")
+
+    def stageout_source(self, dst, location=LOC_DEVICE) -> PackedSource:
+        """The packed source a kvm_stageout destination forms when its ids were
+        0, 1, 2, ... (block b at item b)."""
+        T = self.cfg.block_tokens
+        E = self.cfg.n_head_kv * self.cfg.head_dim
+        rbk, rbv = row_bytes(self.cfg.type_k, E), row_bytes(self.cfg.type_v, E)
+        base = _ptr(dst)
+        item = self.stageout_item_bytes
+        return PackedSource(base, base + T * rbk, T * (rbk + rbv), item, T * (rbk + rbv), item, location, 0)
 
     @property
     def stageout_item_bytes(self) -> int:
