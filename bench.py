@@ -939,6 +939,8 @@ def run_kernels(args):
       stage-in       the config-2 cold-window stage-in plain, with attn_rot
                      (Hadamard 256 on K, 64 on V) and with RoPE + attn_rot;
       stage-out      the 256 selected blocks (1.14 GB) to HBM and to pinned host;
+      packed stage-in  the 256 cold blocks' already-quantized rows (1.14 GB)
+                     from HBM and from pinned host (kvm_stagein_packed);
       select_groups  8192 groups over the 2048 blocks."""
     import torch
     import kvm
@@ -1010,6 +1012,25 @@ def run_kernels(args):
         so[name] = {"ms": round(ms, 4), "GBs_packed": round(len(sel) * item / ms / 1e6, 1)}
     so["hbm"]["frac_rw"] = round(2 * len(sel) * item / (so["hbm"]["ms"] * 1e6) / peak, 3)
     out["stageout"] = so
+    # ---- packed stage-in (already-quantized rows, the reference's stage-in today)
+    sess.reset_window()
+    sess.score()
+    sess.select()
+    sess.diff()
+    n_cold = int(sess.plan()["cold_block"].size)
+    pk = {"blocks": n_cold, "bytes": n_cold * item}
+    hist_dev = torch.empty(B * item, dtype=torch.uint8, device=dev)      # block-indexed history
+    src_dev = sess.stageout_source(hist_dev, kvm.LOC_DEVICE)
+    ms = _time_ms(torch, lambda: sess.stagein_packed(src_dev, kb, vb))
+    pk["hbm"] = {"ms": round(ms, 4), "frac_rw": round(2 * n_cold * item / (ms * 1e6) / peak, 3)}
+    del hist_dev
+    one = torch.empty(item, dtype=torch.uint8).pin_memory()             # every block reads item 0
+    src_host = sess.stageout_source(one, kvm.LOC_HOST)
+    src_host.k_block_stride = 0
+    src_host.v_block_stride = 0
+    ms = _time_ms(torch, lambda: sess.stagein_packed(src_host, kb, vb), reps=3)
+    pk["pinned_host"] = {"ms": round(ms, 3), "GBs_h2d": round(n_cold * item / ms / 1e6, 1)}
+    out["stagein_packed"] = pk
     # ---- semantic groups
     rng = np.random.default_rng(args.seed)
     b0 = rng.integers(0, B * T, 8192)
