@@ -255,13 +255,16 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
                     }
                 }
             }
-            // spans 32 .. nrot/2: lane j pairs with lane j ^ (span / 32)
+            // spans 32 .. nrot/2: lane j pairs with lane j ^ (span / 32).  The
+            // lower lane keeps v + p, the upper p - v: fma(+-1, v, p) forms
+            // p +- v exactly before its one rounding, the same value as the
+            // add or the subtraction, in one instruction.
             for (uint32_t dl = 1; 32u * dl < nrot; dl <<= 1) {
-                const bool upper = (j & dl) != 0u;
+                const float sgn = (j & dl) != 0u ? -1.0f : 1.0f;
 #pragma unroll
                 for (int m = 0; m < 32; ++m) {
                     const float p = __shfl_xor_sync(0xffffffffu, v[m], static_cast<int>(dl));
-                    v[m] = upper ? __fsub_rn(p, v[m]) : __fadd_rn(v[m], p);
+                    v[m] = __fmaf_rn(sgn, v[m], p);
                 }
             }
         }
