@@ -512,9 +512,10 @@ def cpu_baseline(torch, c, hk, hv, qs, qc, sess, n_staged):
     return {"value": round((score_b + stage_b) / step_s / 1e9, 3), "unit": "GB/s",
             "ms_per_step": round(step_s * 1e3, 2), "cores": threads, "kind": "port",
             "stage_ms": {k: round(r[k] * 1e3, 2) for k in ("score", "plan", "stagein")},
-            "sample": (f"one config-2 step: score of all 2048 blocks x 16 layers, select+diff "
+            "sample": (f"one config-{'2' if L > 1 else '1'} step: score of all {B} blocks x {L} layer(s), "
+                       f"select+diff "
                        f"({'reference libkvmem' if ref else 'oracle'}), gather+quantize of "
-                       f"{r['n_sampled']} of {r['n_staged']} staged blocks x 16 layers x K,V "
+                       f"{r['n_sampled']} of {r['n_staged']} staged blocks x {L} layer(s) x K,V "
                        f"scaled to all; {threads} threads")}
 
 
@@ -941,6 +942,7 @@ def run_kernels(args):
       stage-out      the 256 selected blocks (1.14 GB) to HBM and to pinned host;
       packed stage-in  the 256 cold blocks' already-quantized rows (1.14 GB)
                      from HBM and from pinned host (kvm_stagein_packed);
+      stage-in       the config-3 type mixes (q8_0/q4_0; q5_0/q5_0, gen 12288);
       select_groups  8192 groups over the 2048 blocks."""
     import torch
     import kvm
@@ -1031,6 +1033,25 @@ def run_kernels(args):
     ms = _time_ms(torch, lambda: sess.stagein_packed(src_host, kb, vb), reps=3)
     pk["pinned_host"] = {"ms": round(ms, 3), "GBs_h2d": round(n_cold * item / ms / 1e6, 1)}
     out["stagein_packed"] = pk
+    # ---- stage-in of the config-3 type mixes (same history, fresh sessions)
+    mixes = {}
+    for name, tk, tv, gen in (("3a_q8_0_q4_0", 8, 2, c["gen_reserve"]), ("3b_q5_0_q5_0", 6, 6, 12288)):
+        c3 = dict(c, type_k=tk, type_v=tv, gen_reserve=gen)
+        s3 = _make_session(kvm, c3, B, 0)
+        s3.register_append(B * T)
+        s3.summarize(src)
+        wk3, wv3, kb3, vb3 = _window(torch, c3, s3.n_slots, dev)
+        s3.set_query(q.data_ptr(), np.ones(L, np.uint32))
+        s3.reset_window()
+        s3.score()
+        s3.select()
+        s3.diff()
+        ms = _time_ms(torch, lambda: s3.stagein(src, kb3, vb3))
+        b3 = algo_bytes(c3, 256)[1]
+        mixes[name] = {"stagein_ms": round(ms, 4), "bytes": int(b3), "frac": round(b3 / ms / 1e6 / peak, 3)}
+        s3.close()
+        del wk3, wv3
+    out["stagein_type_mixes"] = mixes
     # ---- semantic groups
     rng = np.random.default_rng(args.seed)
     b0 = rng.integers(0, B * T, 8192)
