@@ -51,9 +51,13 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-clock-probe", action="store_true",
                     help="skip the extra second of load that lets nvidia-smi sample clocks")
-    ap.add_argument("--profile-case", choices=("score",), default=None,
-                    help="small profiling case: the scorer alone over config-2 summaries "
-                         "(134 MB on the device, no history)")
+    ap.add_argument("--profile-case", choices=("score", "stagein"), default=None,
+                    help="small profiling cases: score = the scorer alone over config-2 "
+                         "summaries (134 MB on the device, no history); stagein = the cold "
+                         "stage-in of one layer (config 1, 1.07 GB of history) in the "
+                         "--types K,V window formats")
+    ap.add_argument("--types", default="8,8",
+                    help="K,V ggml type ids of --profile-case stagein (8 q8_0, 2 q4_0, 6 q5_0, 1 f16)")
     ap.add_argument("--mode", choices=("sessions", "layer-split", "incremental", "multi-session",
                                        "kernels"),
                     default="sessions",
@@ -610,6 +614,36 @@ def run_profile_score(args):
     sess.close()
 
 
+def run_profile_stagein(args):
+    """The cold-window stage-in of config 1 (one layer, 256 blocks) in the
+    --types window formats, timed alone: the small case for ncu captures of
+    the quantizers."""
+    import torch
+    import kvm
+    tk, tv = (int(x) for x in args.types.split(","))
+    c = dict(CFG2, n_layer=1, type_k=tk, type_v=tv)
+    L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    dev = torch.device("cuda", 0)
+    hk, hv = gen_history(torch, c, args.seed, dev)
+    sess = _make_session(kvm, c, B, 0)
+    sess.register_append(B * T)
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    sess.summarize(src)
+    wk, wv, kb, vb = _window(torch, c, sess.n_slots, dev)
+    q = gen_queries(torch, c, 1, args.seed, dev)[0]
+    sess.set_query(q.data_ptr(), np.ones(L, np.uint32))
+    sess.reset_window()
+    sess.score()
+    sess.select()
+    sess.diff()
+    ms = _time_ms(torch, lambda: sess.stagein(src, kb, vb), reps=max(3, args.steps), warm=args.warmup)
+    b = algo_bytes(c, 256)[1]
+    print(json.dumps({"profile_case": "stagein", "types": [tk, tv], "ms": round(ms, 4),
+                      "achieved_gbs": round(b / ms / 1e6, 1)}))
+    sess.close()
+
+
 def _dist_init(torch):
     import datetime
     import torch.distributed as dist
@@ -1076,6 +1110,8 @@ def main():
         run_kernels(args)
     elif args.profile_case == "score":
         run_profile_score(args)
+    elif args.profile_case == "stagein":
+        run_profile_stagein(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

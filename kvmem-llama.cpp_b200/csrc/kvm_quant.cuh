@@ -133,60 +133,89 @@ __device__ __forceinline__ uint32_t code_q(float x, float id, float off, int max
     return static_cast<uint32_t>(q > maxq ? maxq : q);
 }
 
-// 8 codes of one chunk: code m (q & 15) at bits 4m of `nib`, bit 4 of the
-// code at bit m of `hi` (q5_0).
-__device__ __forceinline__ void chunk_codes(const uint4 &r, float id, float off, int maxq,
-                                            uint32_t &nib, uint32_t &hi) {
+// The 8 codes of one chunk as bytes: word p holds values 4p .. 4p+3.
+__device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, int maxq,
+                                                 uint32_t (&w)[2]) {
     const __half2 *h = halves(r);
-    nib = 0;
-    hi = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 x = __half22float2(h[i]);
-        const uint32_t c0 = code_q(x.x, id, off, maxq);
-        const uint32_t c1 = code_q(x.y, id, off, maxq);
-        nib |= ((c0 & 15u) << (8 * i)) | ((c1 & 15u) << (8 * i + 4));
-        hi |= ((c0 >> 4) << (2 * i)) | ((c1 >> 4) << (2 * i + 1));
+    for (int p = 0; p < 2; ++p) {
+        const float2 x0 = __half22float2(h[2 * p]);
+        const float2 x1 = __half22float2(h[2 * p + 1]);
+        const uint32_t c0 = code_q(x0.x, id, off, maxq), c1 = code_q(x0.y, id, off, maxq);
+        const uint32_t c2 = code_q(x1.x, id, off, maxq), c3 = code_q(x1.y, id, off, maxq);
+        w[p] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
     }
 }
 
-// Interleave two chunks' nibbles into the 8 bytes j | (j+16) << 4.
-__device__ __forceinline__ void store_nibble_pairs(uint8_t *qs, uint32_t lo, uint32_t hi) {
-    // lo/hi hold code m at bits 4m; byte m = lo_m | hi_m << 4
-    uint32_t b[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) b[m] = ((lo >> (4 * m)) & 15u) | (((hi >> (4 * m)) & 15u) << 4);
-#pragma unroll
-    for (int m = 0; m < 8; m += 2) st_u16(qs + m, b[m] | (b[m + 1] << 8));
+// Bit 4 of each of the 4 byte codes of `w`, as bits 0..3: the masked bytes
+// sit at bits 0, 8, 16, 24 and the multiply by 0x01020408 lands them on bits
+// 24..27 (every partial product on its own bit, so no carries).
+__device__ __forceinline__ uint32_t high_bits4(uint32_t w) {
+    return (((w >> 4) & 0x01010101u) * 0x01020408u) >> 24;
 }
 
-// q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes).
+// vmax of q4_0 / q5_0 -- the first value (block order) of largest magnitude --
+// from the block's signed max and min: when max > -min every value of that
+// magnitude is the max, when -min > max the min; only a +a / -a tie needs the
+// first occurrence.  +0.0 when every value is zero.  *amax_out gets amax.
+__device__ __forceinline__ float signed_absmax(const Block32 &b, float *amax_out) {
+    __half2 mx = halves(b.raw[0])[0];
+    __half2 mn = mx;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int i = (k == 0 ? 1 : 0); i < 4; ++i) {
+            mx = __hmax2(mx, halves(b.raw[k])[i]);
+            mn = __hmin2(mn, halves(b.raw[k])[i]);
+        }
+    }
+    const float hi = fmaxf(__low2float(mx), __high2float(mx));
+    const float lo = fminf(__low2float(mn), __high2float(mn));
+    const float amax = fmaxf(hi, -lo);
+    *amax_out = amax;
+    if (amax == 0.0f) return 0.0f;
+    if (hi != -lo) return hi > -lo ? hi : lo;
+    return first_of_absmax(b, amax);
+}
+
+// q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes).  d = vmax /
+// -8 (-16) is computed as vmax * -0.125 (-0.0625): division and
+// multiplication by a power of two return the same correctly rounded value.
 template <bool Q5>
 __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
-    const float amax = absmax32(b);
-    const float vmax = first_of_absmax(b, amax);
-    const float d = __fdiv_rn(vmax, Q5 ? -16.0f : -8.0f);
+    float amax;
+    const float vmax = signed_absmax(b, &amax);
+    const float d = __fmul_rn(vmax, Q5 ? -0.0625f : -0.125f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     const float off = Q5 ? 16.5f : 8.5f;
     const int maxq = Q5 ? 31 : 15;
-    uint32_t nib[4], hb[4];
+    uint32_t w[4][2];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) chunk_codes(b.raw[k], id, off, maxq, nib[k], hb[k]);
+    for (int k = 0; k < 4; ++k) chunk_code_bytes(b.raw[k], id, off, maxq, w[k]);
     st_u16(blk, f16_bits(d));
     uint8_t *qs = blk + (Q5 ? 6 : 2);
-    uint32_t qh = 0;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        // chunks k and k+2 are a nibble pair; the lower chunk index is byte 8*c
-        const int ca = chunk_of(b, k);
-        const bool a_low = ca < 2;
-        const uint32_t lo = a_low ? nib[k] : nib[k + 2];
-        const uint32_t hi = a_low ? nib[k + 2] : nib[k];
-        store_nibble_pairs(qs + 8 * (a_low ? ca : chunk_of(b, k + 2)), lo, hi);
+        // chunks k and k+2 are a nibble pair: value j of the lower chunk index
+        // takes the low nibble of byte j, its partner 16 values on the high one
+        const bool a_low = chunk_of(b, k) < 2;
+        const uint32_t *lo = a_low ? w[k] : w[k + 2];
+        const uint32_t *hi = a_low ? w[k + 2] : w[k];
+        uint8_t *q = qs + 8 * (a_low ? chunk_of(b, k) : chunk_of(b, k + 2));
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const uint32_t by = (lo[p] & 0x0f0f0f0fu) | ((hi[p] << 4) & 0xf0f0f0f0u);
+            st_u16(q + 4 * p, by & 0xffffu);
+            st_u16(q + 4 * p + 2, by >> 16);
+        }
     }
     if (Q5) {
+        uint32_t qh = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) qh |= hb[k] << (8 * chunk_of(b, k));
+        for (int k = 0; k < 4; ++k) {
+            const int c = chunk_of(b, k);
+            qh |= (high_bits4(w[k][0]) | (high_bits4(w[k][1]) << 4)) << (8 * c);
+        }
         st_u16(blk + 2, qh & 0xffffu);
         st_u16(blk + 4, qh >> 16);
     }
