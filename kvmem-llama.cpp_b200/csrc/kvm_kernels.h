@@ -12,7 +12,7 @@ namespace kvm {
 constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
 constexpr int kStageinStages = 3;
-constexpr int kPermuteThreads = 256;
+constexpr int kPermuteThreads = 512;
 constexpr int kScoreBlocks = 64;                   // blocks per scorer CTA (one thread each)
 constexpr int kScoreBatch = 64;                    // channel loads in flight per scorer thread
 constexpr uint32_t kSumGroup = 64;                 // blocks per summary tile (== kScoreBlocks)
@@ -140,7 +140,8 @@ struct PermuteArgs {
     uint32_t row_bytes_v;
     uint32_t span_k;
     uint32_t span_v;
-    uint32_t col_bytes;
+    uint32_t col_bytes;            // widest column a CTA stages (bytes, multiple of 16)
+    uint32_t col_region;           // shared-memory bytes for the staged columns
     uint32_t vec16;
     uint32_t *status;
 };

@@ -310,8 +310,9 @@ cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_
 // least busy 42K, of 89K).  Padding each CTA's shared memory caps residency at
 // ceil(units / SMs) and so spreads the wave over every SM.
 static size_t score_smem_for(uint32_t units, size_t smem_min) {
-    static size_t cache_smem[64] = {};
-    static uint32_t cache_units[64] = {};
+    // per host thread: sessions on different threads must not race on it
+    static thread_local size_t cache_smem[64] = {};
+    static thread_local uint32_t cache_units[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return smem_min;
     if (cache_units[dev] == units && cache_smem[dev] >= smem_min) return cache_smem[dev];

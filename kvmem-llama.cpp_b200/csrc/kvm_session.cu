@@ -284,9 +284,10 @@ kvm_status launch_moves(kvm_session *s, cudaStream_t st) {
     p.row_bytes_v = s->row_bytes_v;
     p.span_k = s->row_bytes_k * s->cfg.block_tokens;
     p.span_v = s->row_bytes_v * s->cfg.block_tokens;
-    uint32_t col = (96u * 1024u) / std::max(1u, s->n_slots);
-    col = std::min(1024u, std::max(16u, col & ~15u));
-    p.col_bytes = col;
+    // the kernel sizes its column from the device move count: any count up to
+    // n_slots fits 96 KiB at 16 bytes or more a move
+    p.col_region = std::max<uint32_t>(96u * 1024u, 16u * s->n_slots);
+    p.col_bytes = 2048u;
     p.vec16 = (p.span_k % 16u == 0 && p.span_v % 16u == 0 && s->row_bytes_k % 16u == 0 &&
                s->row_bytes_v % 16u == 0 && window_aligned16(s)) ? 1u : 0u;
     p.status = s->d_status;

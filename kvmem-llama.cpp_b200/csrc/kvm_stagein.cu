@@ -443,12 +443,12 @@ struct MoveMeta {
 };
 
 template <typename V>
-__device__ __forceinline__ void permute_column(const PermuteArgs &a, const MoveMeta *meta,
-                                               uint8_t *col, uint32_t n_moves, uint8_t *base,
-                                               uint32_t span, uint32_t rb, uint32_t c0) {
+__device__ __forceinline__ void permute_column(const MoveMeta *meta, uint8_t *col, uint32_t n_moves,
+                                               uint32_t cw, uint8_t *base, uint32_t span, uint32_t rb,
+                                               uint32_t c0) {
     constexpr uint32_t G = sizeof(V);
     constexpr uint32_t U = 4;                 // accesses in flight per thread
-    const uint32_t per_move = a.col_bytes / G;
+    const uint32_t per_move = cw / G;
     const uint32_t n_acc = n_moves * per_move;
     const uint32_t stride = kPermuteThreads * U;
     // gather this column of every moving block into shared memory
@@ -464,7 +464,7 @@ __device__ __forceinline__ void permute_column(const PermuteArgs &a, const MoveM
                 const uint32_t m = i / per_move;
                 const uint32_t o = (i - m * per_move) * G;
                 const MoveMeta mm = meta[m];
-                off[j] = m * a.col_bytes + o;
+                off[j] = m * cw + o;
                 if (c0 + o < mm.n_tok * rb) {
                     r[j] = *reinterpret_cast<const V *>(base + static_cast<uint64_t>(mm.from) * span + c0 + o);
                     ok[j] = true;
@@ -483,7 +483,7 @@ __device__ __forceinline__ void permute_column(const PermuteArgs &a, const MoveM
         const MoveMeta mm = meta[m];
         if (c0 + o < mm.n_tok * rb)
             *reinterpret_cast<V *>(base + static_cast<uint64_t>(mm.to) * span + c0 + o) =
-                *reinterpret_cast<const V *>(col + m * a.col_bytes + o);
+                *reinterpret_cast<const V *>(col + m * cw + o);
     }
     __syncthreads();
 }
@@ -494,6 +494,12 @@ __global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a)
     if (n_moves == 0) return;
     MoveMeta *meta = reinterpret_cast<MoveMeta *>(smem);
     uint8_t *col = smem + permute_meta_bytes(a.max_moves);
+    // The column width follows the actual move count: the widest column (a
+    // multiple of 16 bytes, at most col_bytes) whose copy for every moving
+    // block fits the shared-memory region.  Every CTA computes the same width.
+    uint32_t cw = (a.col_region / n_moves) & ~15u;
+    if (cw > a.col_bytes) cw = a.col_bytes;
+    if (cw < 16u) cw = 16u;
     for (uint32_t m = threadIdx.x; m < n_moves; m += kPermuteThreads) {
         const uint32_t blk = a.mv_block[m];
         const int32_t from = a.mv_from[m];
@@ -510,8 +516,8 @@ __global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a)
         meta[m] = mm;
     }
     __syncthreads();
-    const uint32_t n_cols_k = (a.span_k + a.col_bytes - 1) / a.col_bytes;
-    const uint32_t n_cols_v = (a.span_v + a.col_bytes - 1) / a.col_bytes;
+    const uint32_t n_cols_k = (a.span_k + cw - 1) / cw;
+    const uint32_t n_cols_v = (a.span_v + cw - 1) / cw;
     const uint64_t units = static_cast<uint64_t>(a.n_layer) * (n_cols_k + n_cols_v);
     for (uint64_t u = blockIdx.x; u < units; u += gridDim.x) {
         const uint32_t layer = static_cast<uint32_t>(u / (n_cols_k + n_cols_v));
@@ -522,24 +528,25 @@ __global__ void __launch_bounds__(kPermuteThreads) permute_kernel(PermuteArgs a)
         const uint32_t span = is_v ? a.span_v : a.span_k;
         const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
         if (a.vec16)
-            permute_column<uint4>(a, meta, col, n_moves, base, span, rb, c * a.col_bytes);
+            permute_column<uint4>(meta, col, n_moves, cw, base, span, rb, c * cw);
         else
-            permute_column<uint16_t>(a, meta, col, n_moves, base, span, rb, c * a.col_bytes);
+            permute_column<uint16_t>(meta, col, n_moves, cw, base, span, rb, c * cw);
     }
 }
 
 // ------------------------------------------------------------- launchers --
 
-static int g_num_sms = 0;
-
+// SM count of the current device (cached per host thread and device).
 static int num_sms() {
-    if (g_num_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
+    static thread_local int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] <= 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
     }
-    return g_num_sms;
+    return cached[dev];
 }
 
 uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens) {
@@ -601,8 +608,8 @@ cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t g
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
-    const size_t smem = permute_meta_bytes(a.max_moves) + static_cast<size_t>(a.max_moves) * a.col_bytes;
-    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    const size_t smem = permute_meta_bytes(a.max_moves) + a.col_region;
+    if (smem > 200u * 1024u || a.col_region < 16u * a.max_moves) return cudaErrorInvalidValue;
     if (!attr_once(g_permute_attr, reinterpret_cast<const void *>(permute_kernel), 200 * 1024))
         return cudaErrorInvalidValue;
     const uint32_t grid = static_cast<uint32_t>(num_sms() * 2);
