@@ -125,12 +125,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase: false after kWaitLimitNs.
+// try_wait that may suspend the thread until the phase completes or
+// `hint_ns` nanoseconds pass, so a waiting warp stops taking issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: false after kWaitLimitNs.  Each retry
+// suspends for at most kWaitSuspendNs, so the limit is checked at least
+// every 64 * kWaitSuspendNs.
+constexpr uint32_t kWaitSuspendNs = 1000u;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 0;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
         if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) return false;
     }
 }

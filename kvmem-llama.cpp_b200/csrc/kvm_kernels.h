@@ -11,7 +11,12 @@ namespace kvm {
 
 constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
+// Transform mode: 7 consumer warps + the producer, so that two CTAs (16 warps,
+// four per scheduler) leave 128 registers a thread for the packed butterflies.
+constexpr int kXfConsumerWarps = 7;
+constexpr int kXfThreads = (kXfConsumerWarps + 1) * 32;
 constexpr int kStageinStages = 3;
+constexpr int kXfStages = 5;       // transform mode: ALU-heavier tiles, loads further ahead
 constexpr int kPermuteThreads = 512;
 constexpr int kScoreBlocks = 64;                   // blocks per scorer CTA (one thread each)
 constexpr int kScoreBatch = 64;                    // channel loads in flight per scorer thread
@@ -62,9 +67,17 @@ struct StageinArgs {
     uint32_t rot_v;
     uint32_t rope_n_rot;
     const float *theta;            // device [rope_n_rot / 2]
+    float xf_pre_k, xf_pre_v;      // Hadamard scale applied before the butterflies (1: none)
+    float xf_post_k, xf_post_v;    // power-of-two Hadamard scale folded into the quantizer (1: none)
+    uint32_t xf_heads;             // KV heads per row, n_embd / head_dim
+    uint32_t xf_heads_magic;       // ceil(2^32 / xf_heads); 0 when xf_heads == 1
 };
 
 uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens);
+// Fills the transform-mode fields of `a` (xform, rot_k/v, rope_n_rot, theta
+// and the derived scales and head count); all zero / 1 when nothing is set.
+void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, uint32_t rot_k,
+                           uint32_t rot_v, uint32_t rope_n_rot, const float *theta);
 size_t stagein_smem_bytes(const StageinArgs &a);
 cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap);
 

@@ -42,6 +42,20 @@ __device__ __forceinline__ uint32_t f16_bits(float d) {
     return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(d)));
 }
 
+// amax / 127.0f, correctly rounded, for amax >= 0: Markstein's correction
+// step (P. Markstein, "IA-64 and Elementary Functions", 2000) with the
+// correctly rounded reciprocal r = RN(1/127): q0 = RN(a*r) is within an ulp of
+// a/127, the remainder a - q0*127 is exact under one FMA, and RN(q0 + rem*r)
+// is RN(a/127).  Checked against IEEE division for every non-negative finite
+// float; infinity is passed through as IEEE division does.
+__device__ __forceinline__ float div127(float amax) {
+    const float r = 0x1.020408p-7f;
+    const float q0 = __fmul_rn(amax, r);
+    const float rem = __fmaf_rn(-q0, 127.0f, amax);
+    const float q1 = __fmaf_rn(rem, r, q0);
+    return amax == __int_as_float(0x7f800000) ? amax : q1;
+}
+
 // C roundf (round half away from zero) as an integer for |x| < 2^23:
 // truncate x + copysign(0.49999997, x).  Adding the largest float below 0.5
 // instead of 0.5 keeps the sum exact or correctly rounded on both sides of
@@ -102,7 +116,7 @@ __device__ __forceinline__ float first_of_absmax(const Block32 &b, float amax) {
 // q8_0: 34 bytes = f16 d + 32 int8 codes.
 __device__ __forceinline__ void quant_q8_0(const Block32 &b, uint8_t *blk) {
     const float amax = absmax32(b);
-    const float d = __fdiv_rn(amax, 127.0f);
+    const float d = div127(amax);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     st_u16(blk, f16_bits(d));
 #pragma unroll

@@ -255,13 +255,8 @@ StageinArgs stagein_common(kvm_session *s) {
     const uint32_t out_max = a.rows_per_tile * std::max(s->row_bytes_k, s->row_bytes_v);
     a.tile_out_bytes = (out_max + 15u) & ~15u;
     a.bulk_store = (s->row_bytes_k % 16u == 0 && s->row_bytes_v % 16u == 0 && window_aligned16(s)) ? 1u : 0u;
-    if (s->xf.rot_k || s->xf.rot_v || s->xf.rope_n_rot) {
-        a.xform = s->cfg.head_dim / 32u;
-        a.rot_k = s->xf.rot_k;
-        a.rot_v = s->xf.rot_v;
-        a.rope_n_rot = s->xf.rope_n_rot;
-        a.theta = s->d_theta;
-    }
+    stagein_set_transform(a, s->cfg.head_dim, s->n_embd, s->xf.rot_k, s->xf.rot_v, s->xf.rope_n_rot,
+                          s->d_theta);
     a.status = s->d_status;
     return a;
 }

@@ -27,6 +27,7 @@
 #include "kvm_kernels.h"
 
 #include <atomic>
+#include <cmath>
 
 namespace kvm {
 
@@ -117,83 +118,221 @@ constexpr uint32_t kStageinHeader = 384;
 // -- and the head_dim/32 lanes of a (row, head) work together: butterflies of
 // span < 32 stay in the lane's registers, larger spans pair lanes (xor of the
 // lane index), and each lane quantizes its own block in the reference's
-// sequential order.  Every float operation is a round-to-nearest intrinsic,
-// so the Hadamard and the quantizers match the CPU bit for bit; RoPE calls the
-// CUDA sincosf (as the reference's GPU kernel does) and agrees with the host
-// cosf / sinf to within their last-bit errors.
+// order.  The lane keeps its values as 16 float pairs, P[k] = (v[2k],
+// v[2k+1]), so that all butterflies of span >= 2, the cross-lane stages and
+// the quantizer's multiplies run on sm_100's packed FP32x2 instructions
+// (__fadd2_rn, __ffma2_rn, __fmul2_rn: per component the same IEEE operation
+// as the scalar one).  Every float operation rounds to nearest, so the
+// Hadamard and the quantizers match the CPU bit for bit; RoPE calls the CUDA
+// sincosf (as the reference's GPU kernel does) and agrees with the host cosf /
+// sinf to within their last-bit errors.
+//
+// The Hadamard's scale 1/sqrt(n) is a power of two when log2(n) is even (64,
+// 256, 1024).  Multiplying by a power of two then commutes exactly with every
+// butterfly (F16 inputs keep all sums far above the F32 subnormal range), so
+// without RoPE the transform runs unscaled and the quantizer takes the scale
+// into amax and id: amax*s and id*s are exact, and x*(id*s) is the same real
+// product as (x*s)*id, rounded once.
 
-// One 32-value block from F32 values, the reference's loops in their order
-// (quant_q8_0 / quant_q4_0, llama-kvmem-stagein.cu:180-233; q5_0 as ggml).
-__device__ __forceinline__ void quant_f32_block(int type, const float (&v)[32], uint8_t *blk) {
-    if (type == KVM_TYPE_F16) {
+// The 4 low bytes of q0..q3 as one word (byte i = q_i).
+__device__ __forceinline__ uint32_t pack4(int q0, int q1, int q2, int q3) {
+    return __byte_perm(__byte_perm(static_cast<uint32_t>(q0), static_cast<uint32_t>(q1), 0x0040u),
+                       __byte_perm(static_cast<uint32_t>(q2), static_cast<uint32_t>(q3), 0x0040u), 0x5410u);
+}
+
+// A ggml block of a 2-byte header (F16 d) followed by NW payload words (4*NW
+// bytes), at a 2-byte aligned address: NW word stores and one half-word store.
+// At a 4-byte aligned address the words are shifted by two bytes.
+template <int NW>
+__device__ __forceinline__ void store_block(uint8_t *blk, uint32_t hdr, const uint32_t (&w)[NW]) {
+    const bool odd = (reinterpret_cast<uintptr_t>(blk) & 2u) != 0u;
+    const uint32_t sel = odd ? 0x7654u : 0x5432u;
+    uint32_t *wp = reinterpret_cast<uint32_t *>(blk + (odd ? 2 : 0));
+    uint32_t prev = hdr << 16;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            *reinterpret_cast<uint32_t *>(blk + 2 * j) = f16_bits(v[j]) | (f16_bits(v[j + 1]) << 16);
+    for (int k = 0; k < NW; ++k) {
+        wp[k] = __byte_perm(prev, w[k], sel);
+        prev = w[k];
+    }
+    st_u16(blk + (odd ? 0 : 4 * NW), odd ? hdr : (w[NW - 1] >> 16));
+}
+
+__device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
+
+// C roundf of both components, as integers (|x| < 2^23).
+__device__ __forceinline__ void round_half_away2(float2 y, int &q0, int &q1) {
+    const float2 t = __fadd2_rn(y, make_float2(copysignf(0x1.fffffep-2f, y.x), copysignf(0x1.fffffep-2f, y.y)));
+    q0 = __float2int_rz(t.x);
+    q1 = __float2int_rz(t.y);
+}
+
+// q8_0 of the lane's 32 values scaled by fs (a power of two; 1 when the scale
+// was applied already): quant_q8_0 (llama-kvmem-stagein.cu:180-200).  The
+// running fmaxf of the reference is split over four accumulators: max is
+// exact and fmaxf ignores NaN in any order, so the result is the same.
+__device__ __forceinline__ void quant_q8_pairs(const float2 (&P)[16], float fs, uint8_t *blk) {
+    float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+        m0 = fmaxf(m0, fabsf(P[k].x));
+        m1 = fmaxf(m1, fabsf(P[k].y));
+        m2 = fmaxf(m2, fabsf(P[k + 1].x));
+        m3 = fmaxf(m3, fabsf(P[k + 1].y));
+    }
+    const float amax = __fmul_rn(fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)), fs);
+    const float d = div127(amax);
+    const float2 id = splat2(d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f);
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        int q0, q1, q2, q3;
+        round_half_away2(__fmul2_rn(P[2 * k], id), q0, q1);
+        round_half_away2(__fmul2_rn(P[2 * k + 1], id), q2, q3);
+        w[k] = pack4(q0, q1, q2, q3);
+    }
+    store_block<8>(blk, f16_bits(d), w);
+}
+
+// q4_0 / q5_0 of the lane's 32 values scaled by fs (quant_q4_0,
+// llama-kvmem-stagein.cu:202-233; q5_0 as ggml).  vmax -- the first value of
+// largest magnitude -- comes from the signed max and min; only a +a / -a tie
+// needs the first occurrence.
+template <bool Q5>
+__device__ __forceinline__ void quant_q4q5_pairs(const float2 (&P)[16], float fs, uint8_t *blk) {
+    float hx = P[0].x, hy = P[0].y, lx = P[0].x, ly = P[0].y;
+#pragma unroll
+    for (int k = 1; k < 16; ++k) {
+        hx = fmaxf(hx, P[k].x);
+        hy = fmaxf(hy, P[k].y);
+        lx = fminf(lx, P[k].x);
+        ly = fminf(ly, P[k].y);
+    }
+    const float hi = fmaxf(hx, hy), lo = fminf(lx, ly);
+    const float amax = fmaxf(hi, -lo);
+    float vmax = 0.0f;
+    if (amax > 0.0f) {
+        if (hi != -lo) {
+            vmax = hi > -lo ? hi : lo;
+        } else {
+            // first value (block order) with |v| == amax
+            for (int m = 31; m >= 0; --m) {
+                const float x = (m & 1) ? P[m >> 1].y : P[m >> 1].x;
+                vmax = fabsf(x) == amax ? x : vmax;
+            }
         }
-        return;
     }
-    if (type == KVM_TYPE_Q8_0) {
-        float amax = 0.0f;
+    const float d = __fmul_rn(__fmul_rn(vmax, fs), Q5 ? -0.0625f : -0.125f);
+    const float2 id = splat2(d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f);
+    const float2 off = splat2(Q5 ? 16.5f : 8.5f);
+    const int maxq = Q5 ? 31 : 15;
+    uint32_t c[8];   // byte codes: word k holds values 4k .. 4k+3
 #pragma unroll
-        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        st_u16(blk, f16_bits(d));
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            const uint32_t q0 = static_cast<uint32_t>(round_half_away(__fmul_rn(v[j], id))) & 0xffu;
-            const uint32_t q1 = static_cast<uint32_t>(round_half_away(__fmul_rn(v[j + 1], id))) & 0xffu;
-            st_u16(blk + 2 + j, q0 | (q1 << 8));
-        }
-        return;
+    for (int k = 0; k < 8; ++k) {
+        const float2 t0 = __fadd2_rn(__fmul2_rn(P[2 * k], id), off);
+        const float2 t1 = __fadd2_rn(__fmul2_rn(P[2 * k + 1], id), off);
+        c[k] = pack4(min(__float2int_rz(t0.x), maxq), min(__float2int_rz(t0.y), maxq),
+                     min(__float2int_rz(t1.x), maxq), min(__float2int_rz(t1.y), maxq));
     }
-    const bool q5 = type == KVM_TYPE_Q5_0;
-    float amax = 0.0f, vmax = 0.0f;
+    // byte j of the nibbles: value j on the low nibble, value j + 16 on the high
+    constexpr int NW = Q5 ? 5 : 4;
+    uint32_t w[NW];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const float m = fabsf(v[j]);
-        if (amax < m) {
-            amax = m;
-            vmax = v[j];
-        }
-    }
-    const float d = __fdiv_rn(vmax, q5 ? -16.0f : -8.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const float off = q5 ? 16.5f : 8.5f;
-    const int maxq = q5 ? 31 : 15;
-    st_u16(blk, f16_bits(d));
-    uint32_t qh = 0;
-    uint8_t *qs = blk + (q5 ? 6 : 2);
+    for (int k = 0; k < 4; ++k) w[NW - 4 + k] = (c[k] & 0x0f0f0f0fu) | ((c[k + 4] << 4) & 0xf0f0f0f0u);
+    if (Q5) {
+        uint32_t qh = 0;
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
-        const uint32_t a0 = code_q(v[j], id, off, maxq), b0 = code_q(v[j + 16], id, off, maxq);
-        const uint32_t a1 = code_q(v[j + 1], id, off, maxq), b1 = code_q(v[j + 17], id, off, maxq);
-        qh |= ((a0 >> 4) << j) | ((a1 >> 4) << (j + 1)) | ((b0 >> 4) << (j + 16)) | ((b1 >> 4) << (j + 17));
-        st_u16(qs + j, ((a0 & 15u) | ((b0 & 15u) << 4)) | (((a1 & 15u) | ((b1 & 15u) << 4)) << 8));
+        for (int k = 0; k < 8; ++k) qh |= high_bits4(c[k]) << (4 * k);
+        w[0] = qh;
     }
-    if (q5) {
-        st_u16(blk + 2, qh & 0xffffu);
-        st_u16(blk + 4, qh >> 16);
+    store_block<NW>(blk, f16_bits(d), w);
+}
+
+// The lane's block as ggml F16 (no header), scaled by fs.
+__device__ __forceinline__ void store_f16_pairs(const float2 (&P)[16], float fs, uint8_t *blk) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const float2 x = __fmul2_rn(P[k], splat2(fs));
+        st_u16(blk + 4 * k, f16_bits(x.x));
+        st_u16(blk + 4 * k + 2, f16_bits(x.y));
     }
 }
 
-// 32 consecutive F16 values of a tile row, widened.
-__device__ __forceinline__ void load32(const __half *p, float (&v)[32]) {
+// 32 consecutive F16 values of a tile row (64 bytes), widened.  The four
+// 16-byte chunks are read in the order k ^ r, r = (lane >> 1) & 3, so that a
+// quarter warp reading 8 neighbouring blocks hits 8 different bank groups,
+// then put back in order with two conditional swaps.
+__device__ __forceinline__ void load32(const __half *p, int lane, float2 (&P)[16]) {
+    const uint32_t r = static_cast<uint32_t>(lane >> 1) & 3u;
+    uint4 c[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint4 r = *reinterpret_cast<const uint4 *>(p + 8 * c);
-        const __half2 *h = reinterpret_cast<const __half2 *>(&r);
+    for (int k = 0; k < 4; ++k) c[k] = *reinterpret_cast<const uint4 *>(p + 8u * (static_cast<uint32_t>(k) ^ r));
+    // c[k] = chunk k ^ r: swap by bit 0 of r, then by bit 1
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const float2 f = __half22float2(h[m]);
-            v[8 * c + 2 * m] = f.x;
-            v[8 * c + 2 * m + 1] = f.y;
+    for (int k = 0; k < 4; k += 2) {
+        const uint4 a = c[k], b = c[k + 1];
+        c[k] = (r & 1u) ? b : a;
+        c[k + 1] = (r & 1u) ? a : b;
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 a = c[k], b = c[k + 2];
+        c[k] = (r & 2u) ? b : a;
+        c[k + 2] = (r & 2u) ? a : b;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&c[k]);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) P[4 * k + m] = __half22float2(h[m]);
+    }
+}
+
+// Butterflies of span 1 .. 16 inside the lane (fwht_kernel's h loop,
+// ascending): span 1 inside each pair, spans 2 .. 16 between pairs k and
+// k + h/2.  fma(b, -1, a) is a - b with one rounding.
+__device__ __forceinline__ void fwht32_in_lane(float2 (&P)[16]) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const float x = P[k].x, y = P[k].y;
+        P[k] = make_float2(__fadd_rn(x, y), __fsub_rn(x, y));
+    }
+    const float2 neg = splat2(-1.0f);
+#pragma unroll
+    for (int hp = 1; hp < 16; hp <<= 1) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if ((k & hp) == 0) {
+                const float2 a = P[k], b = P[k | hp];
+                P[k] = __fadd2_rn(a, b);
+                P[k | hp] = __ffma2_rn(b, neg, a);
+            }
         }
     }
 }
 
+// Butterflies of span 32 << t: lane j pairs with lane j ^ (1 << t).  The lower
+// lane keeps v + p, the upper p - v: fma(+-1, v, p) forms p +- v exactly
+// before its one rounding.
+__device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, uint32_t dl) {
+    const float2 sgn = splat2((j & dl) != 0u ? -1.0f : 1.0f);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        // one 64-bit shuffle keeps the pair in a register pair
+        const unsigned long long b = __shfl_xor_sync(
+            0xffffffffu,
+            (static_cast<unsigned long long>(__float_as_uint(P[k].y)) << 32) | __float_as_uint(P[k].x),
+            static_cast<int>(dl));
+        const float2 p = make_float2(__uint_as_float(static_cast<uint32_t>(b)),
+                                     __uint_as_float(static_cast<uint32_t>(b >> 32)));
+        P[k] = __ffma2_rn(sgn, P[k], p);
+    }
+}
+
+// (sub, j): the lane's unit within the warp and its block within the head;
+// per_warp = 32 / xform units a warp-iteration.
 __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
-                                               uint8_t *ob, int warp, int lane) {
+                                               uint8_t *ob, int warp, int lane, uint32_t sub, uint32_t j,
+                                               uint32_t per_warp) {
     const bool is_v = (ts.meta >> 31) != 0u;
     const uint32_t pos0 = ts.meta & 0x7fffffffu;
     const uint32_t nrot = is_v ? a.rot_v : a.rot_k;
@@ -201,83 +340,75 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
     const uint32_t half = n_rope / 2u;
     const uint32_t G = a.xform;                    // lanes per (row, head) = head_dim / 32
     const uint32_t D = G * 32u;
-    const uint32_t per_warp = 32u / G;
-    const uint32_t H = a.n_embd / D;
+    const uint32_t H = a.xf_heads;
     const uint32_t rb = is_v ? a.row_bytes_v : a.row_bytes_k;
     const uint32_t bb = static_cast<uint32_t>(block_bytes(ts.type));
-    const float scale = nrot ? __fdiv_rn(1.0f, __fsqrt_rn(__uint2float_rn(nrot))) : 1.0f;
-    const uint32_t sub = static_cast<uint32_t>(lane) / G;
-    const uint32_t j = static_cast<uint32_t>(lane) - sub * G;
+    const float pre = is_v ? a.xf_pre_v : a.xf_pre_k;
+    const float fs = is_v ? a.xf_post_v : a.xf_post_k;
     const uint32_t units = ts.rows * H;
     for (uint32_t u0 = static_cast<uint32_t>(warp) * per_warp; u0 < units;
-         u0 += kStageinConsumerWarps * per_warp) {
+         u0 += kXfConsumerWarps * per_warp) {
         const uint32_t u = u0 + sub;
         const bool valid = sub < per_warp && u < units;
-        const uint32_t row = valid ? u / H : 0u;
+        const uint32_t row = !valid ? 0u : (H == 1u ? u : __umulhi(u, a.xf_heads_magic));
         const uint32_t h = valid ? u - row * H : 0u;
-        float v[32];
-        if (valid) {
-            const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
-            load32(x + 32u * j, v);
-            const uint32_t i0 = 32u * j;
-            if (i0 < n_rope) {
-                // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i]
-                const bool lo = i0 < half;
-                float w[32];
-                load32(x + (lo ? i0 + half : i0 - half), w);
-                const float pos = __uint2float_rn(pos0 + row);
-                const float *th = a.theta + (lo ? i0 : i0 - half);
+        float2 P[16];
+        const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
+        // a lane past the last unit reads row 0 and stores nothing; the lanes
+        // of one unit share validity, so its values never reach a valid lane
+        load32(x + 32u * j, lane, P);
+        const uint32_t i0 = 32u * j;
+        if (valid && i0 < n_rope) {
+            // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i];
+            // the partner half is read 8 values at a time
+            const bool lo = i0 < half;
+            const __half *xp = x + (lo ? i0 + half : i0 - half);
+            const float pos = __uint2float_rn(pos0 + row);
+            const float *th = a.theta + (lo ? i0 : i0 - half);
 #pragma unroll
-                for (int m = 0; m < 32; ++m) {
+            for (int c = 0; c < 4; ++c) {
+                const uint4 raw = *reinterpret_cast<const uint4 *>(xp + 8 * c);
+                const __half2 *hw = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
                     float sn, cs;
-                    sincosf(__fmul_rn(pos, th[m]), &sn, &cs);
-                    v[m] = lo ? __fsub_rn(__fmul_rn(v[m], cs), __fmul_rn(w[m], sn))
-                              : __fadd_rn(__fmul_rn(w[m], sn), __fmul_rn(v[m], cs));
+                    sincosf(__fmul_rn(pos, th[8 * c + m]), &sn, &cs);
+                    float &v = (m & 1) ? P[4 * c + (m >> 1)].y : P[4 * c + (m >> 1)].x;
+                    const float w = (m & 1) ? __high2float(hw[m >> 1]) : __low2float(hw[m >> 1]);
+                    v = lo ? __fsub_rn(__fmul_rn(v, cs), __fmul_rn(w, sn))
+                           : __fadd_rn(__fmul_rn(w, sn), __fmul_rn(v, cs));
                 }
             }
-        } else {
-#pragma unroll
-            for (int m = 0; m < 32; ++m) v[m] = 0.0f;
         }
         if (nrot) {
+            if (pre != 1.0f) {
 #pragma unroll
-            for (int m = 0; m < 32; ++m) v[m] = __fmul_rn(v[m], scale);
-            // spans 1 .. 16 inside the lane (fwht_kernel's h loop, ascending)
-#pragma unroll
-            for (int hh = 1; hh < 32; hh <<= 1) {
-#pragma unroll
-                for (int m = 0; m < 32; ++m) {
-                    if ((m & hh) == 0) {
-                        const float p = v[m];
-                        const float q = v[m | hh];
-                        v[m] = __fadd_rn(p, q);
-                        v[m | hh] = __fsub_rn(p, q);
-                    }
-                }
+                for (int k = 0; k < 16; ++k) P[k] = __fmul2_rn(P[k], splat2(pre));
             }
-            // spans 32 .. nrot/2: lane j pairs with lane j ^ (span / 32).  The
-            // lower lane keeps v + p, the upper p - v: fma(+-1, v, p) forms
-            // p +- v exactly before its one rounding, the same value as the
-            // add or the subtraction, in one instruction.
-            for (uint32_t dl = 1; 32u * dl < nrot; dl <<= 1) {
-                const float sgn = (j & dl) != 0u ? -1.0f : 1.0f;
-#pragma unroll
-                for (int m = 0; m < 32; ++m) {
-                    const float p = __shfl_xor_sync(0xffffffffu, v[m], static_cast<int>(dl));
-                    v[m] = __fmaf_rn(sgn, v[m], p);
-                }
+            fwht32_in_lane(P);
+            for (uint32_t dl = 1; 32u * dl < nrot; dl <<= 1) fwht_cross_stage(P, j, dl);
+        }
+        if (valid) {
+            uint8_t *blk = ob + static_cast<size_t>(row) * rb + static_cast<size_t>(h * G + j) * bb;
+            switch (ts.type) {
+                case KVM_TYPE_Q8_0: quant_q8_pairs(P, fs, blk); break;
+                case KVM_TYPE_Q4_0: quant_q4q5_pairs<false>(P, fs, blk); break;
+                case KVM_TYPE_Q5_0: quant_q4q5_pairs<true>(P, fs, blk); break;
+                default: store_f16_pairs(P, fs, blk); break;
             }
         }
-        if (valid)
-            quant_f32_block(ts.type, v, ob + static_cast<size_t>(row) * rb + static_cast<size_t>(h * G + j) * bb);
     }
 }
 
 // Resident CTAs per SM: three for the plain kernel (its shared memory allows
-// three; at most 75 registers a thread), two for the transform variant (16
-// consumer warps to hide its ALU latencies).
+// three; at most 72 registers a thread), two of 8 warps for the transform
+// variant (14 consumer warps; 128 registers a thread keep the packed float
+// pairs in place).
 template <int NS, bool XF>
-__global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(StageinArgs a) {
+__global__ void __launch_bounds__((XF ? kXfConsumerWarps : kStageinConsumerWarps) * 32 + 32, XF ? 2 : 3)
+    stagein_kernel(StageinArgs a) {
+    constexpr int CW = XF ? kXfConsumerWarps : kStageinConsumerWarps;
+    static_assert(3 * NS * 8 <= 128 && 128 + NS * sizeof(TileSlot) <= kStageinHeader, "stage-in header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
@@ -298,14 +429,14 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&done[s], kStageinConsumerWarps);
+            mbar_init(&done[s], CW);
             mbar_init(&ofree[s], 1);
         }
         fence_mbar_init();
     }
     __syncthreads();   // the only CTA-wide barrier
 
-    if (warp == kStageinConsumerWarps) {
+    if (warp == CW) {
         // ---------------------------------------------------------- producer
         uint64_t ptask = blockIdx.x;
         uint32_t issued = 0;      // tiles armed with data
@@ -394,6 +525,11 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
 
     // ------------------------------------------------------------- consumers
     const uint32_t qb_per_row = a.n_embd / 32u;
+    // transform mode: the lane's (unit, block-in-head), fixed for the launch
+    const uint32_t xg = (XF && a.xform) ? a.xform : 1u;
+    const uint32_t xsub = static_cast<uint32_t>(lane) / xg;
+    const uint32_t xj = static_cast<uint32_t>(lane) - xsub * xg;
+    const uint32_t xper = 32u / xg;
     for (uint32_t j = 0;; ++j) {
         const uint32_t s = j % NS;
         if (!mbar_wait_bounded(&full[s], (j / NS) & 1u)) {
@@ -412,7 +548,7 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
         if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
-                transform_tile(a, ts, ib, ob, warp, lane);
+                transform_tile(a, ts, ib, ob, warp, lane, xsub, xj, xper);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done[s]);
@@ -421,7 +557,7 @@ __global__ void __launch_bounds__(kStageinThreads, XF ? 2 : 3) stagein_kernel(St
         }
         const uint32_t nqb = ts.rows * qb_per_row;
         for (uint32_t qb = static_cast<uint32_t>(warp * 32 + lane); qb < nqb;
-             qb += kStageinConsumerWarps * 32u) {
+             qb += CW * 32u) {
             Block32 b;
             load_block(ib, qb, lane, b);
             quant_block(ts.type, b, ob, qb);
@@ -557,9 +693,52 @@ uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens) {
     return r;
 }
 
+void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, uint32_t rot_k,
+                           uint32_t rot_v, uint32_t rope_n_rot, const float *theta) {
+    a.xform = 0;
+    a.rot_k = a.rot_v = a.rope_n_rot = 0;
+    a.theta = nullptr;
+    a.xf_pre_k = a.xf_pre_v = a.xf_post_k = a.xf_post_v = 1.0f;
+    a.xf_heads = 1;
+    a.xf_heads_magic = 0;
+    if (!(rot_k || rot_v || rope_n_rot) || head_dim < 32u) return;
+    a.xform = head_dim / 32u;
+    a.rot_k = rot_k;
+    a.rot_v = rot_v;
+    a.rope_n_rot = rope_n_rot;
+    a.theta = theta;
+    a.xf_heads = n_embd / head_dim;
+    a.xf_heads_magic = a.xf_heads > 1u
+        ? static_cast<uint32_t>(((1ull << 32) + a.xf_heads - 1u) / a.xf_heads) : 0u;
+    // rows a tile such that its (row, head) units fill the 7 consumer warps
+    // evenly when the shape allows, within 30 KiB of input + output a stage
+    const uint32_t per_warp = 32u / a.xform;
+    const uint32_t out_row = a.row_bytes_k > a.row_bytes_v ? a.row_bytes_k : a.row_bytes_v;
+    uint32_t r = (kXfConsumerWarps * per_warp) / (a.xf_heads ? a.xf_heads : 1u);
+    if (r < 1u) r = 1u;
+    while (r > 1u && r * (n_embd * 2u + out_row) > 30u * 1024u) --r;
+    if (r > a.block_tokens) r = a.block_tokens;
+    a.rows_per_tile = r;
+    a.tile_in_bytes = r * n_embd * 2u;
+    a.tile_out_bytes = (r * out_row + 15u) & ~15u;
+    // fwht_kernel's scale, 1 / sqrtf(n), in IEEE single precision.  A power
+    // of two (log2 n even) folds into the quantizer unless RoPE comes first.
+    auto scales = [](uint32_t n, bool rope, float &pre, float &post) {
+        pre = post = 1.0f;
+        if (!n) return;
+        const float sc = 1.0f / std::sqrt(static_cast<float>(n));
+        uint32_t lg = 0;
+        while ((1u << (lg + 1u)) <= n) ++lg;
+        if (!rope && (lg & 1u) == 0u) post = sc;
+        else pre = sc;
+    };
+    scales(rot_k, rope_n_rot != 0u, a.xf_pre_k, a.xf_post_k);
+    scales(rot_v, false, a.xf_pre_v, a.xf_post_v);
+}
+
 size_t stagein_smem_bytes(const StageinArgs &a) {
-    return kStageinHeader +
-           static_cast<size_t>(kStageinStages) * (a.tile_in_bytes + a.tile_out_bytes);
+    const int ns = a.xform ? kXfStages : kStageinStages;
+    return kStageinHeader + static_cast<size_t>(ns) * (a.tile_in_bytes + a.tile_out_bytes);
 }
 
 // Dynamic shared-memory opt-in is a per-device function attribute: set it
@@ -583,16 +762,18 @@ static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, u
                                     std::atomic<uint64_t> &attr) {
     const size_t smem = stagein_smem_bytes(a);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    const void *fn = reinterpret_cast<const void *>(stagein_kernel<kStageinStages, XF>);
+    constexpr int NS = XF ? kXfStages : kStageinStages;
+    const void *fn = reinterpret_cast<const void *>(stagein_kernel<NS, XF>);
     if (!attr_once(attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<kStageinStages, XF>,
-                                                  kStageinThreads, smem);
+    const int threads = XF ? kXfThreads : kStageinThreads;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<NS, XF>,
+                                                  threads, smem);
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    stagein_kernel<kStageinStages, XF><<<grid, kStageinThreads, smem, stream>>>(a);
+    stagein_kernel<NS, XF><<<grid, threads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
