@@ -42,6 +42,37 @@ __device__ __forceinline__ uint32_t f16_bits(float d) {
     return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(d)));
 }
 
+// Packed FP32x2 arithmetic (sm_100) issued as PTX; per component each is the
+// IEEE operation with the named rounding.  A packed multiply whose result
+// feeds a packed add was observed fused into one FFMA2 -- the product's
+// rounding lost -- both through the CUDA __fmul2_rn / __fadd2_rn intrinsics
+// and through these .rn wrappers, so every product that an add consumes is a
+// scalar __fmul_rn (never merged into a multiply-add); the packed ops below
+// only add, or multiply by a power of two (exact).
+#define KVM_F2_OP(name, op)                                                               \
+    __device__ __forceinline__ float2 name(float2 a, float2 b) {                         \
+        float2 d;                                                                         \
+        asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" \
+            op " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                              \
+            : "=f"(d.x), "=f"(d.y)                                                        \
+            : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                    \
+        return d;                                                                         \
+    }
+KVM_F2_OP(f2_mul_rn, "mul.rn.f32x2")
+KVM_F2_OP(f2_add_rn, "add.rn.f32x2")
+KVM_F2_OP(f2_add_rz, "add.rz.f32x2")
+#undef KVM_F2_OP
+
+// a*b + c per component with one rounding (fused by definition).
+__device__ __forceinline__ float2 f2_fma_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // amax / 127.0f, correctly rounded, for amax >= 0: Markstein's correction
 // step (P. Markstein, "IA-64 and Elementary Functions", 2000) with the
 // correctly rounded reciprocal r = RN(1/127): q0 = RN(a*r) is within an ulp of
@@ -141,23 +172,40 @@ __device__ __forceinline__ void quant_q8_0(const Block32 &b, uint8_t *blk) {
     }
 }
 
-// Nibble / 5-bit code of one value: min(maxq, (int)(x*id + off)).
-__device__ __forceinline__ uint32_t code_q(float x, float id, float off, int maxq) {
-    const int q = __float2int_rz(__fadd_rn(__fmul_rn(x, id), off));
-    return static_cast<uint32_t>(q > maxq ? maxq : q);
+// Byte codes min(MAXQ, (int)t) of four values t >= 0 (the reference's
+// `(int)(x*id + off)` and its clamp), MAXQ = 15 or 31.  (int)t for 0 <= t <
+// 2^23 is the low byte of RZ(t + 2^23): that sum has an ulp of 1, so rounding
+// toward zero drops exactly the fraction.  MAXQ + 1 is the only larger code
+// (t is at most MAXQ + 1.5) and is lowered by one.  A NaN t (a NaN or
+// infinite input) gives the canonical NaN, low byte 0xff, and code 0, as the
+// float-to-int conversion does.
+template <int MAXQ>
+__device__ __forceinline__ uint32_t codes4(float2 t0, float2 t1) {
+    static_assert(MAXQ == 15 || MAXQ == 31, "MAXQ");
+    const float2 mg = make_float2(0x1p23f, 0x1p23f);
+    const float2 u0 = f2_add_rz(t0, mg);
+    const float2 u1 = f2_add_rz(t1, mg);
+    uint32_t v = __byte_perm(__byte_perm(__float_as_uint(u0.x), __float_as_uint(u0.y), 0x0040u),
+                             __byte_perm(__float_as_uint(u1.x), __float_as_uint(u1.y), 0x0040u), 0x5410u);
+    v &= ~(((v >> 7) & 0x01010101u) * 0xffu);
+    return v - ((v >> (MAXQ == 15 ? 4 : 5)) & 0x01010101u);
+}
+
+// RN(RN(x*id) + off) for a pair: the products scalar and rounded, the add packed.
+__device__ __forceinline__ float2 mul_add_off(float2 x, float id, float2 off) {
+    return f2_add_rn(make_float2(__fmul_rn(x.x, id), __fmul_rn(x.y, id)), off);
 }
 
 // The 8 codes of one chunk as bytes: word p holds values 4p .. 4p+3.
-__device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, int maxq,
-                                                 uint32_t (&w)[2]) {
+template <int MAXQ>
+__device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, uint32_t (&w)[2]) {
     const __half2 *h = halves(r);
+    const float2 off2 = make_float2(off, off);
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
-        const float2 x0 = __half22float2(h[2 * p]);
-        const float2 x1 = __half22float2(h[2 * p + 1]);
-        const uint32_t c0 = code_q(x0.x, id, off, maxq), c1 = code_q(x0.y, id, off, maxq);
-        const uint32_t c2 = code_q(x1.x, id, off, maxq), c3 = code_q(x1.y, id, off, maxq);
-        w[p] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+        const float2 t0 = mul_add_off(__half22float2(h[2 * p]), id, off2);
+        const float2 t1 = mul_add_off(__half22float2(h[2 * p + 1]), id, off2);
+        w[p] = codes4<MAXQ>(t0, t1);
     }
 }
 
@@ -202,10 +250,9 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
     const float d = __fmul_rn(vmax, Q5 ? -0.0625f : -0.125f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     const float off = Q5 ? 16.5f : 8.5f;
-    const int maxq = Q5 ? 31 : 15;
     uint32_t w[4][2];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) chunk_code_bytes(b.raw[k], id, off, maxq, w[k]);
+    for (int k = 0; k < 4; ++k) chunk_code_bytes<Q5 ? 31 : 15>(b.raw[k], id, off, w[k]);
     st_u16(blk, f16_bits(d));
     uint8_t *qs = blk + (Q5 ? 6 : 2);
 #pragma unroll

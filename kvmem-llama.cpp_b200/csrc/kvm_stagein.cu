@@ -120,9 +120,9 @@ constexpr uint32_t kStageinHeader = 384;
 // lane index), and each lane quantizes its own block in the reference's
 // order.  The lane keeps its values as 16 float pairs, P[k] = (v[2k],
 // v[2k+1]), so that all butterflies of span >= 2, the cross-lane stages and
-// the quantizer's multiplies run on sm_100's packed FP32x2 instructions
-// (__fadd2_rn, __ffma2_rn, __fmul2_rn: per component the same IEEE operation
-// as the scalar one).  Every float operation rounds to nearest, so the
+// the quantizer's adds run on sm_100's packed FP32x2 instructions (f2_add_rn,
+// f2_fma_rn: per component the same IEEE operation as the scalar one).  Every
+// product that an add consumes is a scalar __fmul_rn, so its rounding stays.  Every float operation rounds to nearest, so the
 // Hadamard and the quantizers match the CPU bit for bit; RoPE calls the CUDA
 // sincosf (as the reference's GPU kernel does) and agrees with the host cosf /
 // sinf to within their last-bit errors.
@@ -159,9 +159,10 @@ __device__ __forceinline__ void store_block(uint8_t *blk, uint32_t hdr, const ui
 
 __device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
 
-// C roundf of both components, as integers (|x| < 2^23).
+// C roundf of both components, as integers (|x| < 2^23).  y must come from
+// a rounded product (scalar __fmul_rn), never from a packed multiply.
 __device__ __forceinline__ void round_half_away2(float2 y, int &q0, int &q1) {
-    const float2 t = __fadd2_rn(y, make_float2(copysignf(0x1.fffffep-2f, y.x), copysignf(0x1.fffffep-2f, y.y)));
+    const float2 t = f2_add_rn(y, make_float2(copysignf(0x1.fffffep-2f, y.x), copysignf(0x1.fffffep-2f, y.y)));
     q0 = __float2int_rz(t.x);
     q1 = __float2int_rz(t.y);
 }
@@ -181,13 +182,13 @@ __device__ __forceinline__ void quant_q8_pairs(const float2 (&P)[16], float fs, 
     }
     const float amax = __fmul_rn(fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)), fs);
     const float d = div127(amax);
-    const float2 id = splat2(d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f);
+    const float id = d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f;
     uint32_t w[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         int q0, q1, q2, q3;
-        round_half_away2(__fmul2_rn(P[2 * k], id), q0, q1);
-        round_half_away2(__fmul2_rn(P[2 * k + 1], id), q2, q3);
+        round_half_away2(make_float2(__fmul_rn(P[2 * k].x, id), __fmul_rn(P[2 * k].y, id)), q0, q1);
+        round_half_away2(make_float2(__fmul_rn(P[2 * k + 1].x, id), __fmul_rn(P[2 * k + 1].y, id)), q2, q3);
         w[k] = pack4(q0, q1, q2, q3);
     }
     store_block<8>(blk, f16_bits(d), w);
@@ -222,17 +223,12 @@ __device__ __forceinline__ void quant_q4q5_pairs(const float2 (&P)[16], float fs
         }
     }
     const float d = __fmul_rn(__fmul_rn(vmax, fs), Q5 ? -0.0625f : -0.125f);
-    const float2 id = splat2(d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f);
+    const float id = d != 0.0f ? __fmul_rn(__frcp_rn(d), fs) : 0.0f;
     const float2 off = splat2(Q5 ? 16.5f : 8.5f);
-    const int maxq = Q5 ? 31 : 15;
     uint32_t c[8];   // byte codes: word k holds values 4k .. 4k+3
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const float2 t0 = __fadd2_rn(__fmul2_rn(P[2 * k], id), off);
-        const float2 t1 = __fadd2_rn(__fmul2_rn(P[2 * k + 1], id), off);
-        c[k] = pack4(min(__float2int_rz(t0.x), maxq), min(__float2int_rz(t0.y), maxq),
-                     min(__float2int_rz(t1.x), maxq), min(__float2int_rz(t1.y), maxq));
-    }
+    for (int k = 0; k < 8; ++k)
+        c[k] = codes4<Q5 ? 31 : 15>(mul_add_off(P[2 * k], id, off), mul_add_off(P[2 * k + 1], id, off));
     // byte j of the nibbles: value j on the low nibble, value j + 16 on the high
     constexpr int NW = Q5 ? 5 : 4;
     uint32_t w[NW];
@@ -251,7 +247,7 @@ __device__ __forceinline__ void quant_q4q5_pairs(const float2 (&P)[16], float fs
 __device__ __forceinline__ void store_f16_pairs(const float2 (&P)[16], float fs, uint8_t *blk) {
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-        const float2 x = __fmul2_rn(P[k], splat2(fs));
+        const float2 x = f2_mul_rn(P[k], splat2(fs));
         st_u16(blk + 4 * k, f16_bits(x.x));
         st_u16(blk + 4 * k + 2, f16_bits(x.y));
     }
@@ -303,8 +299,8 @@ __device__ __forceinline__ void fwht32_in_lane(float2 (&P)[16]) {
         for (int k = 0; k < 16; ++k) {
             if ((k & hp) == 0) {
                 const float2 a = P[k], b = P[k | hp];
-                P[k] = __fadd2_rn(a, b);
-                P[k | hp] = __ffma2_rn(b, neg, a);
+                P[k] = f2_add_rn(a, b);
+                P[k | hp] = f2_fma_rn(b, neg, a);
             }
         }
     }
@@ -324,7 +320,7 @@ __device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, ui
             static_cast<int>(dl));
         const float2 p = make_float2(__uint_as_float(static_cast<uint32_t>(b)),
                                      __uint_as_float(static_cast<uint32_t>(b >> 32)));
-        P[k] = __ffma2_rn(sgn, P[k], p);
+        P[k] = f2_fma_rn(sgn, P[k], p);
     }
 }
 
@@ -383,7 +379,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
         if (nrot) {
             if (pre != 1.0f) {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) P[k] = __fmul2_rn(P[k], splat2(pre));
+                for (int k = 0; k < 16; ++k) P[k] = make_float2(__fmul_rn(P[k].x, pre), __fmul_rn(P[k].y, pre));
             }
             fwht32_in_lane(P);
             for (uint32_t dl = 1; 32u * dl < nrot; dl <<= 1) fwht_cross_stage(P, j, dl);

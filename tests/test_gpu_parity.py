@@ -64,6 +64,61 @@ def test_quantize_rows_wide_and_narrow(kvm_lib, oracle):
                                   oracle.quantize_rows_f16(t, rows)), (E, t)
 
 
+@pytest.mark.parametrize("type_id", [8, 2, 6])
+def test_quantize_rows_many(kvm_lib, oracle, type_id):
+    """8M values: a contracted multiply-add in the code computation changes a
+    q4_0 / q5_0 code a few times per million values."""
+    torch = _cuda()
+    rng = np.random.default_rng(40 + type_id)
+    n, E = 8192, 1024
+    rows = oracle.synth_f16(rng, (n, E), E)
+    src = torch.from_numpy(rows).cuda()
+    rb = kvm_lib.row_bytes(type_id, E)
+    dst = torch.zeros(n * rb, dtype=torch.uint8, device="cuda")
+    kvm_lib.quantize_rows(type_id, src.data_ptr(), n, E, dst.data_ptr())
+    assert np.array_equal(dst.cpu().numpy().reshape(n, rb), oracle.quantize_rows_f16(type_id, rows))
+
+
+def _edge_rows():
+    """Blocks at the quantizers' boundaries: zeros and -0, +a/-a magnitude
+    ties (q4/q5 keep the first), F16 max and subnormals, and scales where
+    x*id + off lands exactly on integers and half-integers."""
+    f = np.float16
+    E = 256
+    rows = []
+    rows.append(np.zeros(E, f))
+    rows.append(np.full(E, -0.0, f))
+    r = np.zeros(E, np.float32)
+    for blk in range(E // 32):                   # tie at varying positions, either sign first
+        r[blk * 32 + (blk * 5) % 32] = 3.0 if blk % 2 else -3.0
+        r[blk * 32 + (blk * 11 + 7) % 32] = -3.0 if blk % 2 else 3.0
+        r[blk * 32 + (blk * 3 + 1) % 32] = 1.5
+    rows.append(r.astype(f))
+    rows.append(np.tile(np.array([65504.0, -65504.0, 1.0, -0.5], f), E // 4))
+    rows.append((np.arange(E) % 17 - 8).astype(f) * f(2.0 ** -24))          # subnormal F16
+    rows.append((np.arange(E) % 32 - 16).astype(np.float32).astype(f) * f(0.5))  # vmax -8: id 1
+    rows.append((np.arange(E) % 32 - 15.5).astype(f))                            # half-integers
+    rows.append(np.where(np.arange(E) % 32 == 0, -16.0, (np.arange(E) % 33) - 16.0).astype(f))
+    # x*id rounds to exactly -7.5 (q4_0: x0 + 8.5 = 1.0); a multiply-add fused
+    # without the product's rounding gives 0.99999976 and code 0 instead of 1
+    blk = np.zeros(32, np.float32)
+    blk[21], blk[26], blk[0] = -2.578125, -2.75, -2.263671875
+    rows.append(np.tile(blk, E // 32).astype(f))
+    return np.stack(rows)
+
+
+@pytest.mark.parametrize("type_id", [8, 2, 6])
+def test_quantize_rows_edge_values(kvm_lib, oracle, type_id):
+    torch = _cuda()
+    rows = _edge_rows()
+    n, E = rows.shape
+    src = torch.from_numpy(rows).cuda()
+    rb = kvm_lib.row_bytes(type_id, E)
+    dst = torch.zeros(n * rb, dtype=torch.uint8, device="cuda")
+    kvm_lib.quantize_rows(type_id, src.data_ptr(), n, E, dst.data_ptr())
+    assert np.array_equal(dst.cpu().numpy().reshape(n, rb), oracle.quantize_rows_f16(type_id, rows))
+
+
 # --------------------------------------------------------------- scorer ---
 
 def test_score_bitexact_uploaded_summaries(kvm_lib, oracle):

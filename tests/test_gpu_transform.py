@@ -11,7 +11,7 @@ L = 2
 
 
 class TRig:
-    def __init__(self, kvm, torch, oracle, H, D, T, B, tk, tv, seed, host=False):
+    def __init__(self, kvm, torch, oracle, H, D, T, B, tk, tv, seed, host=False, budget_blocks=8):
         self.kvm, self.torch, self.O = kvm, torch, oracle
         self.H, self.D, self.T, self.B, self.tk, self.tv = H, D, T, B, tk, tv
         E = self.E = H * D
@@ -24,7 +24,8 @@ class TRig:
         else:
             self.hk = torch.from_numpy(self.hk_np).cuda()
             self.hv = torch.from_numpy(self.hv_np).cuda()
-        cfg = kvm.default_config(block_tokens=T, select_budget=8 * T, gen_reserve=2 * T, sink_blocks=1,
+        cfg = kvm.default_config(block_tokens=T, select_budget=budget_blocks * T, gen_reserve=2 * T,
+                                 sink_blocks=1,
                                  n_layer=L, n_head_kv=H, head_dim=D, n_head_q=2 * H,
                                  max_blocks=B + 4, type_k=tk, type_v=tv)
         self.s = kvm.Session(cfg, 0)
@@ -96,6 +97,32 @@ def test_attn_rot_stagein_bit_exact(kvm_lib, oracle, case):
         sel = r.step()
         b = int(sel[1])
         assert np.array_equal(r.window(0, 0, 1), oracle.quantize_rows_f16(tk, r.hk_np[0, b]))
+    finally:
+        r.close()
+
+
+@pytest.mark.parametrize("tk,tv", [(8, 2), (6, 6)])
+def test_attn_rot_many_values(kvm_lib, oracle, tk, tv):
+    """About 25M values through the attn_rot stage-in: a product rounded
+    together with the following add (a contracted multiply-add) changes a
+    q4_0 / q5_0 code a few times per million values, so this size catches it."""
+    import torch
+    H, D, T, B = 4, 256, 128, 56
+    r = TRig(kvm_lib, torch, oracle, H, D, T, B, tk, tv, seed=31 + tk, budget_blocks=48)
+    try:
+        rot_k, rot_v = kvm_lib.attn_rot_nrot(tk, D, True), kvm_lib.attn_rot_nrot(tv, D, False)
+        r.s.set_transform(rot_k=rot_k, rot_v=rot_v)
+        sel = r.step()
+        assert sel.size >= 40
+        for l in range(L):
+            got_k = r.wk[l, :sel.size * T * r.rbk].cpu().numpy().reshape(sel.size, T, r.rbk)
+            got_v = r.wv[l, :sel.size * T * r.rbv].cpu().numpy().reshape(sel.size, T, r.rbv)
+            for slot in range(sel.size):
+                b = int(sel[slot])
+                k = oracle.transform_quantize_rows(tk, r.hk_np[l, b], H, D, nrot=rot_k)
+                v = oracle.transform_quantize_rows(tv, r.hv_np[l, b], H, D, nrot=rot_v)
+                assert np.array_equal(got_k[slot], k), ("K", slot, l)
+                assert np.array_equal(got_v[slot], v), ("V", slot, l)
     finally:
         r.close()
 
