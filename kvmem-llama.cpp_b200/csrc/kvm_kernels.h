@@ -11,10 +11,10 @@ namespace kvm {
 
 constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
-// Transform mode: 7 consumer warps + the producer, so that two CTAs (16 warps,
-// four per scheduler) leave 128 registers a thread for the packed butterflies.
+// Transform mode without RoPE: 7 consumer warps + the producer, so that two
+// CTAs (16 warps, four per scheduler) leave 128 registers a thread for the
+// packed butterflies.
 constexpr int kXfConsumerWarps = 7;
-constexpr int kXfThreads = (kXfConsumerWarps + 1) * 32;
 constexpr int kStageinStages = 3;
 constexpr int kXfStages = 5;       // transform mode: ALU-heavier tiles, loads further ahead
 constexpr int kPermuteThreads = 512;

@@ -112,6 +112,24 @@ static_assert(sizeof(TileSlot) == 24, "TileSlot");
 // tile slots; then NS input tiles and NS output tiles.
 constexpr uint32_t kStageinHeader = 384;
 
+// Shared-memory copy of the RoPE frequencies (transform mode), between the
+// header and the tiles; a multiple of 128 bytes so the tiles stay aligned.
+__host__ __device__ inline uint32_t stagein_theta_bytes(const StageinArgs &a) {
+    return (a.xform && a.rope_n_rot) ? ((a.rope_n_rot / 2u) * 4u + 127u) & ~127u : 0u;
+}
+
+// Pipeline depth: transform tiles are ALU-heavier, so their loads run further
+// ahead -- except with RoPE, whose sincosf wants the L1 that a deeper
+// pipeline's shared memory would take.
+__host__ __device__ inline int stagein_stages(const StageinArgs &a) {
+    return !a.xform ? kStageinStages : (a.rope_n_rot ? kStageinStages : kXfStages);
+}
+
+// Consumer warps of a launch (see stagein_kernel).
+__host__ __device__ inline int stagein_consumer_warps(const StageinArgs &a) {
+    return (a.xform && !a.rope_n_rot) ? kXfConsumerWarps : kStageinConsumerWarps;
+}
+
 // ------------------------------------------------------- transform mode --
 //
 // A lane owns one ggml block -- 32 consecutive values of one head of one row
@@ -326,9 +344,10 @@ __device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, ui
 
 // (sub, j): the lane's unit within the warp and its block within the head;
 // per_warp = 32 / xform units a warp-iteration.
+template <int CW>
 __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
                                                uint8_t *ob, int warp, int lane, uint32_t sub, uint32_t j,
-                                               uint32_t per_warp) {
+                                               uint32_t per_warp, const float *theta_s) {
     const bool is_v = (ts.meta >> 31) != 0u;
     const uint32_t pos0 = ts.meta & 0x7fffffffu;
     const uint32_t nrot = is_v ? a.rot_v : a.rot_k;
@@ -343,7 +362,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
     const float fs = is_v ? a.xf_post_v : a.xf_post_k;
     const uint32_t units = ts.rows * H;
     for (uint32_t u0 = static_cast<uint32_t>(warp) * per_warp; u0 < units;
-         u0 += kXfConsumerWarps * per_warp) {
+         u0 += CW * per_warp) {
         const uint32_t u = u0 + sub;
         const bool valid = sub < per_warp && u < units;
         const uint32_t row = !valid ? 0u : (H == 1u ? u : __umulhi(u, a.xf_heads_magic));
@@ -360,7 +379,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
             const bool lo = i0 < half;
             const __half *xp = x + (lo ? i0 + half : i0 - half);
             const float pos = __uint2float_rn(pos0 + row);
-            const float *th = a.theta + (lo ? i0 : i0 - half);
+            const float *th = theta_s + (lo ? i0 : i0 - half);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const uint4 raw = *reinterpret_cast<const uint4 *>(xp + 8 * c);
@@ -396,21 +415,21 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
     }
 }
 
-// Resident CTAs per SM: three for the plain kernel (its shared memory allows
-// three; at most 72 registers a thread), two of 8 warps for the transform
-// variant (14 consumer warps; 128 registers a thread keep the packed float
-// pairs in place).
-template <int NS, bool XF>
-__global__ void __launch_bounds__((XF ? kXfConsumerWarps : kStageinConsumerWarps) * 32 + 32, XF ? 2 : 3)
-    stagein_kernel(StageinArgs a) {
-    constexpr int CW = XF ? kXfConsumerWarps : kStageinConsumerWarps;
+// CW consumer warps + the producer.  Resident CTAs per SM: three for the
+// plain kernel (its shared memory allows three; at most 72 registers a
+// thread), two for the transform variants: 7 consumer warps for attn_rot (16
+// warps an SM leave 128 registers a thread, which keep the packed float pairs
+// in place), 8 with RoPE, whose sincosf latencies want the extra warps more.
+template <int NS, bool XF, int CW>
+__global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(StageinArgs a) {
     static_assert(3 * NS * 8 <= 128 && 128 + NS * sizeof(TileSlot) <= kStageinHeader, "stage-in header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
     uint64_t *ofree = done + NS;   // phase k of ofree[s]: the store of tile s + k*NS has read out[s]
     TileSlot *slot = reinterpret_cast<TileSlot *>(smem + 128);
-    uint8_t *in_buf = smem + kStageinHeader;
+    float *theta_s = reinterpret_cast<float *>(smem + kStageinHeader);   // RoPE frequencies
+    uint8_t *in_buf = smem + kStageinHeader + stagein_theta_bytes(a);
     uint8_t *out_buf = in_buf + NS * a.tile_in_bytes;
 
     const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
@@ -422,6 +441,10 @@ __global__ void __launch_bounds__((XF ? kXfConsumerWarps : kStageinConsumerWarps
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    if (XF && a.rope_n_rot) {
+        for (uint32_t i = static_cast<uint32_t>(tid); i < a.rope_n_rot / 2u; i += blockDim.x)
+            theta_s[i] = a.theta[i];
+    }
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -544,7 +567,7 @@ __global__ void __launch_bounds__((XF ? kXfConsumerWarps : kStageinConsumerWarps
         if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
-                transform_tile(a, ts, ib, ob, warp, lane, xsub, xj, xper);
+                transform_tile<CW>(a, ts, ib, ob, warp, lane, xsub, xj, xper, theta_s);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done[s]);
@@ -706,11 +729,11 @@ void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, u
     a.xf_heads = n_embd / head_dim;
     a.xf_heads_magic = a.xf_heads > 1u
         ? static_cast<uint32_t>(((1ull << 32) + a.xf_heads - 1u) / a.xf_heads) : 0u;
-    // rows a tile such that its (row, head) units fill the 7 consumer warps
+    // rows a tile such that its (row, head) units fill the consumer warps
     // evenly when the shape allows, within 30 KiB of input + output a stage
     const uint32_t per_warp = 32u / a.xform;
     const uint32_t out_row = a.row_bytes_k > a.row_bytes_v ? a.row_bytes_k : a.row_bytes_v;
-    uint32_t r = (kXfConsumerWarps * per_warp) / (a.xf_heads ? a.xf_heads : 1u);
+    uint32_t r = (static_cast<uint32_t>(stagein_consumer_warps(a)) * per_warp) / (a.xf_heads ? a.xf_heads : 1u);
     if (r < 1u) r = 1u;
     while (r > 1u && r * (n_embd * 2u + out_row) > 30u * 1024u) --r;
     if (r > a.block_tokens) r = a.block_tokens;
@@ -733,8 +756,8 @@ void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, u
 }
 
 size_t stagein_smem_bytes(const StageinArgs &a) {
-    const int ns = a.xform ? kXfStages : kStageinStages;
-    return kStageinHeader + static_cast<size_t>(ns) * (a.tile_in_bytes + a.tile_out_bytes);
+    return kStageinHeader + stagein_theta_bytes(a) +
+           static_cast<size_t>(stagein_stages(a)) * (a.tile_in_bytes + a.tile_out_bytes);
 }
 
 // Dynamic shared-memory opt-in is a per-device function attribute: set it
@@ -753,35 +776,39 @@ static bool attr_once(std::atomic<uint64_t> &done, const void *fn, int bytes) {
 static std::atomic<uint64_t> g_stagein_attr{0};
 static std::atomic<uint64_t> g_permute_attr{0};
 
-template <bool XF>
+template <int NS, bool XF, int CW>
 static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap,
                                     std::atomic<uint64_t> &attr) {
     const size_t smem = stagein_smem_bytes(a);
-    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    constexpr int NS = XF ? kXfStages : kStageinStages;
-    const void *fn = reinterpret_cast<const void *>(stagein_kernel<NS, XF>);
+    if (smem > 200u * 1024u || stagein_stages(a) != NS || stagein_consumer_warps(a) != CW)
+        return cudaErrorInvalidValue;
+    const void *fn = reinterpret_cast<const void *>(stagein_kernel<NS, XF, CW>);
     if (!attr_once(attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
     int per_sm = 1;
-    const int threads = XF ? kXfThreads : kStageinThreads;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<NS, XF>,
+    const int threads = CW * 32 + 32;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<NS, XF, CW>,
                                                   threads, smem);
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    stagein_kernel<NS, XF><<<grid, threads, smem, stream>>>(a);
+    stagein_kernel<NS, XF, CW><<<grid, threads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
 static std::atomic<uint64_t> g_xform_attr{0};
+static std::atomic<uint64_t> g_xform_rope_attr{0};
 
 cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
-    if (a.xform == 0) return launch_stagein_t<false>(a, stream, grid_cap, g_stagein_attr);
+    if (a.xform == 0)
+        return launch_stagein_t<kStageinStages, false, kStageinConsumerWarps>(a, stream, grid_cap, g_stagein_attr);
     // lanes of a (row, head) must tile the warp's xor pairs: head_dim / 32 in
     // 1 .. 32 and, for every Hadamard size, a multiple of size / 32
     if (a.xform > 32u || (a.rot_k && a.xform % (a.rot_k / 32u)) || (a.rot_v && a.xform % (a.rot_v / 32u)))
         return cudaErrorInvalidValue;
-    return launch_stagein_t<true>(a, stream, grid_cap, g_xform_attr);
+    if (a.rope_n_rot)
+        return launch_stagein_t<kStageinStages, true, kStageinConsumerWarps>(a, stream, grid_cap, g_xform_rope_attr);
+    return launch_stagein_t<kXfStages, true, kXfConsumerWarps>(a, stream, grid_cap, g_xform_attr);
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
