@@ -73,7 +73,8 @@ def parse():
     ap.add_argument("--combine", choices=("allgather", "allreduce"), default="allgather")
     ap.add_argument("--config", type=int, choices=(1, 2), default=2,
                     help="2: BASELINE configs[1] (16 layers, the bench line); "
-                         "1: configs[0] (one layer, the small profiling case)")
+                         "1: configs[0] (one layer, the small profiling case; with "
+                         "--mode incremental, 2048 blocks x 4 layers)")
     return ap.parse_args()
 
 
@@ -695,7 +696,12 @@ def run_incremental(args):
     import kvm
     world, rank, local, dev, dist = _dist_init(torch)
     c = dict(CFG2)
-    B, L, T = 8192, c["n_layer"], c["block_tokens"]
+    B = 8192
+    if args.config == 1:
+        # the small profiling case: 2048 blocks x 4 layers (4.3 GB of history),
+        # still ~170 MB of moves a step, above the 126 MB L2
+        B, c["n_layer"] = 2048, 4
+    L, T = c["n_layer"], c["block_tokens"]
     c["n_blocks"] = B
     E = c["n_head_kv"] * c["head_dim"]
     steps = 40 if args.steps == 200 else args.steps
@@ -761,7 +767,7 @@ def run_incremental(args):
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16->q8_0",
             "data": "synthetic: seeded F16 history, drifting seeded queries",
-            "config": {"workload": "config 4: 1048576-token session (8192 blocks) x 16 layers, "
+            "config": {"workload": f"config 4: {B * T}-token session ({B} blocks) x {L} layers, "
                                    "q8_0 K+V, budget 32768, 40 incremental reselections, window kept",
                        "parallelism": f"sessions x{world}"},
             "per_step_ms": {"mean": round(statistics.mean(per_step), 4),

@@ -156,12 +156,21 @@ struct PermuteArgs {
     uint32_t col_bytes;            // widest column a CTA stages (bytes, multiple of 16)
     uint32_t col_region;           // shared-memory bytes for the staged columns
     uint32_t vec16;
+    uint32_t piece;                // streaming permute: bytes of a block span a stream moves
     uint32_t *status;
 };
 
 // shared-memory bytes of the per-move metadata table (12 bytes a move, 16-aligned)
 __host__ __device__ inline size_t permute_meta_bytes(uint32_t max_moves) {
     return (static_cast<size_t>(max_moves) * 12u + 15u) & ~static_cast<size_t>(15u);
+}
+
+// Streaming permute: ring depth and the offset of its buffers in shared
+// memory (a 256-byte header, the move table, the processing order).
+constexpr int kChainStages = 4;
+__host__ __device__ inline size_t permute_chain_buf_offset(uint32_t max_moves) {
+    return (256u + permute_meta_bytes(max_moves) + 2u * static_cast<size_t>(max_moves) + 127u) &
+           ~static_cast<size_t>(127u);
 }
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream);
 

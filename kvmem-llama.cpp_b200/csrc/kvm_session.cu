@@ -279,12 +279,22 @@ kvm_status launch_moves(kvm_session *s, cudaStream_t st) {
     p.row_bytes_v = s->row_bytes_v;
     p.span_k = s->row_bytes_k * s->cfg.block_tokens;
     p.span_v = s->row_bytes_v * s->cfg.block_tokens;
-    // the kernel sizes its column from the device move count: any count up to
-    // n_slots fits 96 KiB at 16 bytes or more a move
-    p.col_region = std::max<uint32_t>(96u * 1024u, 16u * s->n_slots);
-    p.col_bytes = 2048u;
+    // aligned windows: the streaming kernel, each (layer, K|V, piece) a stream,
+    // pieces sized for about three streams an SM (2-16 KiB); otherwise the
+    // SIMT column kernel, which sizes its column from the device move count
+    // (any count up to n_slots fits 96 KiB at 16 bytes or more a move)
     p.vec16 = (p.span_k % 16u == 0 && p.span_v % 16u == 0 && s->row_bytes_k % 16u == 0 &&
                s->row_bytes_v % 16u == 0 && window_aligned16(s)) ? 1u : 0u;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->device) != cudaSuccess || sms < 1)
+        sms = 148;
+    const uint64_t all = static_cast<uint64_t>(p.n_layer) * (p.span_k + p.span_v);
+    uint64_t piece = (all / (3u * static_cast<uint64_t>(sms))) & ~static_cast<uint64_t>(15u);
+    piece = std::min<uint64_t>(16384u, std::max<uint64_t>(2048u, piece));
+    piece = std::max<uint64_t>(piece, (4u * s->n_slots + kChainStages - 1u) / kChainStages * 4u);
+    p.piece = static_cast<uint32_t>((piece + 15u) & ~static_cast<uint64_t>(15u));
+    p.col_region = std::max<uint32_t>(96u * 1024u, 16u * s->n_slots);
+    p.col_bytes = 2048u;
     p.status = s->d_status;
     KVM_CUDA(s, launch_permute(p, st), "permute launch");
     s->launches++;

@@ -289,6 +289,56 @@ def test_step_window_bytes(kvm_lib, oracle, tk, tv):
             assert moves.shape[0] > 0 or cold.shape[0] < sel.size
 
 
+def test_step_after_scrambled_slots(kvm_lib, oracle):
+    """A layout that is not chronological (kvm_set_block_gpu_slot reversing the
+    resident blocks' slots, the window bytes permuted to match): the next
+    step's moves are not monotone, so the streaming permute must take its
+    order-free column path; the window must still match the oracle."""
+    torch = _cuda()
+    shape = Shape(n_layer=2, n_blocks=64, block_tokens=32, budget_blocks=12, gen_blocks=4,
+                  partial_tokens=20)
+    rig = make_rig(shape, seed=17)
+    om = OracleModel(rig)
+    rng = np.random.default_rng(18)
+    q, qc = make_query(shape, rng)
+    rig.sess.set_query(q, qc)
+    rig.sess.step(rig.src, rig.k_bases(), rig.v_bases())
+    om.step(q, qc)
+    _check_window(rig, om)
+    # reverse the slots of the resident blocks, on the device and in the oracle
+    res = np.nonzero(om.blocks.gpu_slot >= 0)[0]
+    old = om.blocks.gpu_slot[res].copy()
+    new = old[::-1].copy()
+    L, T = shape.n_layer, shape.block_tokens
+    for win_t, win_np, rb in ((rig.win_k, om.win_k, om.rbk), (rig.win_v, om.win_v, om.rbv)):
+        span = T * rb
+        dev = win_t.view(L, -1, span)
+        snap_d = dev.clone()
+        host = win_np.reshape(L, -1, span)
+        snap_h = host.copy()
+        for o, n in zip(old, new):
+            dev[:, n] = snap_d[:, o]
+            host[:, n] = snap_h[:, o]
+    for b, n in zip(res, new):
+        rig.sess.set_block_gpu_slot(int(b), int(n))
+        om.blocks.gpu_slot[b] = n
+    torch.cuda.synchronize()
+    for step in range(2):
+        q2, _ = make_query(shape, rng)
+        q = (0.85 * q + 0.5 * q2).astype(np.float32)
+        rig.sess.set_query(q, qc)
+        rig.sess.step(rig.src, rig.k_bases(), rig.v_bases())
+        _, sel, plan, moves, cold = om.step(q, qc)
+        got = rig.sess.plan()
+        assert np.array_equal(got["selected"], sel)
+        assert np.array_equal(np.stack([got["mv_block"], got["mv_from"], got["mv_to"]], 1)
+                              .astype(np.int64), moves.astype(np.int64))
+        if step == 0:
+            assert moves.shape[0] > 1 and np.any(np.diff(moves[:, 1]) < 0)   # not monotone
+        _check_window(rig, om)
+    rig.sess.wait()                     # raises on a device error status
+
+
 def test_step_host_source(kvm_lib, oracle):
     torch = _cuda()
     shape = Shape(n_layer=2, n_blocks=48, block_tokens=32, budget_blocks=10, gen_blocks=2)
