@@ -57,6 +57,10 @@ struct kvm_session {
     std::vector<uint32_t> h_n_tokens;
     std::vector<int32_t> h_slot;       // valid when slots_known
     bool slots_known = true;           // a fresh session has no resident block
+    // No block holds a window slot (fresh session, kvm_reset_window, no slot
+    // set since): the next diff can produce no moves.
+    bool window_empty = true;
+    bool plan_moveless = false;        // the current plan came from an empty window
     bool have_selection = false;
     bool have_plan = false;
 
@@ -262,6 +266,8 @@ StageinArgs stagein_common(kvm_session *s) {
 }
 
 kvm_status launch_moves(kvm_session *s, cudaStream_t st) {
+    // a plan made over an empty window moves nothing: skip the launch
+    if (s->plan_moveless) return KVM_OK;
     PermuteArgs p{};
     p.n_moves_dev = &s->plan.hdr->n_moves;
     p.mv_block = s->plan.mv_block;
@@ -800,6 +806,7 @@ kvm_status kvm_register_append(kvm_session *s, kvm_stream stream, uint32_t n_new
     if (r == KVM_OK && n_add) {
         r = upload_small(s, st, s->bt.tier + first_new, tier.data(), n_add);
         if (r == KVM_OK) r = upload_small(s, st, s->bt.gpu_slot + first_new, slot.data(), 4u * n_add);
+        if (r == KVM_OK && resident) s->window_empty = false;
         if (r == KVM_OK) r = upload_small(s, st, s->bt.baked_pos + first_new, baked.data(), 8u * n_add);
         if (r == KVM_OK) KVM_CUDA(s, cudaMemsetAsync(s->bt.remap_count + first_new, 0, 4u * n_add, st), "clear");
         if (r == KVM_OK) KVM_CUDA(s, cudaMemsetAsync(s->bt.remap_abs_delta + first_new, 0, 8u * n_add, st), "clear");
@@ -838,6 +845,7 @@ kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t bl
     const int32_t v = slot < 0 ? -1 : slot;
     kvm_status r = upload_small(s, as_stream(stream), s->bt.gpu_slot + block_id, &v, sizeof v);
     if (r == KVM_OK && block_id < s->h_slot.size()) s->h_slot[block_id] = v;
+    if (r == KVM_OK && v >= 0) s->window_empty = false;
     return r;
 }
 
@@ -852,6 +860,7 @@ kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream) {
     }
     std::fill(s->h_slot.begin(), s->h_slot.end(), -1);
     s->slots_known = true;
+    s->window_empty = true;
     s->have_plan = false;
     return KVM_OK;
 }
@@ -1367,6 +1376,8 @@ kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh) {
     s->have_selection = false;
     s->have_plan = true;
     s->slots_known = false;
+    s->plan_moveless = s->window_empty;
+    s->window_empty = false;
     return KVM_OK;
 }
 

@@ -52,19 +52,41 @@ class LayerSplit:
     def n_local(self) -> int:
         return self.l1 - self.l0
 
+    def _buffers(self, B, dtype, device):
+        """Persistent send [rows, B] and receive [world * rows, B] buffers of the
+        all-gather (rows = the largest layer share; padding rows stay zero)."""
+        import torch
+        key = (B, dtype, str(device))
+        if getattr(self, "_buf_key", None) != key:
+            rows = max(self.counts)
+            self._send = torch.zeros((rows, B), dtype=dtype, device=device)
+            self._recv = torch.empty((self.world * rows, B), dtype=dtype, device=device)
+            self._buf_key = key
+        return self._send, self._recv
+
+    def send_buffer(self, B, dtype, device):
+        """[n_local, B] view of the all-gather's send buffer: scoring straight
+        into it saves the copy in gather_terms."""
+        return self._buffers(B, dtype, device)[0][:self.n_local]
+
     def gather_terms(self, local_terms):
-        """[n_local, B] f64 (any device) -> [n_layers, B] in global layer order."""
+        """[n_local, B] f64 (any device) -> [n_layers, B] in global layer order.
+        One all_gather_into_tensor into a persistent buffer; when every rank has
+        the same number of layers that buffer already is [n_layers, B] in
+        global order."""
         if self.world == 1:
             return local_terms.contiguous()
         import torch
         import torch.distributed as dist
         B = local_terms.shape[1]
-        rows = max(self.counts)
-        pad = torch.zeros((rows, B), dtype=local_terms.dtype, device=local_terms.device)
-        pad[:self.n_local].copy_(local_terms)
-        parts = [torch.empty_like(pad) for _ in range(self.world)]
-        dist.all_gather(parts, pad, group=self.group)
-        return torch.cat([p[:c] for p, c in zip(parts, self.counts)], dim=0).contiguous()
+        send, recv = self._buffers(B, local_terms.dtype, local_terms.device)
+        if local_terms.data_ptr() != send.data_ptr():
+            send[:self.n_local].copy_(local_terms)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        rows = send.shape[0]
+        if all(c == rows for c in self.counts):
+            return recv
+        return torch.cat([recv[r * rows:r * rows + c] for r, c in enumerate(self.counts)], dim=0)
 
     def reduce_partial(self, partial):
         """In-place sum over ranks of each rank's [B] f64 partial layer sum."""
@@ -82,11 +104,17 @@ def layer_split_scores(sess, split: LayerSplit, terms_local, acc, n_active: int,
     installed in the session, ready for kvm_select."""
     n_blocks = sess.block_count
     ldt = terms_local.shape[1]
-    sess.score_terms(0, split.n_local, terms_local.data_ptr(), ldt, stream=stream)
-    if split.mode == "allgather":
-        full = split.gather_terms(terms_local[:, :n_blocks])
+    if split.mode == "allgather" and split.world > 1:
+        # score straight into the all-gather's send buffer (ldt = n_blocks)
+        send = split.send_buffer(n_blocks, terms_local.dtype, terms_local.device)
+        sess.score_terms(0, split.n_local, send.data_ptr(), n_blocks, stream=stream)
+        full = split.gather_terms(send)
         sess.reduce_terms(full.data_ptr(), split.n_layers, n_blocks, acc.data_ptr(), stream=stream)
+    elif split.mode == "allgather":
+        sess.score_terms(0, split.n_local, terms_local.data_ptr(), ldt, stream=stream)
+        sess.reduce_terms(terms_local.data_ptr(), split.n_layers, ldt, acc.data_ptr(), stream=stream)
     else:
+        sess.score_terms(0, split.n_local, terms_local.data_ptr(), ldt, stream=stream)
         sess.reduce_terms(terms_local.data_ptr(), split.n_local, ldt, acc.data_ptr(), stream=stream)
         split.reduce_partial(acc[:n_blocks])
     sess.set_scores_from_sum(acc.data_ptr(), n_active, stream=stream)
