@@ -343,7 +343,7 @@ def run_kvm(args):
                      "select_diff": round(statistics.mean(st_plan), 4),
                      "stagein": round(stage_ms, 4)},
         "algorithmic_bytes_per_step": {"score": score_b, "stagein": stage_b},
-        "roofline": {"kernel": "stagein_kernel (+ empty layout launch)", "bound": "hbm",
+        "roofline": {"kernel": "stagein_kernel", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": traffic,

@@ -10,7 +10,6 @@
 namespace kvm {
 
 constexpr int kStageinConsumerWarps = 8;
-constexpr int kStageinThreads = (kStageinConsumerWarps + 1) * 32;   // + 1 producer warp
 // Transform mode without RoPE: 7 consumer warps + the producer, so that two
 // CTAs (16 warps, four per scheduler) leave 128 registers a thread for the
 // packed butterflies.

@@ -1015,14 +1015,13 @@ cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t g
 static std::atomic<uint64_t> g_permute_chain_attr{0};
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream) {
-    if (a.vec16) {
-        // pieces of 2-16 KiB (16-byte multiples), small enough for about
-        // three streams an SM; the fallback's columns must fit the ring too
-        if (a.piece < 16u || a.piece % 16u || a.max_moves > 65535u ||
-            static_cast<uint64_t>(kChainStages) * a.piece < 16ull * a.max_moves)
-            return cudaErrorInvalidValue;
-        const size_t smem = permute_chain_buf_offset(a.max_moves) + static_cast<size_t>(kChainStages) * a.piece;
-        if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    // the streaming kernel when the window is 16-byte aligned and its move
+    // table, order and ring (whose columns must also hold 16 bytes of every
+    // move for the fallback) fit; the SIMT column kernel otherwise
+    const size_t chain_smem = permute_chain_buf_offset(a.max_moves) + static_cast<size_t>(kChainStages) * a.piece;
+    if (a.vec16 && a.piece >= 16u && a.piece % 16u == 0 && a.max_moves <= 65535u &&
+        static_cast<uint64_t>(kChainStages) * a.piece >= 16ull * a.max_moves && chain_smem <= 200u * 1024u) {
+        const size_t smem = chain_smem;
         const void *fn = reinterpret_cast<const void *>(permute_chain_kernel);
         if (!attr_once(g_permute_chain_attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
         int per_sm = 1;

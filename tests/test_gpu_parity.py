@@ -289,6 +289,30 @@ def test_step_window_bytes(kvm_lib, oracle, tk, tv):
             assert moves.shape[0] > 0 or cold.shape[0] < sel.size
 
 
+def test_step_unaligned_rows(kvm_lib, oracle):
+    """n_embd 96: q8_0 rows of 102 bytes are not 16-byte multiples, so the
+    moves take the SIMT column kernel and the stage-in its word-store path."""
+    shape = Shape(n_layer=2, n_blocks=64, block_tokens=32, n_head_kv=1, head_dim=96, n_head_q=3,
+                  budget_blocks=12, gen_blocks=4, partial_tokens=11)
+    rig = make_rig(shape, seed=23)
+    om = OracleModel(rig)
+    rng = np.random.default_rng(24)
+    q, qc = make_query(shape, rng)
+    n_moves = 0
+    for step in range(4):
+        if step:
+            q2, _ = make_query(shape, rng)
+            q = (0.8 * q + 0.6 * q2).astype(np.float32)
+        rig.sess.set_query(q, qc)
+        rig.sess.step(rig.src, rig.k_bases(), rig.v_bases(), mandatory=[shape.n_blocks - 1])
+        _, sel, plan, moves, cold = om.step(q, qc, [shape.n_blocks - 1])
+        got = rig.sess.plan()
+        assert np.array_equal(got["selected"], sel)
+        n_moves += moves.shape[0]
+        _check_window(rig, om)
+    assert n_moves > 0
+
+
 def test_step_after_scrambled_slots(kvm_lib, oracle):
     """A layout that is not chronological (kvm_set_block_gpu_slot reversing the
     resident blocks' slots, the window bytes permuted to match): the next
