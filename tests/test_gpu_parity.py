@@ -121,10 +121,12 @@ def test_quantize_rows_edge_values(kvm_lib, oracle, type_id):
 
 # --------------------------------------------------------------- scorer ---
 
-def test_score_bitexact_uploaded_summaries(kvm_lib, oracle):
+@pytest.mark.parametrize("Hkv,D,Hq", [(4, 64, 12), (2, 80, 6), (1, 1024, 2)])
+def test_score_bitexact_uploaded_summaries(kvm_lib, oracle, Hkv, D, Hq):
+    """Head sizes below, off and at the top of the channel batch (64, 80, 1024)."""
     torch = _cuda()
-    rng = np.random.default_rng(21)
-    L, B, Hkv, D, Hq = 3, 300, 4, 64, 12
+    rng = np.random.default_rng(21 + D)
+    L, B = 3, 300
     E = Hkv * D
     cfg = kvm_lib.default_config(n_layer=L, n_head_kv=Hkv, head_dim=D, n_head_q=Hq,
                                  max_blocks=512, block_tokens=128, select_budget=128 * 32,
