@@ -17,11 +17,15 @@
 // to the consumers separately (ofree barrier) once the store has read it, so
 // the loads run NSTAGE-1 tiles ahead of the quantizers.  Every wait is bounded.
 //
-// permute_kernel: moves retained blocks from their old slot to their new slot
-// in place.  Each CTA owns a byte column of the slot span for one (layer, K|V)
-// and stages that column of every moving block in shared memory before
-// writing any of them, so chains and cycles of moves need no scratch buffer
-// and each byte crosses HBM once in each direction.
+// permute_chain_kernel / permute_kernel: move retained blocks from their old
+// slot to their new slot in place, each byte crossing HBM once each way.  The
+// chronological layout keeps retained blocks in order, so the streaming kernel
+// copies the moves of each (layer, K|V, piece of the span) in an order where
+// every slot is read before it is overwritten, through a ring of TMA buffers.
+// Move lists that are not monotone, and windows that are not 16-byte aligned,
+// use column staging instead: a CTA owns a byte column of the slot span for
+// one (layer, K|V) and stages that column of every moving block in shared
+// memory before writing any of them, so any permutation needs no scratch.
 #include "kvm_internal.cuh"
 #include "kvm_quant.cuh"
 #include "kvm_kernels.h"
