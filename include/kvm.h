@@ -446,6 +446,15 @@ kvm_status kvm_step(kvm_session *s, kvm_stream stream, const uint32_t *mandatory
 /* Bounded host wait for all work queued on `stream`; checks the device error
  * flags.  KVM_ETIMEOUT if not done within timeout_ms. */
 kvm_status kvm_wait(kvm_session *s, kvm_stream stream, uint32_t timeout_ms);
+
+/* Test hook for the failure path (no reference counterpart).  With
+ * KVM_TEST_SKIP_TILE_LOAD the next stage-in launch of this session leaves the
+ * first tile of its first CTA unloaded: that CTA's bounded waits run out
+ * (about 2 s each), it drains its other copies and returns, and the next
+ * kvm_wait reports KVM_EDEVICE ("wait-timeout") and clears the flags.  The
+ * hook applies to one launch; nothing faults and the session stays usable. */
+#define KVM_TEST_SKIP_TILE_LOAD 1u
+kvm_status kvm_test_inject(kvm_session *s, uint32_t flags);
 /* Copy the last plan to host arrays (waits on `stream`, bounded by
  * timeout_ms) and refresh the host view of window slots. */
 kvm_status kvm_get_plan(kvm_session *s, kvm_stream stream, kvm_plan *plan, uint32_t timeout_ms);

@@ -70,6 +70,7 @@ struct StageinArgs {
     float xf_post_k, xf_post_v;    // power-of-two Hadamard scale folded into the quantizer (1: none)
     uint32_t xf_heads;             // KV heads per row, n_embd / head_dim
     uint32_t xf_heads_magic;       // ceil(2^32 / xf_heads); 0 when xf_heads == 1
+    uint32_t test_skip;            // kvm_test_inject: CTA 0 leaves its first tile unloaded
 };
 
 uint32_t stagein_rows_per_tile(uint32_t n_embd, uint32_t block_tokens);

@@ -61,6 +61,7 @@ struct kvm_session {
     // set since): the next diff can produce no moves.
     bool window_empty = true;
     bool plan_moveless = false;        // the current plan came from an empty window
+    uint32_t test_inject = 0;          // kvm_test_inject flags for the next stage-in launch
     bool have_selection = false;
     bool have_plan = false;
 
@@ -1405,6 +1406,8 @@ kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
     a.layer_stride = src->layer_stride;
     a.item_stride = src->block_stride;
     a.row_stride = src->row_stride;
+    a.test_skip = (s->test_inject & KVM_TEST_SKIP_TILE_LOAD) ? 1u : 0u;
+    s->test_inject = 0;
     KVM_CUDA(s, launch_stagein(a, st, 0), "stage-in launch");
     s->launches++;
     return KVM_OK;
@@ -1551,6 +1554,13 @@ kvm_status kvm_step(kvm_session *s, kvm_stream stream, const uint32_t *mandatory
     if (r == KVM_OK) KVM_CUDA(s, cudaEventRecord(s->ev[4], st), "event");
     s->timed = false;
     return r;
+}
+
+kvm_status kvm_test_inject(kvm_session *s, uint32_t flags) {
+    if (!s) return KVM_EINVAL;
+    if (flags & ~KVM_TEST_SKIP_TILE_LOAD) return fail(s, KVM_EINVAL, "unknown test flags 0x%x", flags);
+    s->test_inject = flags;
+    return KVM_OK;
 }
 
 kvm_status kvm_wait(kvm_session *s, kvm_stream stream, uint32_t timeout_ms) {

@@ -29,6 +29,8 @@ KVM_OK, KVM_EINVAL, KVM_ENOMEM, KVM_ECUDA, KVM_ETIMEOUT, KVM_ESTATE, KVM_EDEVICE
 _STATUS = {1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESTATE", 6: "EDEVICE"}
 
 # every symbol include/kvm.h declares
+TEST_SKIP_TILE_LOAD = 1           # kvm_test_inject flag
+
 ABI_SYMBOLS = (
     "kvm_config_default", "kvm_session_create", "kvm_session_destroy", "kvm_last_error",
     "kvm_window_slots", "kvm_block_count", "kvm_row_bytes", "kvm_register_append",
@@ -40,7 +42,7 @@ ABI_SYMBOLS = (
     "kvm_quantize_rows_noalloc", "kvm_write_mean_k", "kvm_meank_add", "kvm_meank_flush",
     "kvm_meank_zero", "kvm_query_reset", "kvm_query_add", "kvm_set_transform",
     "kvm_attn_rot_nrot", "kvm_stageout", "kvm_stageout_item_bytes", "kvm_select_groups",
-    "kvm_stagein_packed",
+    "kvm_stagein_packed", "kvm_test_inject",
 )
 
 
@@ -184,6 +186,7 @@ def lib():
             "kvm_stagein": (C.c_int, [vp, vp, C.POINTER(Source), C.POINTER(Window)]),
             "kvm_step": (C.c_int, [vp, vp, vp, u32, C.POINTER(Source), C.POINTER(Window)]),
             "kvm_wait": (C.c_int, [vp, vp, u32]),
+            "kvm_test_inject": (C.c_int, [vp, u32]),
             "kvm_get_plan": (C.c_int, [vp, vp, C.POINTER(_Plan), u32]),
             "kvm_get_scores": (C.c_int, [vp, vp, vp, u32, u32]),
             "kvm_get_timings": (C.c_int, [vp, C.POINTER(Timings)]),
@@ -483,6 +486,11 @@ class Session:
     # ---- results
     def wait(self, timeout_ms=60000, stream=None):
         self._check(lib().kvm_wait(self.h, _stream(stream), timeout_ms), "wait")
+
+    def test_inject(self, flags):
+        """Failure-path test hook (kvm_test_inject): TEST_SKIP_TILE_LOAD makes the
+        next stage-in's first CTA time out on a tile that is never loaded."""
+        self._check(lib().kvm_test_inject(self.h, flags), "test_inject")
 
     def scores(self, timeout_ms=60000, stream=None) -> np.ndarray:
         n = self.block_count
