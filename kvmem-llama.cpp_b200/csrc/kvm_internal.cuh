@@ -7,6 +7,8 @@
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <stdint.h>
 
 #include "../../include/kvm.h"
@@ -270,6 +272,34 @@ __device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t *scratch) {
     uint32_t total;
     (void)block_exclusive_scan<NT>(v, scratch, &total);
     return total;
+}
+
+// ---------------------------------------------------------- host helpers --
+
+// SM count of the current device (cached per host thread and device).
+inline int num_sms() {
+    static thread_local int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] <= 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+// Dynamic shared-memory opt-in is a per-device function attribute: set it
+// once per device the process launches on.
+inline bool attr_once(std::atomic<uint64_t> &done, const void *fn, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+        return false;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return true;
 }
 
 }  // namespace kvm
