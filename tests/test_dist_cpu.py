@@ -1,4 +1,4 @@
-"""Multi-rank host logic on CPU (gloo, world size 2): the layer split of one
+"""Multi-rank host logic on CPU (gloo, world sizes 2 and 4): the layer split of one
 session over ranks, with the per-layer score terms from the CPU oracle.
 
 allgather mode must reproduce the single-process scores bit for bit and the
@@ -79,21 +79,23 @@ def _run(mode, world=2):
     return dict(results)
 
 
-@pytest.mark.parametrize("mode", ["allgather", "allreduce"])
-def test_layer_split_matches_single_process(oracle, mode):
+@pytest.mark.parametrize("mode,world", [("allgather", 2), ("allreduce", 2), ("allgather", 4)])
+def test_layer_split_matches_single_process(oracle, mode, world):
+    """World 4 splits the 6 layers 2, 2, 1, 1: the all-gather pads the short
+    ranks' shares and drops the padding rows again."""
     sums, cnt, has, q, qc = _inputs()
     want = oracle.score(sums, cnt, has, q, qc, HKV, HQ, D)
     want_sel = oracle.pick_topk(oracle.make_cfg(128, 20, 1, 0), want)
-    res = _run(mode)
-    assert len(res) == 2
-    for rank in range(2):
+    res = _run(mode, world)
+    assert len(res) == world
+    for rank in range(world):
         got = np.frombuffer(res[rank][0], dtype=np.float64)
         if mode == "allgather":
             assert got.tobytes() == want.tobytes()
         else:
             assert np.allclose(got, want, rtol=1e-12, atol=0)
         assert res[rank][1] == want_sel.tolist()
-    assert res[0][0] == res[1][0]    # identical scores on every rank
+    assert all(res[r][0] == res[0][0] for r in range(world))    # identical scores on every rank
 
 
 def test_layer_ranges_cover_all_layers():
