@@ -17,6 +17,14 @@
  * serves one sequence on one device; sessions are independent and may be
  * used from different threads; one session is single-threaded.
  *
+ * Deferred launches: kvm_select and kvm_reset_window record their work and
+ * the next kvm_diff performs both inside its own launch (one kernel for
+ * select + diff).  Any other call that depends on that work -- one that
+ * rewrites the scores or the plan, reads or writes the block table, appends
+ * blocks, waits or reads results -- launches it first, on the stream it was
+ * recorded on, so every sequence of calls has the effect of running them in
+ * order.
+ *
  * Reference interfaces this ABI replaces (paths in CrKcel/kvmem-llama.cpp):
  *   - llama_memory_kvmem::score_retrieval        src/adapter/llama-memory-kvmem.cpp:2869-2916
  *   - KvMemStore::pick_topk_blocks(mandatory)    kvmem/src/host/kvmem_store.cpp:357-359, :482-623
@@ -230,7 +238,9 @@ kvm_status kvm_set_block_tier(kvm_session *s, kvm_stream stream, uint32_t block_
 kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t block_id,
                                   int32_t slot);
 /* KvMemStore::clear_working_set + drop every window slot: the next step
- * treats the window as empty (cold).  Stream-ordered on `stream`. */
+ * treats the window as empty (cold).  Stream-ordered on `stream`; the reset
+ * is applied by the next kvm_diff inside its own launch (deferred launches,
+ * above). */
 kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream);
 
 /* ------------------------------------------------- summaries and query -- */
@@ -383,7 +393,9 @@ kvm_status kvm_set_scores_from_sum(kvm_session *s, kvm_stream stream, const doub
 kvm_status kvm_set_scores(kvm_session *s, kvm_stream stream, const double *scores,
                           uint32_t n);
 /* pick_topk_blocks(mandatory): mandatory is a host array in reference order
- * (walked from its end, newest first). */
+ * (walked from its end, newest first), copied before the call returns.  The
+ * selection kernel runs fused with the next kvm_diff (deferred launches,
+ * above). */
 kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandatory,
                       uint32_t n_mandatory);
 /* KvMemStore::pick_semantic_groups (kvmem/src/host/kvmem_store.cpp:625-756)

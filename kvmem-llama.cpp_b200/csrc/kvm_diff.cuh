@@ -1,0 +1,213 @@
+// kvm_diff.cuh -- the body of the selection diff, shared by diff_kernel
+// (kvm_diff.cu) and the fused select + diff kernel (kvm_select.cu).
+//
+// KvMemStore::set_selection (kvmem/src/host/kvmem_store.cpp:758-882) on the
+// device, for an already canonical (ascending, unique, in-range) selection:
+//   stage_out = GPU-tier blocks not selected (or every GPU block when
+//               optimize_stage_in is off), ascending; they leave the working set
+//   stage_in  = selected blocks not in the working set, ascending
+//   remaps    = one per selected block in window order: from_base = current
+//               bake position, to_base = running window position, skip /
+//               raw_refresh per the immutable-source rules; counters
+//               selection_overlap / gpu_reused / retained_position_{stable,moved}
+// plus the adapter's chronological layout (layout_gpu_slots_by_orig_pos,
+// src/adapter/llama-memory-kvmem.cpp:931-1254, with reset_slots/alloc_slot):
+// the i-th selected block ends in window slot i; a selected block already
+// resident in another slot is moved (move list), a selected block not
+// resident is gathered + quantized from the stored history (cold list);
+// unselected GPU blocks lose their slot and drop to the CPU tier
+// (KvMemRuntime::stage_out with no lower tier, kvmem_runtime.cpp:238-292).
+//
+// One CTA of kDiffThreads threads; per-block work is split into contiguous
+// id chunks per thread so every output list comes out in ascending order
+// from one block-wide exclusive scan.
+#pragma once
+
+#include "kvm_internal.cuh"
+#include "kvm_kernels.h"
+
+namespace kvm {
+
+// KvMemStore::set_selection + the chronological layout for the `k` selected
+// blocks in a.plan.selected.  Called by every thread of a kDiffThreads CTA.
+// now / was: n bytes of shared memory each; with now_ready the caller has
+// already set now[i] != 0 exactly for the selected blocks.  With
+// a.reset_window the block table is first reset as kvm_reset_window does
+// (nothing in the working set, GPU-tier blocks drop to the CPU tier, no
+// slots), in the same pass that reads it.
+static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, uint8_t *was,
+                                 bool now_ready) {
+    __shared__ uint4 scratch4[kDiffThreads / 32 + 1];
+    const uint32_t n = a.n_blocks;
+    PlanHeader *hdr = a.plan.hdr;
+    const uint32_t tid = threadIdx.x;
+    const bool reset = a.reset_window != 0;
+    const uint32_t *sel = a.plan.selected;
+    const bool ffr = a.optimize_stage_in == 0;
+    const bool imm = a.immutable_source_k != 0;
+    BlockTable bt = a.bt;
+
+    if (!now_ready) {
+        for (uint32_t i = tid; i < n; i += kDiffThreads) now[i] = 0;
+        __syncthreads();
+        for (uint32_t s = tid; s < k; s += kDiffThreads) {
+            const uint32_t id = sel[s];
+            if (id < n) now[id] = 1;
+            else set_status(a.status, kErrIndex);
+        }
+        __syncthreads();
+    }
+
+    // ---- pass over every block: overlap, stage_out
+    const uint32_t per = (n + kDiffThreads - 1u) / kDiffThreads;
+    const uint32_t lo = min(n, tid * per);
+    const uint32_t hi = min(n, lo + per);
+    uint32_t overlap = 0, n_out = 0;
+    for (uint32_t i = lo; i < hi; ++i) {
+        uint8_t w = bt.in_ws[i];
+        uint8_t t = bt.tier[i];
+        if (reset) {
+            if (w) bt.in_ws[i] = 0;
+            w = 0;
+            if (t == KVM_TIER_GPU) {
+                t = KVM_TIER_CPU;
+                bt.tier[i] = t;
+            }
+            bt.gpu_slot[i] = -1;
+        }
+        was[i] = w;
+        overlap += (w && now[i]) ? 1u : 0u;
+        n_out += (t == KVM_TIER_GPU && (!now[i] || ffr)) ? 1u : 0u;
+    }
+    uint4 tot1;
+    const uint4 off1 = block_exclusive_scan4<kDiffThreads>(make_uint4(n_out, overlap, 0u, 0u), scratch4, &tot1);
+    uint32_t off_out = off1.x;
+    const uint32_t tot_out = tot1.x;
+    const uint32_t tot_overlap = tot1.y;
+    for (uint32_t i = lo; i < hi; ++i) {
+        if (bt.tier[i] == KVM_TIER_GPU && (!now[i] || ffr)) {
+            a.plan.stage_out[off_out++] = i;
+            bt.in_ws[i] = 0;
+        }
+    }
+    __syncthreads();
+
+    // ---- pass over the selection: window positions, stage_in, remaps, layout
+    const uint32_t sper = (k + kDiffThreads - 1u) / kDiffThreads;
+    const uint32_t slo = min(k, tid * sper);
+    const uint32_t shi = min(k, slo + sper);
+    uint32_t tok = 0, n_in = 0, n_mv = 0, n_cold = 0;
+    for (uint32_t s = slo; s < shi; ++s) {
+        const uint32_t id = sel[s];
+        tok += bt.n_tokens[id];
+        n_in += bt.in_ws[id] ? 0u : 1u;
+        const bool resident = !ffr && bt.tier[id] == KVM_TIER_GPU && bt.gpu_slot[id] >= 0;
+        if (resident) n_mv += bt.gpu_slot[id] != static_cast<int32_t>(s) ? 1u : 0u;
+        else ++n_cold;
+    }
+    uint4 tot2;
+    const uint4 off2 = block_exclusive_scan4<kDiffThreads>(make_uint4(tok, n_in, n_mv, n_cold), scratch4, &tot2);
+    uint32_t wpos = off2.x, off_in = off2.y, off_mv = off2.z, off_cold = off2.w;
+    const uint32_t tot_tok = tot2.x, tot_in = tot2.y, tot_mv = tot2.z, tot_cold = tot2.w;
+    uint32_t stable = 0, moved = 0, reused = 0, err = 0;
+    for (uint32_t s = slo; s < shi; ++s) {
+        const uint32_t id = sel[s];
+        const uint8_t tier = bt.tier[id];
+        const int32_t slot_before = bt.gpu_slot[id];
+        const int64_t baked = bt.baked_pos[id];
+        const uint32_t ntok = bt.n_tokens[id];
+        const bool reusable = was[id] && tier == KVM_TIER_GPU;
+        if (reusable) {
+            if (baked == static_cast<int64_t>(wpos)) ++stable;
+            else ++moved;
+            if (!ffr) ++reused;
+        }
+        const bool cold = tier != KVM_TIER_GPU || ffr;
+        if (!bt.in_ws[id]) a.plan.stage_in[off_in++] = id;
+        const bool wkr = !cold;
+        const bool same = baked == static_cast<int64_t>(wpos);
+        const bool skip = same && (!imm || wkr) && !a.force_raw_refresh;
+        const uint64_t delta = static_cast<uint64_t>(baked > static_cast<int64_t>(wpos)
+                                                         ? baked - static_cast<int64_t>(wpos)
+                                                         : static_cast<int64_t>(wpos) - baked);
+        bool raw = false;
+        if (imm && (cold || !same)) {
+            const uint64_t lim = a.immutable_refresh_abs_delta_tokens;
+            const uint64_t have = bt.remap_abs_delta[id];
+            const bool remap_limit = a.immutable_refresh_remaps > 0 &&
+                                     bt.remap_count[id] >= a.immutable_refresh_remaps;
+            const bool delta_limit = lim > 0 && (have >= lim || delta >= lim - (have < lim ? have : lim));
+            const uint64_t maxp = a.immutable_max_baked_position;
+            const bool out_of_range = maxp > 0 && (baked < 0 || static_cast<uint64_t>(baked) + ntok > maxp);
+            raw = cold || remap_limit || delta_limit || out_of_range;
+        }
+        if (imm && a.force_raw_refresh) raw = true;
+        if (skip && raw) ++err;   // std::logic_error in the reference (unreachable)
+        a.plan.rm_block_id[s] = id;
+        a.plan.rm_n_tokens[s] = ntok;
+        a.plan.rm_from_base[s] = static_cast<int32_t>(baked);
+        a.plan.rm_to_base[s] = static_cast<int32_t>(wpos);
+        a.plan.rm_wkr[s] = wkr ? 1 : 0;
+        a.plan.rm_skip[s] = skip ? 1 : 0;
+        a.plan.rm_raw[s] = raw ? 1 : 0;
+        // layout
+        const bool resident = !ffr && tier == KVM_TIER_GPU && slot_before >= 0;
+        if (resident) {
+            if (slot_before != static_cast<int32_t>(s)) {
+                a.plan.mv_block[off_mv] = id;
+                a.plan.mv_from[off_mv] = slot_before;
+                a.plan.mv_to[off_mv] = static_cast<int32_t>(s);
+                ++off_mv;
+            }
+        } else {
+            a.plan.cold_block[off_cold] = id;
+            a.plan.cold_to[off_cold] = static_cast<int32_t>(s);
+            ++off_cold;
+        }
+        if (s >= a.n_slots) err += 1u << 16;
+        // working-set and bake updates
+        bt.in_ws[id] = 1;
+        if (!skip) {
+            if (raw) {
+                bt.remap_count[id] = 0;
+                bt.remap_abs_delta[id] = 0;
+            } else {
+                bt.remap_count[id] += 1u;
+                bt.remap_abs_delta[id] += delta;
+            }
+        }
+        bt.baked_pos[id] = static_cast<int64_t>(wpos);
+        wpos += ntok;
+    }
+    uint4 tot3;
+    (void)block_exclusive_scan4<kDiffThreads>(make_uint4(stable, moved, reused, err), scratch4, &tot3);
+    const uint32_t tot_stable = tot3.x, tot_moved = tot3.y, tot_reused = tot3.z, tot_err = tot3.w;
+    // every selected block's old slot was read above; now install the layout
+    for (uint32_t i = lo; i < hi; ++i) {
+        if (now[i]) continue;
+        if (bt.tier[i] == KVM_TIER_GPU) bt.tier[i] = KVM_TIER_CPU;
+        bt.gpu_slot[i] = -1;
+    }
+    for (uint32_t s = slo; s < shi; ++s) {
+        const uint32_t id = sel[s];
+        bt.tier[id] = KVM_TIER_GPU;
+        bt.gpu_slot[id] = static_cast<int32_t>(s);
+    }
+    if (tid == 0) {
+        hdr->n_stage_in = tot_in;
+        hdr->n_stage_out = tot_out;
+        hdr->n_remaps = k;
+        hdr->total_window_tokens = tot_tok;
+        hdr->selection_overlap_blocks = tot_overlap;
+        hdr->gpu_reused_blocks = tot_reused;
+        hdr->retained_position_stable = tot_stable;
+        hdr->retained_position_moved = tot_moved;
+        hdr->n_moves = tot_mv;
+        hdr->n_cold = tot_cold;
+        hdr->n_blocks = n;
+        if (tot_err & 0xffffu) set_status(a.status, kErrConfig);
+        if (tot_err >> 16) set_status(a.status, kErrSlot);
+    }
+}
+
+}  // namespace kvm

@@ -17,10 +17,10 @@ constexpr int kXfConsumerWarps = 7;
 constexpr int kStageinStages = 3;
 constexpr int kXfStages = 5;       // transform mode: ALU-heavier tiles, loads further ahead
 constexpr int kPermuteThreads = 512;
-constexpr int kScoreBlocks = 64;                   // blocks per scorer CTA (one thread each)
-constexpr int kScoreBatch = 64;                    // channel loads in flight per scorer thread
-constexpr uint32_t kSumGroup = 64;                 // blocks per summary tile (== kScoreBlocks)
-constexpr int kScoreThreads = kScoreBlocks;        // one thread per block
+constexpr uint32_t kSumGroup = 32;                 // blocks per summary tile
+constexpr uint32_t kScoreRange = 32;               // blocks per scorer CTA (a warp's lanes)
+static_assert(kScoreRange == kSumGroup, "a scorer CTA reads one summary tile per layer");
+constexpr int kScoreStages = 12;                   // scorer: 16-byte vectors in flight per lane
 constexpr int kSelectThreads = 1024;
 constexpr int kDiffThreads = 1024;
 
@@ -175,22 +175,25 @@ __host__ __device__ inline size_t permute_chain_buf_offset(uint32_t max_moves) {
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t stream);
 
 // ---------------------------------------------------------- summaries --
-// Summary tensor, tiled: [layer][block group of 64][channel][64 blocks], so
-// the channel rows of one (layer, group) are contiguous 256-byte rows and one
-// (layer, kv head, group) scorer unit is D*256 contiguous bytes.
+// Summary tensor, tiled: [layer][block group of 32][n_embd/4][32 blocks][4
+// channels].  Four consecutive channels of one block are one 16-byte vector,
+// and the vectors of the 32 blocks of a group sit side by side: a warp of
+// threads, one per block, reads its blocks' next four channels as 512
+// contiguous bytes, and one KV head of a group is head_dim * 128 contiguous
+// bytes.  n_embd is a multiple of 32 (ggml blocks).
 struct SummaryLayout {
-    float *sum_t;          // [n_layer][ldb/64][n_embd][64]
+    float *sum_t;          // [n_layer][ldb/32][n_embd/4][32][4]
     uint32_t *mean_tok;    // [n_layer][ldb]
     float *inv_tok;        // [n_layer][ldb]  1.0f / mean_tok (0 when none)
-    uint32_t ldb;          // block capacity, a multiple of 64
+    uint32_t ldb;          // block capacity, a multiple of 32
     uint32_t n_layer;
     uint32_t n_embd;
 };
 
 __host__ __device__ inline size_t sum_index(const SummaryLayout &s, uint32_t l, uint32_t e,
                                             uint32_t b) {
-    return ((static_cast<size_t>(l) * (s.ldb / kSumGroup) + b / kSumGroup) * s.n_embd + e) * kSumGroup +
-           (b % kSumGroup);
+    return (((static_cast<size_t>(l) * (s.ldb / kSumGroup) + b / kSumGroup) * (s.n_embd / 4u) + e / 4u) *
+                kSumGroup + (b % kSumGroup)) * 4u + (e % 4u);
 }
 
 cudaError_t launch_upload_summaries(const SummaryLayout &s, uint32_t layer, uint32_t block0,
@@ -251,34 +254,37 @@ cudaError_t launch_meank_flush(const SummaryLayout &s, float *meank, uint32_t la
 struct QueryState {
     float *q_sum;          // [n_layer][n_head_q*head_dim]  (device copy)
     uint32_t *q_count;     // [n_layer]
-    float *qv;             // [n_layer][n_head_kv][head_dim]
-    float *nq;             // [n_layer][n_head_kv]
+    float *qv;             // [n_layer][n_head_kv][head_dim] prepared query
+    float *nq;             // [n_layer][n_head_kv] its squared norm
 };
-
-cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_head_kv,
-                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream);
 
 // -------------------------------------------------------------- scorer --
 struct ScoreArgs {
     SummaryLayout sum;
-    const float *qv;
+    const float *qv;       // QueryState::qv / nq, made by the query prep
     const float *nq;
     const uint32_t *q_count;
     uint32_t n_head_kv;
+    uint32_t n_head_q;
     uint32_t head_dim;
     uint32_t n_blocks;
     uint32_t layer0;       // first layer scored by this launch
     uint32_t n_layers;     // layers scored by this launch
-    double *terms;         // [layer][ldt]
+    double *terms;         // [layer][ldt], indexed by the session's layer
     uint32_t ldt;
-    float *rbuf;           // [layer][n_head_kv][ldb] per-head results
     uint32_t *status;
-    // combine_kernel: scores too (only when n_layers == all layers of the session)
+    // combine: the last CTA of each block range also forms the final scores
+    // (only when n_layers == all layers of the session)
     int combine;
+    uint32_t *range_done;  // [ldb / kScoreRange] arrival counters, zero between launches
     double *scores;        // [ldb]
 };
 
-cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream);
+// The query prep (when `prep`, qv / nq from q_sum for every layer), then the
+// scorer.  After a prep the scorer is a programmatic dependent launch: its
+// CTAs start their summary loads while the prep runs and wait for it
+// (griddepcontrol) before they read the query.
+cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream);
 cudaError_t launch_reduce_terms(const double *terms, uint32_t n_layers, uint32_t ldt,
                                 uint32_t n_blocks, double *acc, cudaStream_t stream);
 cudaError_t launch_scores_from_sum(const SummaryLayout &s, uint32_t n_blocks, const double *acc,
@@ -335,10 +341,14 @@ struct DiffArgs {
     uint64_t immutable_refresh_abs_delta_tokens;
     uint64_t immutable_max_baked_position;
     int force_raw_refresh;
+    uint32_t reset_window;         // apply a pending kvm_reset_window first
     PlanArrays plan;
     uint32_t *status;
 };
 
 cudaError_t launch_diff(const DiffArgs &a, cudaStream_t stream);
+// kvm_select + kvm_diff as one launch
+cudaError_t launch_select_diff(const SelectArgs &sa, const DiffArgs &da, cudaStream_t stream);
+cudaError_t launch_reset_window(const BlockTable &bt, uint32_t n, cudaStream_t stream);
 
 }  // namespace kvm

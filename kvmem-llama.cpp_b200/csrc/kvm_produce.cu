@@ -13,8 +13,8 @@
 //   Each warp owns one block and each lane V consecutive channels (V = 8 for
 //   16-bit sources, 4 for F32: 16-byte loads, 4 rows in flight), so the rows
 //   stream in coalesced 512-byte warp accesses; the 8 blocks of a CTA are
-//   transposed through shared memory so every channel's 8 block sums leave
-//   as one 32-byte sector of the [layer][64-block group][channel][64] tile.
+//   transposed through shared memory so every 4 channels' 8 block sums leave
+//   as one 128-byte run of the [layer][64-block group][channel/4][64][4] tile.
 //   Token-mode calls over few blocks (one ubatch of one layer) instead use
 //   mean_k_staged_kernel, which has every row of the block in flight at once.
 //
@@ -164,9 +164,12 @@ __global__ void __launch_bounds__(kMeanWarps * 32) mean_k_kernel(MeanKArgs a) {
         a.sum.inv_tok[at] = mt ? __fdiv_rn(1.0f, __uint2float_rn(mt)) : 0.0f;
     }
     __syncthreads();
+    // 4 channels x 8 blocks of the tiled layout are 32 consecutive floats:
+    // thread i writes channel 4*(i/32) + i%4 of block (i%32)/4
+    static_assert(kMeanWarps * 4 == 32, "one 128-byte run per channel quad");
     for (uint32_t i = threadIdx.x; i < kMeanWarps * 32u * V; i += kMeanWarps * 32u) {
-        const uint32_t el = i / kMeanWarps;
-        const uint32_t bw = i % kMeanWarps;
+        const uint32_t el = (i / 32u) * 4u + (i % 4u);
+        const uint32_t bw = (i % 32u) / 4u;
         const uint32_t bb = grp0 + bw;
         const uint32_t e = ec + el;
         if (bb >= a.block0 && bb < a.block0 + a.n_blk && e < E)

@@ -1,4 +1,4 @@
-// kvm_score.cu -- mean-K summaries, query preparation and the block scorer.
+// kvm_score.cu -- mean-K summary upload/download and the block scorer.
 //
 // Scorer: llama_memory_kvmem::score_retrieval (src/adapter/llama-memory-kvmem.cpp:2869-2916),
 // restated for the device without changing its arithmetic:
@@ -6,17 +6,13 @@
 //     r = dot / (sqrt(nq) * sqrt(nk) + 1e-6f)
 //   per (block, layer): layer = sum of r over heads in order (double), term = layer / H_kv
 //   per block: score = (sum of terms over layers with a query, in layer order) / n_active
-// The summaries are stored channel-major in 64-block tiles
-// ([layer][64-block group][channel][64]) so that a warp of threads, one per
-// block, reads 128 contiguous bytes per channel while each thread keeps the
-// reference's sequential channel order -- coalesced streaming without
-// changing the float rounding of a single block's score.  A tree
-// (warp-shuffle) reduction over channels would round differently, and a
-// near-tie at the top-k boundary could then flip the selection.
-//
-// The head/layer combine is a second, per-block kernel.  Doing it in the last
-// CTA of each block group (threadfence + atomic counter) put a serial tail of
-// L2 round trips after the last unit: 17 us of a 53 us scorer.
+// The summaries are tiled ([layer][64-block group][channel/4][64][4]) so that
+// a warp of threads, one per block, reads 512 contiguous bytes per four
+// channels while each thread keeps the reference's sequential channel order
+// -- coalesced 16-byte streaming without changing the float rounding of a
+// single block's score.  A tree (warp-shuffle) reduction over channels would
+// round differently, and a near-tie at the top-k boundary could then flip the
+// selection.
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
@@ -79,118 +75,6 @@ __global__ void download_summaries_kernel(SummaryLayout s, uint32_t layer, uint3
     }
 }
 
-// ----------------------------------------------------------------- query --
-
-// qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq and
-// nq[l][h] = sum over d of qv*qv, both exactly as the reference loop computes
-// them; invq = 1.0f / (q_count * g).
-__global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_head_q,
-                                  uint32_t head_dim) {
-    extern __shared__ float qv_s[];
-    const uint32_t l = blockIdx.x;
-    const uint32_t cnt = q.q_count[l];
-    if (cnt == 0) return;
-    const uint32_t g = n_head_kv == 0 ? 1u : n_head_q / n_head_kv;
-    const uint32_t gg = g > 1u ? g : 1u;
-    const float invq = __fdiv_rn(1.0f, __uint2float_rn(cnt * gg));
-    const uint32_t E = n_head_kv * head_dim;
-    const float *qs = q.q_sum + static_cast<size_t>(l) * n_head_q * head_dim;
-    float *qv = q.qv + static_cast<size_t>(l) * E;
-    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) {
-        const uint32_t h = i / head_dim;
-        const uint32_t d = i % head_dim;
-        // the group members' values are loaded together, then added in order
-        const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
-        float qh = 0.0f;
-        for (uint32_t g0 = 0; g0 < n_in; g0 += 8u) {
-            float x[8];
-#pragma unroll
-            for (uint32_t k = 0; k < 8u; ++k)
-                x[k] = g0 + k < n_in ? qs[static_cast<size_t>(h * g + g0 + k) * head_dim + d] : 0.0f;
-#pragma unroll
-            for (uint32_t k = 0; k < 8u; ++k)
-                if (g0 + k < n_in) qh = __fadd_rn(qh, x[k]);
-        }
-        const float v = __fmul_rn(qh, invq);
-        qv[i] = v;
-        qv_s[i] = v;
-    }
-    __syncthreads();
-    // nq per head: the reference's sequential sum over d, one thread per head,
-    // reading the prepared vector from shared memory
-    for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
-        float nq = 0.0f;
-        const float *v = qv_s + static_cast<size_t>(h) * head_dim;
-#pragma unroll 16
-        for (uint32_t d = 0; d < head_dim; ++d) nq = __fadd_rn(nq, __fmul_rn(v[d], v[d]));
-        q.nq[static_cast<size_t>(l) * n_head_kv + h] = nq;
-    }
-}
-
-// ---------------------------------------------------------------- scorer --
-
-// One CTA = (group of kScoreBlocks blocks, one KV head, one layer): D*256
-// contiguous bytes of the tiled summary tensor.  Each thread owns one block
-// and keeps kScoreBatch coalesced channel loads in flight, then walks the
-// channels in the reference's order.  Small units (2048 at config 2) and
-// small CTAs (~14 per SM) make one balanced wave.  Per-head results go to rbuf; the last CTA of a
-// block range (over heads x layers) forms the per-layer terms in head order
-// and, when combining, the final scores in layer order.
-__global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    float *q_s = reinterpret_cast<float *>(smem);
-    const uint32_t H = a.n_head_kv;
-    const uint32_t D = a.head_dim;
-    const uint32_t ldb = a.sum.ldb;
-    const uint32_t g = blockIdx.x;
-    const uint32_t h = blockIdx.y;
-    const uint32_t l = a.layer0 + blockIdx.z;
-    const uint32_t b0 = g * kScoreBlocks;
-    const uint32_t nb = min(static_cast<uint32_t>(kScoreBlocks), a.n_blocks - b0);
-    const bool active = a.q_count[l] > 0;
-    const int tid = threadIdx.x;
-    for (uint32_t i = tid; i < D; i += blockDim.x)
-        q_s[i] = active ? a.qv[(static_cast<size_t>(l) * H + h) * D + i] : 0.0f;
-    __syncthreads();
-    {
-        // One thread per block.  Channel c of the unit is the 256-byte row
-        // h*D + c of tile (l, g): a warp's 32 loads of one channel are one
-        // 128-byte line.  kScoreBatch channels are loaded at once, then added
-        // in the reference's channel order.
-        const uint32_t b = b0 + tid;
-        const bool mine = active && static_cast<uint32_t>(tid) < nb;
-        const float inv = mine ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
-        float dot = 0.0f;
-        float nk = 0.0f;
-        if (inv != 0.0f) {
-            const float *col = a.sum.sum_t + sum_index(a.sum, l, h * D, b0) + tid;
-            for (uint32_t c0 = 0; c0 < D; c0 += kScoreBatch) {
-                float x[kScoreBatch];
-#pragma unroll
-                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreBatch); ++r)
-                    x[r] = c0 + r < D ? __ldcs(col + static_cast<size_t>(c0 + r) * kSumGroup) : 0.0f;
-#pragma unroll
-                for (uint32_t r = 0; r < static_cast<uint32_t>(kScoreBatch); ++r) {
-                    if (c0 + r < D) {
-                        const float mk = __fmul_rn(x[r], inv);
-                        dot = __fadd_rn(dot, __fmul_rn(q_s[c0 + r], mk));
-                        nk = __fadd_rn(nk, __fmul_rn(mk, mk));
-                    }
-                }
-            }
-        }
-        if (static_cast<uint32_t>(tid) < nb) {
-            float rr = 0.0f;
-            if (active) {
-                const float den = __fadd_rn(__fmul_rn(__fsqrt_rn(a.nq[static_cast<size_t>(l) * H + h]),
-                                                      __fsqrt_rn(nk)), 1e-6f);
-                rr = __fdiv_rn(dot, den);
-            }
-            a.rbuf[(static_cast<size_t>(l) * H + h) * ldb + b] = rr;
-        }
-    }
-}
-
 // x / d in double; a power-of-two d divides exactly by scaling, so the
 // product with its reciprocal is the same value as the quotient.
 __device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
@@ -198,62 +82,219 @@ __device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
     return __ddiv_rn(x, static_cast<double>(d));
 }
 
-// Combine of the scorer's per-head results (llama-memory-kvmem.cpp:2881-2912):
-// the layer term is the sum over heads in head order (double) divided by
-// n_head_kv; the score is the sum of the active layers' terms in layer order
-// divided by their number, 0 for a block without statistics.  A CTA covers
-// kCombineBlocks blocks x kCombineLanes layer lanes: each thread forms the
-// terms of its layers (their head values loaded together, coalesced across
-// the blocks), parks them in shared memory, and one thread per block then
-// adds them in layer order.
-constexpr uint32_t kCombineBlocks = 32;
-constexpr uint32_t kCombineLanes = 8;
+// ----------------------------------------------------------------- query --
 
-__global__ void __launch_bounds__(kCombineBlocks * kCombineLanes) combine_kernel(ScoreArgs a) {
-    extern __shared__ double term_s[];                 // [n_layers][kCombineBlocks]
-    const uint32_t tb = threadIdx.x % kCombineBlocks;
-    const uint32_t ly = threadIdx.x / kCombineBlocks;
-    const uint32_t bb = blockIdx.x * kCombineBlocks + tb;
-    const uint32_t H = a.n_head_kv;
-    const uint32_t ldb = a.sum.ldb;
-    const bool mine = bb < a.n_blocks;
-    if (mine) {
-        for (uint32_t li = ly; li < a.n_layers; li += kCombineLanes) {
-            const uint32_t ll = a.layer0 + li;
-            const float *rb = a.rbuf + static_cast<size_t>(ll) * H * ldb + bb;
-            double term = 0.0;
-            if (a.q_count[ll] > 0) {
-                double layer = 0.0;
-                for (uint32_t h0 = 0; h0 < H; h0 += 8u) {
-                    float x[8];
+// Programmatic dependent launch (sm_90+ PTX): let the next grid of the
+// stream launch now / wait until the grids this one depends on are complete
+// and their writes visible.  Without a programmatic launch both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// One CTA = (layer, KV head), one thread per channel:
+//   qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq,
+//   invq = 1.0f / (q_count * g); nq[l][h] = sum over d of qv*qv in order.
+__global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_head_q, uint32_t head_dim) {
+    extern __shared__ float qv_s[];
+    pdl_launch_dependents();     // the scorer may start its summary loads now
+    const uint32_t l = blockIdx.x;
+    const uint32_t h = blockIdx.y;
+    const uint32_t D = head_dim;
+    const uint32_t cnt = q.q_count[l];
+    if (cnt == 0) return;        // the scorer skips a layer without query
+    const uint32_t g = n_head_kv == 0 ? 1u : n_head_q / n_head_kv;
+    const uint32_t gg = g > 1u ? g : 1u;
+    const float invq = __fdiv_rn(1.0f, __uint2float_rn(cnt * gg));
+    const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
+    const float *qs = q.q_sum + static_cast<size_t>(l) * n_head_q * D + static_cast<size_t>(h) * g * D;
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+        float qh = 0.0f;
+        for (uint32_t g0 = 0; g0 < n_in; g0 += 8u) {
+            float x[8];
 #pragma unroll
-                    for (uint32_t k = 0; k < 8u; ++k)
-                        x[k] = h0 + k < H ? rb[static_cast<size_t>(h0 + k) * ldb] : 0.0f;
+            for (uint32_t k = 0; k < 8u; ++k)
+                x[k] = g0 + k < n_in ? qs[static_cast<size_t>(g0 + k) * D + d] : 0.0f;
 #pragma unroll
-                    for (uint32_t k = 0; k < 8u; ++k)
-                        if (h0 + k < H) layer = __dadd_rn(layer, static_cast<double>(x[k]));
-                }
-                term = div_exact_pow2(layer, H > 1u ? H : 1u);
-            }
-            a.terms[static_cast<size_t>(ll) * a.ldt + bb] = term;
-            term_s[li * kCombineBlocks + tb] = term;
+            for (uint32_t k = 0; k < 8u; ++k)
+                if (g0 + k < n_in) qh = __fadd_rn(qh, x[k]);
         }
+        const float v = __fmul_rn(qh, invq);
+        q.qv[(static_cast<size_t>(l) * n_head_kv + h) * D + d] = v;
+        qv_s[d] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float nq = 0.0f;
+#pragma unroll 16
+        for (uint32_t d = 0; d < D; ++d) nq = __fadd_rn(nq, __fmul_rn(qv_s[d], qv_s[d]));
+        q.nq[static_cast<size_t>(l) * n_head_kv + h] = nq;
+    }
+}
+
+// ---------------------------------------------------------------- scorer --
+
+// 16-byte global -> shared copy by this thread (L2 only), completing in the
+// thread's current cp.async group.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// One CTA = (range of kScoreRange blocks = one summary tile, one layer);
+// warp h scores KV head h of the range, one lane per block.  Per (block,
+// head) the thread walks the head's channels in the reference's order; its
+// next four channels are one 16-byte vector of the tiled summary tensor, so
+// the warp's loads are consecutive 512-byte pieces of one contiguous
+// head_dim*128-byte run.  Each lane streams its vectors through a ring of S
+// shared-memory stages with cp.async (S vectors in flight, no registers
+// held); the ring is filled before the CTA waits for the query prep (a
+// programmatic dependent launch).  The per-layer term (heads in order,
+// double, / H_kv) is formed in shared memory; with `combine`, the last CTA
+// of a range to finish adds the layers' terms in layer order into the block
+// scores.
+
+template <bool VEC, int S>
+__global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ uint32_t s_last;
+    const uint32_t H = a.n_head_kv;
+    const uint32_t D = a.head_dim;
+    const uint32_t ldb = a.sum.ldb;
+    const uint32_t h = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t l = a.layer0 + blockIdx.y;
+    const uint32_t b = blockIdx.x * kScoreRange + lane;
+    const bool mine = b < a.n_blocks;
+    const bool active = a.q_count[l] > 0;
+    float4 *ring = reinterpret_cast<float4 *>(sm);                 // [H][S][32]
+    float *qv_s = sm + static_cast<size_t>(H) * S * 128u;          // [H][D]
+    float *r_s = qv_s + static_cast<size_t>(H) * D;                // [H][32]
+    float *nq_s = r_s + H * 32u;                                   // [H]
+    const float inv = (mine && active) ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
+    const bool go = inv != 0.0f;
+
+    // summary vectors of (block b, head h): channel quad c of the head is at
+    // vec[c * kSumGroup]; ring stage c % S of this lane at slot[(c % S) * 32]
+    const uint32_t n4 = D / 4u;
+    const float4 *vec = reinterpret_cast<const float4 *>(a.sum.sum_t) +
+                        ((static_cast<size_t>(l) * (ldb / kSumGroup) + b / kSumGroup) * (a.sum.n_embd / 4u) +
+                         (VEC ? h * n4 : 0u)) * kSumGroup + (b % kSumGroup);
+    float4 *slot = ring + static_cast<size_t>(h) * S * 32u + lane;
+    if (VEC && go) {
+#pragma unroll
+        for (int c = 0; c < S; ++c) {
+            if (static_cast<uint32_t>(c) < n4) cp_async16(slot + c * 32, vec + static_cast<size_t>(c) * kSumGroup);
+            cp_async_commit();
+        }
+    }
+    pdl_wait();                  // the query prep's qv / nq are complete
+    if (active) {
+        const float *qg = a.qv + (static_cast<size_t>(l) * H + h) * D;
+        for (uint32_t d = lane; d < D; d += 32u) qv_s[h * D + d] = qg[d];
+        if (lane == 0) nq_s[h] = a.nq[static_cast<size_t>(l) * H + h];
+    }
+    __syncwarp();
+
+    float dot = 0.0f;
+    float nk = 0.0f;
+    const float *q = qv_s + h * D;
+    if (go) {
+        if (VEC) {
+            // group c is complete once at most S-1 later groups are pending;
+            // its stage is refilled with vector c+S after its values are used
+            uint32_t st = 0;
+            for (uint32_t c = 0; c < n4; ++c) {
+                cp_async_wait<S - 1>();
+                const float4 x = slot[st * 32u];
+                const float4 qq = *reinterpret_cast<const float4 *>(q + 4u * c);
+                float mk = __fmul_rn(x.x, inv);
+                dot = __fadd_rn(dot, __fmul_rn(qq.x, mk));
+                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                mk = __fmul_rn(x.y, inv);
+                dot = __fadd_rn(dot, __fmul_rn(qq.y, mk));
+                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                mk = __fmul_rn(x.z, inv);
+                dot = __fadd_rn(dot, __fmul_rn(qq.z, mk));
+                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                mk = __fmul_rn(x.w, inv);
+                dot = __fadd_rn(dot, __fmul_rn(qq.w, mk));
+                nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                if (c + S < n4) cp_async16(slot + st * 32u, vec + static_cast<size_t>(c + S) * kSumGroup);
+                cp_async_commit();
+                st = st + 1u == static_cast<uint32_t>(S) ? 0u : st + 1u;
+            }
+        } else {
+            // head_dim not a multiple of 4: one channel at a time
+            const uint32_t e0 = h * D;
+            for (uint32_t d0 = 0; d0 < D; d0 += 8u) {
+                float x[8];
+#pragma unroll
+                for (uint32_t k = 0; k < 8u; ++k)
+                    x[k] = d0 + k < D ? __ldcs(a.sum.sum_t + sum_index(a.sum, l, e0 + d0 + k, b)) : 0.0f;
+#pragma unroll
+                for (uint32_t k = 0; k < 8u; ++k) {
+                    if (d0 + k < D) {
+                        const float mk = __fmul_rn(x[k], inv);
+                        dot = __fadd_rn(dot, __fmul_rn(q[d0 + k], mk));
+                        nk = __fadd_rn(nk, __fmul_rn(mk, mk));
+                    }
+                }
+            }
+        }
+    }
+    // r = dot / (sqrt(nq) * sqrt(nk) + 1e-6f) of (block, head)
+    float rr = 0.0f;
+    if (active)
+        rr = __fdiv_rn(dot, __fadd_rn(__fmul_rn(__fsqrt_rn(nq_s[h]), __fsqrt_rn(nk)), 1e-6f));
+    r_s[h * 32u + lane] = rr;
+    __syncthreads();
+    if (h == 0 && mine) {
+        // layer term: the heads' results summed in head order (double) / H
+        double term = 0.0;
+        if (active) {
+            double layer = 0.0;
+            for (uint32_t hh = 0; hh < H; ++hh) layer = __dadd_rn(layer, static_cast<double>(r_s[hh * 32u + lane]));
+            term = div_exact_pow2(layer, H > 1u ? H : 1u);
+        }
+        a.terms[static_cast<size_t>(l) * a.ldt + b] = term;
     }
     if (!a.combine) return;
+    // publish the terms, then count the range's arrivals; the last CTA of the
+    // range adds the layers' terms in layer order
+    __threadfence();
     __syncthreads();
-    if (ly != 0 || !mine) return;
-    double acc = 0.0;
-    uint32_t nlay = 0;
-    for (uint32_t li = 0; li < a.n_layers; ++li) {
-        if (a.q_count[a.layer0 + li] > 0) {
-            acc = __dadd_rn(acc, term_s[li * kCombineBlocks + tb]);
-            ++nlay;
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.range_done[blockIdx.x], 1u) == gridDim.y - 1u ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (h == 0 && mine) {
+        double acc = 0.0;
+        uint32_t nlay = 0;
+        for (uint32_t l0 = 0; l0 < a.n_layers; l0 += 8u) {
+            double t[8];
+            uint32_t c[8];
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k) {
+                const uint32_t ll = a.layer0 + l0 + k;
+                const bool in = l0 + k < a.n_layers;
+                c[k] = in ? a.q_count[ll] : 0u;
+                t[k] = in ? __ldcg(a.terms + static_cast<size_t>(ll) * a.ldt + b) : 0.0;
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k) {
+                if (c[k] > 0u) {
+                    acc = __dadd_rn(acc, t[k]);
+                    ++nlay;
+                }
+            }
         }
+        bool has = false;
+        for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
+            has |= __ldcg(a.sum.mean_tok + static_cast<size_t>(ll) * ldb + b) > 0u;
+        a.scores[b] = (has && nlay) ? div_exact_pow2(acc, nlay) : 0.0;
     }
-    bool has = false;
-    for (uint32_t ll = 0; ll < a.sum.n_layer; ++ll)
-        has |= a.sum.mean_tok[static_cast<size_t>(ll) * ldb + bb] > 0u;
-    a.scores[bb] = (has && nlay) ? div_exact_pow2(acc, nlay) : 0.0;
+    if (threadIdx.x == 0) a.range_done[blockIdx.x] = 0u;    // ready for the next launch
 }
 
 __global__ void reduce_terms_kernel(const double *__restrict__ terms, uint32_t n_layers,
@@ -295,63 +336,86 @@ cudaError_t launch_download_summaries(const SummaryLayout &s, uint32_t layer, ui
     return cudaGetLastError();
 }
 
-cudaError_t launch_query_prep(const QueryState &q, uint32_t n_layer, uint32_t n_head_kv,
-                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(n_head_kv) * head_dim * sizeof(float);
-    if (smem > 48u * 1024u)
-        cudaFuncSetAttribute(query_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    query_prep_kernel<<<n_layer, 1024, smem, stream>>>(q, n_head_kv, n_head_q, head_dim);
-    return cudaGetLastError();
-}
-
-// The hardware fills an SM with as many resident CTAs as its shared memory
-// allows before it uses the next one, so a one-wave grid smaller than the
-// GPU's capacity lands unevenly (measured: busiest SM active 83K cycles, the
-// least busy 42K, of 89K).  Padding each CTA's shared memory caps residency at
+// The hardware fills an SM with as many resident CTAs as its resources allow
+// before it uses the next one, so a one-wave grid smaller than the GPU's
+// capacity lands unevenly (measured: busiest SM active 83K cycles, the least
+// busy 42K, of 89K).  Padding each CTA's shared memory caps residency at
 // ceil(units / SMs) and so spreads the wave over every SM.
-static size_t score_smem_for(uint32_t units, size_t smem_min) {
+// The hardware fills an SM with as many resident CTAs as its resources allow
+// before it uses the next one, so a one-wave grid smaller than the GPU's
+// capacity lands unevenly (measured: busiest SM active 83K cycles, the least
+// busy 42K, of 89K).  Padding each CTA's shared memory caps residency at
+// ceil(units / SMs) and so spreads the wave over every SM.
+template <bool VEC, int S>
+static size_t score_smem_for(uint32_t units, uint32_t threads, size_t smem_min) {
     // per host thread: sessions on different threads must not race on it
     static thread_local size_t cache_smem[64] = {};
     static thread_local uint32_t cache_units[64] = {};
+    static thread_local uint32_t cache_threads[64] = {};
+    static thread_local size_t cache_min[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return smem_min;
-    if (cache_units[dev] == units && cache_smem[dev] >= smem_min) return cache_smem[dev];
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cache_units[dev] == units && cache_threads[dev] == threads && cache_min[dev] == smem_min)
+        return cache_smem[dev];
+    const int sms = num_sms();
     const int want = static_cast<int>((units + static_cast<uint32_t>(sms) - 1u) / static_cast<uint32_t>(sms));
     size_t smem = smem_min;
     int occ = 0;
-    for (int it = 0; it < 512; ++it) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, score_kernel, kScoreThreads, smem) != cudaSuccess)
+    for (int it = 0; it < 1024; ++it) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, score_kernel<VEC, S>, static_cast<int>(threads),
+                                                          smem) != cudaSuccess)
             return smem_min;
         if (occ <= want || smem >= 200u * 1024u) break;
         smem += 256u;
     }
     if (occ < want) smem = smem_min;       // never cap below one wave
     cache_units[dev] = units;
+    cache_threads[dev] = threads;
+    cache_min[dev] = smem_min;
     cache_smem[dev] = smem;
     return smem;
 }
 
-cudaError_t launch_score(const ScoreArgs &a, cudaStream_t stream) {
+template <bool VEC, int S>
+static cudaError_t launch_score_t(const ScoreArgs &a, bool after_prep, cudaStream_t stream) {
+    static std::atomic<uint64_t> attr{0};
+    if (!attr_once(attr, reinterpret_cast<const void *>(score_kernel<VEC, S>), 200 * 1024))
+        return cudaErrorInvalidValue;
+    const uint32_t threads = 32u * a.n_head_kv;
+    const size_t smem_min = (static_cast<size_t>(a.n_head_kv) * (S * 128u + a.head_dim + 33u) * sizeof(float) +
+                             127u) & ~static_cast<size_t>(127u);
+    dim3 grid((a.n_blocks + kScoreRange - 1u) / kScoreRange, a.n_layers);
+    const size_t smem = score_smem_for<VEC, S>(grid.x * grid.y, threads, smem_min);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = after_prep ? 1u : 0u;
+    return cudaLaunchKernelEx(&cfg, score_kernel<VEC, S>, a);
+}
+
+cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream) {
     if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
-    const size_t smem_min = (a.head_dim * sizeof(float) + 127u) & ~static_cast<size_t>(127u);
-    cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    dim3 grid((a.n_blocks + kScoreBlocks - 1u) / kScoreBlocks, a.n_head_kv, a.n_layers);
-    const size_t smem = score_smem_for(grid.x * grid.y * grid.z, smem_min);
-    score_kernel<<<grid, kScoreThreads, smem, stream>>>(a);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    const size_t csmem = static_cast<size_t>(a.n_layers) * kCombineBlocks * sizeof(double);
-    if (csmem > 48u * 1024u) {
-        e = cudaFuncSetAttribute(combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(csmem));
+    if (a.n_head_kv == 0 || a.n_head_kv > 32u || a.head_dim == 0 || a.head_dim > 1024u)
+        return cudaErrorInvalidValue;
+    if (prep) {
+        const size_t smem = static_cast<size_t>(a.head_dim) * sizeof(float);
+        query_prep_kernel<<<dim3(n_layer_all, a.n_head_kv), a.head_dim, smem, stream>>>(*prep, a.n_head_kv,
+                                                                                          a.n_head_q, a.head_dim);
+        const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    combine_kernel<<<(a.n_blocks + kCombineBlocks - 1u) / kCombineBlocks, kCombineBlocks * kCombineLanes,
-                     csmem, stream>>>(a);
-    return cudaGetLastError();
+    // ring depth: kScoreStages vectors a lane while the ring stays within
+    // 48 KiB a CTA (up to 8 KV heads), 3 beyond
+    const bool after = prep != nullptr;
+    if (a.head_dim % 4u != 0u) return launch_score_t<false, 1>(a, after, stream);
+    if (a.n_head_kv <= 8u) return launch_score_t<true, kScoreStages>(a, after, stream);
+    return launch_score_t<true, 3>(a, after, stream);
 }
 
 cudaError_t launch_reduce_terms(const double *terms, uint32_t n_layers, uint32_t ldt,

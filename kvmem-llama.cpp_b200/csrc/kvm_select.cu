@@ -17,6 +17,7 @@
 // selected set is identical to its nth_element.  -0.0 and +0.0 compare equal
 // as in the reference; NaN scores (undefined behaviour in the reference's
 // comparator) rank below every number.
+#include "kvm_diff.cuh"
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
 
@@ -46,8 +47,10 @@ __device__ uint32_t compact_flags(const uint8_t *flags, uint32_t n, uint32_t *ou
     return total;
 }
 
-__global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
-    extern __shared__ uint8_t kept[];
+// The selection into kept[] (n bytes of shared memory: nonzero = selected)
+// and a.selected (ascending); returns the selected count to every thread.
+// Called by every thread of a kSelectThreads CTA.
+static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
     __shared__ uint32_t scratch[40];
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_kc;
@@ -60,12 +63,16 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
     const uint32_t tid = threadIdx.x;
     if (n == 0) {
         if (tid == 0) a.hdr->n_selected = 0;
-        return;
+        return 0u;
     }
     if (budget == 0 || n <= budget) {
-        for (uint32_t i = tid; i < n; i += kSelectThreads) a.selected[i] = i;
+        for (uint32_t i = tid; i < n; i += kSelectThreads) {
+            a.selected[i] = i;
+            kept[i] = 1;
+        }
         if (tid == 0) a.hdr->n_selected = n;
-        return;
+        __syncthreads();
+        return n;
     }
     for (uint32_t i = tid; i < n; i += kSelectThreads) kept[i] = 0;
     __syncthreads();
@@ -203,6 +210,26 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
     }
     const uint32_t m = compact_flags(kept, n, a.selected, scratch);
     if (tid == 0) a.hdr->n_selected = m;
+    __syncthreads();
+    return m;
+}
+
+__global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
+    extern __shared__ uint8_t kept[];
+    (void)select_core(a, kept);
+}
+
+// kvm_select followed by kvm_diff in one launch: the selection stays in
+// shared memory as the diff's block flags, and the selected list is read
+// back from the plan (written by this CTA, visible after the barrier).
+static_assert(kSelectThreads == kDiffThreads, "one CTA runs both");
+__global__ void __launch_bounds__(kSelectThreads) select_diff_kernel(SelectArgs sa, DiffArgs da) {
+    extern __shared__ uint8_t fl[];
+    const uint32_t n = sa.n_blocks;
+    uint8_t *kept = fl;
+    uint8_t *was = fl + (n ? n : 1u);
+    const uint32_t m = select_core(sa, kept);
+    diff_core(da, min(m, n), kept, was, true);
 }
 
 // set_selection's canonicalisation: sort ascending, drop duplicates and ids
@@ -229,6 +256,17 @@ cudaError_t launch_select(const SelectArgs &a, cudaStream_t stream) {
     if (smem > 48u * 1024u)
         cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     select_kernel<<<1, kSelectThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select_diff(const SelectArgs &sa, const DiffArgs &da, cudaStream_t stream) {
+    const size_t smem = 2u * (sa.n_blocks ? sa.n_blocks : 1u);
+    if (smem > 48u * 1024u) {
+        const cudaError_t e = cudaFuncSetAttribute(select_diff_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    select_diff_kernel<<<1, kSelectThreads, smem, stream>>>(sa, da);
     return cudaGetLastError();
 }
 

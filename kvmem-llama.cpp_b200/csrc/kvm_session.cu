@@ -64,12 +64,22 @@ struct kvm_session {
     uint32_t test_inject = 0;          // kvm_test_inject flags for the next stage-in launch
     bool have_selection = false;
     bool have_plan = false;
+    // Deferred launches.  kvm_select records its selection here and the next
+    // kvm_diff runs select + diff as one kernel; kvm_reset_window records the
+    // reset and the next diff applies it while it reads the block table.
+    // Every other entry point first launches what is pending (flush_pending),
+    // so the order of the calls keeps its meaning.
+    bool select_pending = false;
+    uint32_t select_n_mandatory = 0;
+    cudaStream_t select_stream = nullptr;
+    bool reset_pending = false;
+    cudaStream_t reset_stream = nullptr;
 
     // device state
     SummaryLayout sum{};
     QueryState q{};
     double *d_terms = nullptr;
-    float *d_rbuf = nullptr;           // per-head scorer results [L][H][ldb]
+    uint32_t *d_range_done = nullptr;  // scorer arrival counters [ldb / kScoreRange]
     double *d_scores = nullptr;
     double *d_acc = nullptr;
     BlockTable bt{};
@@ -207,13 +217,55 @@ kvm_status check_status(kvm_session *s) {
     return KVM_OK;
 }
 
-__global__ void reset_window_kernel(BlockTable bt, uint32_t n) {
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        bt.in_ws[i] = 0;
-        if (bt.tier[i] == KVM_TIER_GPU) bt.tier[i] = KVM_TIER_CPU;
-        bt.gpu_slot[i] = -1;
-    }
+SelectArgs select_args(kvm_session *s, uint32_t n_mandatory) {
+    SelectArgs a{};
+    a.scores = s->d_scores;
+    a.n_blocks = s->n_blocks;
+    a.budget = s->budget_blocks;
+    a.sink = s->cfg.sink_blocks;
+    a.recent = s->cfg.recent_blocks;
+    a.mandatory = s->d_mandatory;
+    a.n_mandatory = n_mandatory;
+    a.selected = s->plan.selected;
+    a.hdr = s->plan.hdr;
+    return a;
 }
+
+// Launch the deferred select / window reset, each on the stream of the call
+// that recorded it.  An entry point flushes what it depends on: the
+// selection before anything that rewrites the scores, the plan or the block
+// count; the reset before anything that reads or writes the block table.
+kvm_status flush_select(kvm_session *s) {
+    if (!s->select_pending) return KVM_OK;
+    s->select_pending = false;
+    KVM_CUDA(s, launch_select(select_args(s, s->select_n_mandatory), s->select_stream), "select launch");
+    s->launches++;
+    return KVM_OK;
+}
+
+kvm_status flush_reset(kvm_session *s) {
+    if (!s->reset_pending) return KVM_OK;
+    s->reset_pending = false;
+    KVM_CUDA(s, launch_reset_window(s->bt, s->n_blocks, s->reset_stream), "reset launch");
+    s->launches++;
+    return KVM_OK;
+}
+
+#define KVM_FLUSH_SEL(s)                               \
+    do {                                               \
+        const kvm_status f__ = flush_select(s);        \
+        if (f__ != KVM_OK) return f__;                 \
+    } while (0)
+#define KVM_FLUSH_RESET(s)                             \
+    do {                                               \
+        const kvm_status f__ = flush_reset(s);         \
+        if (f__ != KVM_OK) return f__;                 \
+    } while (0)
+#define KVM_FLUSH(s)                                   \
+    do {                                               \
+        KVM_FLUSH_SEL(s);                              \
+        KVM_FLUSH_RESET(s);                            \
+    } while (0)
 
 kvm_status upload_window(kvm_session *s, cudaStream_t st, const kvm_window *win) {
     const uint32_t L = s->cfg.n_layer;
@@ -664,7 +716,7 @@ kvm_status kvm_session_create(const kvm_config *cfg, int device, kvm_session **o
         {reinterpret_cast<void **>(&s->q.qv), sizeof(float) * L * E},
         {reinterpret_cast<void **>(&s->q.nq), sizeof(float) * L * c.n_head_kv},
         {reinterpret_cast<void **>(&s->d_terms), sizeof(double) * L * ldb},
-        {reinterpret_cast<void **>(&s->d_rbuf), sizeof(float) * L * c.n_head_kv * ldb},
+        {reinterpret_cast<void **>(&s->d_range_done), sizeof(uint32_t) * (ldb / kScoreRange)},
         {reinterpret_cast<void **>(&s->d_scores), sizeof(double) * ldb},
         {reinterpret_cast<void **>(&s->d_acc), sizeof(double) * ldb},
         {reinterpret_cast<void **>(&s->bt.n_tokens), sizeof(uint32_t) * nb},
@@ -752,6 +804,7 @@ kvm_status kvm_register_append(kvm_session *s, kvm_stream stream, uint32_t n_new
     if (!s) return KVM_EINVAL;
     if (n_new == 0) return KVM_OK;
     DeviceGuard g(s->device);
+    KVM_FLUSH(s);
     cudaStream_t st = as_stream(stream);
     const uint32_t bt = s->cfg.block_tokens;
     // plan the append on the host (KvMemStore::register_append)
@@ -827,6 +880,7 @@ kvm_status kvm_set_block_tier(kvm_session *s, kvm_stream stream, uint32_t block_
     if (tier != KVM_TIER_GPU && tier != KVM_TIER_CPU && tier != KVM_TIER_SSD)
         return fail(s, KVM_EINVAL, "bad tier %d", tier);
     DeviceGuard g(s->device);
+    KVM_FLUSH_RESET(s);
     cudaStream_t st = as_stream(stream);
     const uint8_t t = static_cast<uint8_t>(tier);
     kvm_status r = upload_small(s, st, s->bt.tier + block_id, &t, 1);
@@ -843,6 +897,7 @@ kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t bl
     if (block_id >= s->n_blocks) return KVM_OK;
     if (slot >= static_cast<int32_t>(s->n_slots)) return fail(s, KVM_EINVAL, "slot %d >= window slots", slot);
     DeviceGuard g(s->device);
+    KVM_FLUSH_RESET(s);
     const int32_t v = slot < 0 ? -1 : slot;
     kvm_status r = upload_small(s, as_stream(stream), s->bt.gpu_slot + block_id, &v, sizeof v);
     if (r == KVM_OK && block_id < s->h_slot.size()) s->h_slot[block_id] = v;
@@ -853,11 +908,11 @@ kvm_status kvm_set_block_gpu_slot(kvm_session *s, kvm_stream stream, uint32_t bl
 kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
+    // a pending select does not read the block table: it may stay pending
+    // and fuse with the next diff, which also applies this reset
     if (s->n_blocks) {
-        reset_window_kernel<<<std::min(1024u, (s->n_blocks + 255u) / 256u), 256, 0, as_stream(stream)>>>(
-            s->bt, s->n_blocks);
-        KVM_CUDA(s, cudaGetLastError(), "reset launch");
-        s->launches++;
+        s->reset_pending = true;
+        s->reset_stream = as_stream(stream);
     }
     std::fill(s->h_slot.begin(), s->h_slot.end(), -1);
     s->slots_known = true;
@@ -972,17 +1027,13 @@ AddRowsArgs add_rows_args(const kvm_rows *r, float *acc, uint32_t n_elem) {
     return a;
 }
 
-// Query prep (qv, nq) after the query accumulators changed.
-kvm_status ensure_query(kvm_session *s, cudaStream_t st) {
+// After the query changed: upload q_count; *prep tells the scorer launch to
+// run the query prep (qv, nq) first.
+kvm_status ensure_query(kvm_session *s, cudaStream_t st, bool *prep) {
+    *prep = s->q_dirty;
     if (!s->q_dirty) return KVM_OK;
     const uint32_t L = s->cfg.n_layer;
-    kvm_status r = upload_small(s, st, s->q.q_count, s->h_q_count.data(), sizeof(uint32_t) * L);
-    if (r != KVM_OK) return r;
-    KVM_CUDA(s, launch_query_prep(s->q, L, s->cfg.n_head_kv, s->cfg.n_head_q, s->cfg.head_dim, st),
-             "query prep");
-    s->launches++;
-    s->q_dirty = false;
-    return KVM_OK;
+    return upload_small(s, st, s->q.q_count, s->h_q_count.data(), sizeof(uint32_t) * L);
 }
 
 }  // namespace
@@ -1178,7 +1229,7 @@ kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum, 
                                 cudaMemcpyDefault, st), "query copy");
     s->h_q_count.assign(q_count, q_count + L);
     s->q_dirty = true;
-    return ensure_query(s, st);
+    return KVM_OK;
 }
 
 static ScoreArgs score_args(kvm_session *s) {
@@ -1188,28 +1239,41 @@ static ScoreArgs score_args(kvm_session *s) {
     a.nq = s->q.nq;
     a.q_count = s->q.q_count;
     a.n_head_kv = s->cfg.n_head_kv;
+    a.n_head_q = s->cfg.n_head_q;
     a.head_dim = s->cfg.head_dim;
     a.n_blocks = s->n_blocks;
     a.terms = s->d_terms;
     a.ldt = s->sum.ldb;
-    a.rbuf = s->d_rbuf;
     a.status = s->d_status;
+    a.range_done = s->d_range_done;
     a.scores = s->d_scores;
     return a;
+}
+
+// The scorer launch, after the query prep when the query changed (the prep
+// covers every layer; nothing runs when there are no blocks or layers).
+static kvm_status run_score(kvm_session *s, const ScoreArgs &a, bool prep, cudaStream_t st) {
+    if (s->n_blocks == 0 || a.n_layers == 0) return KVM_OK;
+    KVM_CUDA(s, launch_score(a, prep ? &s->q : nullptr, s->cfg.n_layer, st), "score launch");
+    s->launches += prep ? 2u : 1u;
+    if (prep) s->q_dirty = false;
+    return KVM_OK;
 }
 
 kvm_status kvm_score(kvm_session *s, kvm_stream stream, double *d_scores) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
+    KVM_FLUSH_SEL(s);
     cudaStream_t st = as_stream(stream);
-    kvm_status r = ensure_query(s, st);
+    bool prep = false;
+    kvm_status r = ensure_query(s, st, &prep);
     if (r != KVM_OK) return r;
     ScoreArgs a = score_args(s);
     a.layer0 = 0;
     a.n_layers = s->cfg.n_layer;
     a.combine = 1;
-    KVM_CUDA(s, launch_score(a, st), "score launch");
-    s->launches++;
+    r = run_score(s, a, prep, st);
+    if (r != KVM_OK) return r;
     if (d_scores && s->n_blocks)
         KVM_CUDA(s, cudaMemcpyAsync(d_scores, s->d_scores, sizeof(double) * s->n_blocks,
                                     cudaMemcpyDeviceToDevice, st), "score copy");
@@ -1222,7 +1286,9 @@ kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0, u
     if (static_cast<uint64_t>(layer0) + n_layers > s->cfg.n_layer) return fail(s, KVM_EINVAL, "layers out of range");
     if (!d_terms || ldt < s->n_blocks) return fail(s, KVM_EINVAL, "bad terms buffer");
     DeviceGuard g(s->device);
-    kvm_status r = ensure_query(s, as_stream(stream));
+    KVM_FLUSH_SEL(s);
+    bool prep = false;
+    kvm_status r = ensure_query(s, as_stream(stream), &prep);
     if (r != KVM_OK) return r;
     ScoreArgs a = score_args(s);
     a.layer0 = layer0;
@@ -1230,9 +1296,7 @@ kvm_status kvm_score_terms(kvm_session *s, kvm_stream stream, uint32_t layer0, u
     a.terms = d_terms;
     a.ldt = ldt;
     a.combine = 0;
-    KVM_CUDA(s, launch_score(a, as_stream(stream)), "score launch");
-    s->launches++;
-    return KVM_OK;
+    return run_score(s, a, prep, as_stream(stream));
 }
 
 kvm_status kvm_reduce_terms(kvm_session *s, kvm_stream stream, const double *d_terms, uint32_t n_layers,
@@ -1249,6 +1313,7 @@ kvm_status kvm_reduce_terms(kvm_session *s, kvm_stream stream, const double *d_t
 kvm_status kvm_set_scores_from_sum(kvm_session *s, kvm_stream stream, const double *d_acc, uint32_t n_active) {
     if (!s || !d_acc) return KVM_EINVAL;
     DeviceGuard g(s->device);
+    KVM_FLUSH_SEL(s);
     KVM_CUDA(s, launch_scores_from_sum(s->sum, s->n_blocks, d_acc, n_active, s->d_scores, as_stream(stream)),
              "scores from sum");
     s->launches++;
@@ -1258,6 +1323,7 @@ kvm_status kvm_set_scores_from_sum(kvm_session *s, kvm_stream stream, const doub
 kvm_status kvm_set_scores(kvm_session *s, kvm_stream stream, const double *scores, uint32_t n) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
+    KVM_FLUSH_SEL(s);
     cudaStream_t st = as_stream(stream);
     // KvMemStore::set_retrieval_scores: entries beyond `n` read as 0
     if (s->n_blocks) KVM_CUDA(s, cudaMemsetAsync(s->d_scores, 0, sizeof(double) * s->n_blocks, st), "clear");
@@ -1274,21 +1340,16 @@ kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandato
     if (n_mandatory > s->max_blocks) return fail(s, KVM_EINVAL, "too many mandatory blocks");
     if (n_mandatory && !mandatory) return fail(s, KVM_EINVAL, "null mandatory");
     DeviceGuard g(s->device);
+    // an earlier select still pending runs now; a pending reset may wait for the diff
+    KVM_FLUSH_SEL(s);
     cudaStream_t st = as_stream(stream);
     kvm_status r = upload_small(s, st, s->d_mandatory, mandatory, sizeof(uint32_t) * n_mandatory);
     if (r != KVM_OK) return r;
-    SelectArgs a{};
-    a.scores = s->d_scores;
-    a.n_blocks = s->n_blocks;
-    a.budget = s->budget_blocks;
-    a.sink = s->cfg.sink_blocks;
-    a.recent = s->cfg.recent_blocks;
-    a.mandatory = s->d_mandatory;
-    a.n_mandatory = n_mandatory;
-    a.selected = s->plan.selected;
-    a.hdr = s->plan.hdr;
-    KVM_CUDA(s, launch_select(a, st), "select launch");
-    s->launches++;
+    // the selection kernel runs with the next kvm_diff (one fused launch) or
+    // with whatever entry point comes first
+    s->select_pending = true;
+    s->select_n_mandatory = n_mandatory;
+    s->select_stream = st;
     s->have_selection = true;
     return KVM_OK;
 }
@@ -1303,6 +1364,7 @@ kvm_status kvm_select_groups(kvm_session *s, kvm_stream stream, const uint32_t *
     if (group_select_smem(n_groups, s->n_blocks) > 200u * 1024u)
         return fail(s, KVM_EINVAL, "too many groups for %u blocks", s->n_blocks);
     DeviceGuard g(s->device);
+    KVM_FLUSH_SEL(s);
     cudaStream_t st = as_stream(stream);
     kvm_status r = upload_small(s, st, s->d_mandatory, mandatory, sizeof(uint32_t) * n_mandatory);
     if (r != KVM_OK) return r;
@@ -1347,6 +1409,7 @@ kvm_status kvm_set_selection_ids(kvm_session *s, kvm_stream stream, const uint32
     if (n > s->max_blocks) return fail(s, KVM_EINVAL, "too many ids");
     if (n && !ids) return fail(s, KVM_EINVAL, "null ids");
     DeviceGuard g(s->device);
+    KVM_FLUSH_SEL(s);
     cudaStream_t st = as_stream(stream);
     kvm_status r = upload_small(s, st, s->d_ids, ids, sizeof(uint32_t) * n);
     if (r != KVM_OK) return r;
@@ -1360,6 +1423,10 @@ kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh) {
     if (!s) return KVM_EINVAL;
     if (!s->have_selection) return fail(s, KVM_ESTATE, "kvm_diff needs a selection (kvm_select)");
     DeviceGuard g(s->device);
+    cudaStream_t st = as_stream(stream);
+    // a pending select or reset recorded on another stream runs there first
+    if (s->select_pending && s->select_stream != st) KVM_FLUSH_SEL(s);
+    if (s->reset_pending && s->reset_stream != st) KVM_FLUSH_RESET(s);
     DiffArgs a{};
     a.bt = s->bt;
     a.n_blocks = s->n_blocks;
@@ -1372,7 +1439,14 @@ kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh) {
     a.force_raw_refresh = force_raw_refresh;
     a.plan = s->plan;
     a.status = s->d_status;
-    KVM_CUDA(s, launch_diff(a, as_stream(stream)), "diff launch");
+    a.reset_window = s->reset_pending ? 1u : 0u;
+    s->reset_pending = false;
+    if (s->select_pending) {
+        s->select_pending = false;
+        KVM_CUDA(s, launch_select_diff(select_args(s, s->select_n_mandatory), a, st), "select+diff launch");
+    } else {
+        KVM_CUDA(s, launch_diff(a, st), "diff launch");
+    }
     s->launches++;
     s->have_selection = false;
     s->have_plan = true;
@@ -1389,6 +1463,7 @@ kvm_status kvm_stagein(kvm_session *s, kvm_stream stream, const kvm_source *src,
     kvm_status r = source_check(s, src);
     if (r != KVM_OK) return r;
     DeviceGuard g(s->device);
+    KVM_FLUSH(s);
     cudaStream_t st = as_stream(stream);
     r = upload_window(s, st, win);
     if (r != KVM_OK) return r;
@@ -1422,6 +1497,7 @@ kvm_status kvm_stagein_packed(kvm_session *s, kvm_stream stream, const kvm_packe
     if (src->location != KVM_LOC_DEVICE && src->location != KVM_LOC_HOST)
         return fail(s, KVM_EINVAL, "bad source location");
     DeviceGuard g(s->device);
+    KVM_FLUSH(s);
     cudaStream_t st = as_stream(stream);
     kvm_status r = upload_window(s, st, win);
     if (r != KVM_OK) return r;
@@ -1458,6 +1534,7 @@ kvm_status kvm_stageout(kvm_session *s, kvm_stream stream, const uint32_t *ids, 
     if (n > s->max_blocks) return fail(s, KVM_EINVAL, "at most max_blocks (%u) blocks per call", s->max_blocks);
     if (!win || !win->d_k || !win->d_v) return fail(s, KVM_EINVAL, "null window");
     DeviceGuard g(s->device);
+    KVM_FLUSH(s);
     cudaStream_t st = as_stream(stream);
     kvm_status r = upload_window(s, st, win);
     if (r != KVM_OK) return r;
@@ -1566,6 +1643,7 @@ kvm_status kvm_test_inject(kvm_session *s, uint32_t flags) {
 kvm_status kvm_wait(kvm_session *s, kvm_stream stream, uint32_t timeout_ms) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
+    KVM_FLUSH(s);
     cudaEvent_t ev;
     KVM_CUDA(s, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
     cudaError_t e = cudaEventRecord(ev, as_stream(stream));
