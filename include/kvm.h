@@ -482,17 +482,21 @@ uint64_t kvm_kernel_launches(const kvm_session *s);
 
 /* Quantize n_rows F16 rows of n_embd values (device pointers, rows
  * contiguous) to `type` rows at d_dst -- the stage-in kernel on a plain
- * row range.  Returns KVM_EINVAL for unsupported widths. */
+ * row range.  d_src must be 16-byte and d_dst 2-byte aligned.  Returns
+ * KVM_EINVAL for unsupported widths or alignments, KVM_EDEVICE when a
+ * bounded device wait ran out (message in kvm_last_error(NULL)).  Allocates
+ * a small work list and waits on the host for the stream before it returns. */
 kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
                              uint64_t n_rows, uint32_t n_embd, void *d_dst);
 
 /*
  * kvm_quantize_rows without any device allocation.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc while they
- * run -- code being recorded into a CUDA graph, runtimes whose caching
- * allocator owns all free HBM, latency-critical loops that cannot take the
- * device-wide synchronisation of cudaMalloc/cudaFree.  Same arguments and
- * bytes as kvm_quantize_rows; stream-ordered, no host wait.
+ * run -- runtimes whose caching allocator owns all free HBM, latency-critical
+ * loops that cannot take the device-wide synchronisation of
+ * cudaMalloc/cudaFree.  Same arguments, alignment rules and bytes as
+ * kvm_quantize_rows; stream-ordered, no host wait, so a bounded device wait
+ * that runs out inside the kernel is not reported.
  * The work list lives in a fixed device array of 16384 row tiles (a tile is
  * 8192 / n_embd rows, at most 128: 131072 rows at n_embd 1024); larger calls
  * return KVM_EINVAL (message in kvm_last_error(NULL)).  The array is shared

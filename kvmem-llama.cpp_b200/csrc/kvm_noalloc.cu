@@ -2,10 +2,9 @@
 // its work list in a fixed device array instead of a cudaMalloc'd buffer.
 //
 // Who needs it: callers that must not allocate device memory while they run.
-// For example, a decode loop being recorded into a CUDA graph (allocation is
-// not a capturable operation), a runtime whose caching allocator already owns
-// all free HBM (a raw cudaMalloc fails or fragments it), or a latency-critical
-// path that cannot afford the implicit device synchronisation of cudaMalloc /
+// For example, a runtime whose caching allocator already owns all free HBM
+// (a raw cudaMalloc then fails or fragments it), or a latency-critical path
+// that cannot afford the implicit device synchronisation of cudaMalloc /
 // cudaFree.  kvm_quantize_rows allocates, uses and frees a small work list on
 // every call, so those callers cannot use it.
 //
@@ -87,6 +86,10 @@ extern "C" kvm_status kvm_quantize_rows_noalloc(kvm_stream stream, int32_t type,
     if (!type_ok || n_embd == 0 || n_embd % 32u != 0 || n_embd > 16384u) return KVM_EINVAL;
     if (n_rows == 0) return KVM_OK;
     if (!d_src || !d_dst || (reinterpret_cast<uintptr_t>(d_src) & 15u)) return KVM_EINVAL;
+    if (reinterpret_cast<uintptr_t>(d_dst) & 1u) {
+        set_sessionless_error("kvm_quantize_rows_noalloc: d_dst must be 2-byte aligned");
+        return KVM_EINVAL;
+    }
     const uint32_t R = stagein_rows_per_tile(n_embd, 128u);
     const uint64_t n_items64 = (n_rows + R - 1) / R;
     if (n_items64 > kNoallocMaxItems) {
@@ -104,9 +107,11 @@ extern "C" kvm_status kvm_quantize_rows_noalloc(kvm_stream stream, int32_t type,
     noalloc_fill_kernel<<<(n_items + 255u) / 256u, 256, 0, st>>>(w, n_items, n_rows, R,
                                                                   static_cast<uint8_t *>(d_dst));
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return KVM_ECUDA;
-    const uint32_t rb = static_cast<uint32_t>((n_embd / 32u) * static_cast<uint32_t>(
-        type == KVM_TYPE_Q8_0 ? 34 : type == KVM_TYPE_Q4_0 ? 18 : type == KVM_TYPE_Q5_0 ? 22 : 64));
+    if (e != cudaSuccess) {
+        set_sessionless_error(cudaGetErrorString(e));
+        return KVM_ECUDA;
+    }
+    const uint32_t rb = static_cast<uint32_t>(kvm_row_bytes(type, n_embd));
     StageinArgs a{};
     a.cold_block = w;
     a.cold_to = reinterpret_cast<const int32_t *>(w + kNoallocMaxItems);
@@ -137,7 +142,11 @@ extern "C" kvm_status kvm_quantize_rows_noalloc(kvm_stream stream, int32_t type,
     a.tile_in_bytes = R * n_embd * 2u;
     a.tile_out_bytes = (R * rb + 15u) & ~15u;
     a.bulk_store = (rb % 16u == 0 && (reinterpret_cast<uintptr_t>(d_dst) & 15u) == 0) ? 1u : 0u;
-    a.status = nullptr;
+    a.status = nullptr;        // no host wait: a wait timeout inside is not reported
     e = launch_stagein(a, st, 0);
-    return e == cudaSuccess ? KVM_OK : KVM_ECUDA;
+    if (e != cudaSuccess) {
+        set_sessionless_error(cudaGetErrorString(e));
+        return KVM_ECUDA;
+    }
+    return KVM_OK;
 }

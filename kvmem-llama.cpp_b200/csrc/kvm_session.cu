@@ -274,6 +274,9 @@ kvm_status upload_window(kvm_session *s, cudaStream_t st, const kvm_window *win)
         w[l] = win->d_k[l];
         w[L + l] = win->d_v[l];
         if (!w[l] || !w[L + l]) return fail(s, KVM_EINVAL, "window layer %u has a null base", l);
+        // every copy into the window stores at least 2-byte words
+        if ((reinterpret_cast<uintptr_t>(w[l]) | reinterpret_cast<uintptr_t>(w[L + l])) & 1u)
+            return fail(s, KVM_EINVAL, "window layer %u base is not 2-byte aligned", l);
     }
     if (w != s->h_win) {
         const kvm_status r = upload_small(s, st, s->d_win, w.data(), w.size() * sizeof(void *));
@@ -1700,7 +1703,8 @@ kvm_status kvm_get_plan(kvm_session *s, kvm_stream stream, kvm_plan *p, uint32_t
     if ((r = get(p->cold_block, s->plan.cold_block, h.n_cold, 4)) != KVM_OK) return r;
     if ((r = get(p->cold_to, s->plan.cold_to, h.n_cold, 4)) != KVM_OK) return r;
     // host view of the window after this plan: slot i = i-th selected block
-    if (s->have_plan && h.n_blocks == s->n_blocks) {
+    // (only when the selection read back is the one the last diff laid out)
+    if (s->have_plan && !s->have_selection && h.n_blocks == s->n_blocks) {
         std::fill(s->h_slot.begin(), s->h_slot.end(), -1);
         for (uint32_t i = 0; i < h.n_selected; ++i)
             if (sel[i] < s->h_slot.size()) s->h_slot[sel[i]] = static_cast<int32_t>(i);
@@ -1736,6 +1740,10 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     if (!type_ok(type) || n_embd == 0 || n_embd % 32u != 0 || n_embd > 16384u) return KVM_EINVAL;
     if (n_rows == 0) return KVM_OK;
     if (!d_src || !d_dst || (reinterpret_cast<uintptr_t>(d_src) & 15u)) return KVM_EINVAL;
+    if (reinterpret_cast<uintptr_t>(d_dst) & 1u) {
+        set_sessionless_error("kvm_quantize_rows: d_dst must be 2-byte aligned");
+        return KVM_EINVAL;
+    }
     // rows as one pseudo-block per tile run: item i = rows [i*R, (i+1)*R)
     const uint32_t rb = static_cast<uint32_t>(kvm_row_bytes(type, n_embd));
     const uint32_t R = stagein_rows_per_tile(n_embd, 128u);
@@ -1746,8 +1754,9 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     uint32_t *d_list = nullptr;
     uint8_t **d_dst_arr = nullptr;
     const size_t list_bytes = (3ull * n_items * sizeof(uint32_t) + 255u) & ~static_cast<size_t>(255u);
-    if (cudaMalloc(&d_list, list_bytes + 256) != cudaSuccess) return KVM_ENOMEM;
+    if (cudaMalloc(&d_list, list_bytes + 512) != cudaSuccess) return KVM_ENOMEM;
     d_dst_arr = reinterpret_cast<uint8_t **>(reinterpret_cast<uint8_t *>(d_list) + list_bytes);
+    uint32_t *d_stat = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(d_list) + list_bytes + 256);
     std::vector<uint32_t> h(3ull * n_items);
     for (uint32_t i = 0; i < n_items; ++i) {
         h[i] = i;
@@ -1760,6 +1769,7 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     cudaError_t e = cudaMemcpyAsync(d_list, h.data(), h.size() * sizeof(uint32_t),
                                     cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_dst_arr, dst_ptrs, sizeof dst_ptrs, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_stat, 0, sizeof(uint32_t), st);
     StageinArgs a{};
     a.cold_block = d_list;
     a.cold_to = reinterpret_cast<const int32_t *>(d_list + n_items);
@@ -1790,11 +1800,22 @@ kvm_status kvm_quantize_rows(kvm_stream stream, int32_t type, const void *d_src,
     a.tile_in_bytes = R * n_embd * 2u;
     a.tile_out_bytes = (R * rb + 15u) & ~15u;
     a.bulk_store = (rb % 16u == 0 && (reinterpret_cast<uintptr_t>(d_dst) & 15u) == 0) ? 1u : 0u;
-    a.status = nullptr;
+    a.status = d_stat;
     if (e == cudaSuccess) e = launch_stagein(a, st, 0);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    uint32_t stat = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&stat, d_stat, sizeof stat, cudaMemcpyDeviceToHost);
     cudaFree(d_list);
-    return e == cudaSuccess ? KVM_OK : (e == cudaErrorMemoryAllocation ? KVM_ENOMEM : KVM_ECUDA);
+    if (e != cudaSuccess) {
+        set_sessionless_error(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? KVM_ENOMEM : KVM_ECUDA;
+    }
+    if (stat) {
+        set_sessionless_error(stat & kErrTimeout ? "kvm_quantize_rows: a bounded device wait timed out"
+                                                 : "kvm_quantize_rows: device error flag");
+        return KVM_EDEVICE;
+    }
+    return KVM_OK;
 }
 
 }  // extern "C"

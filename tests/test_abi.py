@@ -60,6 +60,19 @@ def test_host_only_calls_without_gpu():
     assert L.kvm_session_create(None, 0, C.byref(h)) == kvm.KVM_EINVAL
 
 
+def test_row_quantizers_reject_odd_destinations_before_any_launch():
+    """An odd d_dst would reach 2-byte device stores; both row quantizers
+    return KVM_EINVAL first (the pointers are never dereferenced or launched
+    on, so this runs without a GPU)."""
+    import kvm
+    L = kvm.lib()
+    src, odd = 0x10000, 0x20001
+    for fn in (L.kvm_quantize_rows, L.kvm_quantize_rows_noalloc):
+        assert fn(None, kvm.TYPE_Q8_0, src, 4, 1024, odd) == kvm.KVM_EINVAL
+        assert b"2-byte aligned" in L.kvm_last_error(None)
+        assert fn(None, kvm.TYPE_Q8_0, src + 8, 4, 1024, 0x20000) == kvm.KVM_EINVAL
+
+
 C_LAYOUT = r"""
 #include <stddef.h>
 #include <stdio.h>

@@ -1,8 +1,10 @@
 """kvm_quantize_rows_noalloc: the quantize entry point for callers that cannot
-call cudaMalloc (graph capture, allocator-owned HBM, latency-critical loops).
+call cudaMalloc (a caching allocator owns all free HBM, or a latency-critical
+loop cannot take the device-wide synchronisation of cudaMalloc/cudaFree).
 It must write exactly the bytes of kvm_quantize_rows.  Two calls in a row
 check that the shared fixed work array carries nothing from one call into the
-next.  Named so pytest collects it last; it calls the C ABI directly."""
+next; a call of exactly 16384 row tiles fills the whole array.  Named so
+pytest collects it last; it calls the C ABI directly."""
 import ctypes as C
 
 import numpy as np
@@ -47,3 +49,19 @@ def test_noalloc_rejects_oversized_calls(kvm_lib):
                                      dst.data_ptr())
     assert st == kvm_lib.KVM_EINVAL
     assert b"16384 row tiles" in L.kvm_last_error(None)
+
+
+def test_noalloc_full_array(kvm_lib, oracle):
+    """Exactly the array's 16384 row tiles (n_embd 8192: one row a tile), then
+    a small call: both equal kvm_quantize_rows byte for byte."""
+    import torch
+    L = kvm_lib.lib()
+    rng = np.random.default_rng(77)
+    for n, E in ((16384, 8192), (5, 1024)):
+        rows = oracle.synth_f16(rng, (n, E), E)
+        src = torch.from_numpy(rows).cuda()
+        want = _run(kvm_lib, L.kvm_quantize_rows, kvm_lib.TYPE_Q8_0, src, n, E, torch)
+        got = _run(kvm_lib, L.kvm_quantize_rows_noalloc, kvm_lib.TYPE_Q8_0, src, n, E, torch)
+        assert np.array_equal(got, want), (n, E)
+        del src
+    torch.cuda.empty_cache()
