@@ -11,8 +11,13 @@ sink 1, cold window: all 256 selected blocks staged every step).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kvm|reference]
 
 N > 1 runs under torchrun, one process per GPU; every rank runs its own
-session (independent agent sessions: weak scaling, no data-path collective).
-Prints one JSON line on rank 0.
+session (independent agent sessions: weak scaling, no data-path collective)
+for the headline value.  The same line then carries the north star's other
+two multi-GPU workloads on the same ranks: `config5` (64 sessions of 131072
+tokens split over the ranks) and `layer_split` (one 1M-token session whose 16
+layers are split over the ranks, per-layer score terms combined over NCCL by
+all-gather and by all-reduce, with a bit-exact check against one full-session
+score on rank 0).  Prints one JSON line on rank 0.
 """
 import argparse
 import json
@@ -48,6 +53,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-scale-extras", action="store_true",
+                    help="N > 1: skip the config-5 and layer-split keys of the bench line")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-clock-probe", action="store_true",
                     help="skip the extra second of load that lets nvidia-smi sample clocks")
@@ -363,6 +370,14 @@ def run_kvm(args):
     if dist:
         dist.barrier()
     sess.close()
+    if world > 1 and not args.no_scale_extras:
+        # the north star's other two multi-GPU workloads, same ranks and group
+        del hk, hv, win_k, win_v, qs
+        torch.cuda.empty_cache()
+        result["config5"] = config5_phase(args, torch, kvm, dist, world, rank, local, dev,
+                                          args.steps, args.warmup)
+        result["layer_split"] = layer_split_phase(args, torch, kvm, dist, world, rank, local, dev,
+                                                  args.steps, args.warmup)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if dist:
@@ -441,12 +456,17 @@ def host_cores():
 
 
 def cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref_store=None, blocks=None,
-             sample_blocks=None):
-    """The reference's CPU reselection on host cores: score_retrieval restated,
-    pick_topk + set_selection (the reference's own libkvmem when given), then
-    gather + quantize of the staged blocks.  Returns per-stage seconds."""
-    L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
+             sample_blocks=None, q_threads=None):
+    """The reference's CPU reselection on host cores: score_retrieval restated
+    (`threads` threads), pick_topk + set_selection (the reference's own
+    libkvmem when given; single-threaded as in the reference), then the
+    gather of the staged blocks' F16 rows of every layer and their
+    quantization in one call per K/V (`q_threads` threads, default
+    `threads`), on the first `sample_blocks` staged blocks when given and
+    scaled to all.  Returns per-stage seconds."""
+    T = c["block_tokens"]
     E = c["n_head_kv"] * c["head_dim"]
+    q_threads = threads if q_threads is None else q_threads
     t0 = time.perf_counter()
     scores = O.score(sums, cnt, has, q, qc, c["n_head_kv"], c["n_head_q"], c["head_dim"],
                      n_threads=threads)
@@ -467,14 +487,46 @@ def cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref_store=Non
     t2 = time.perf_counter()
     todo = staged if sample_blocks is None else staged[:sample_blocks]
     P = pool_k.shape[1]
-    for blk in todo:
-        for l in range(L):
-            O.quantize_rows_f16(c["type_k"], pool_k[l, int(blk) % P], n_threads=threads)
-            O.quantize_rows_f16(c["type_v"], pool_v[l, int(blk) % P], n_threads=threads)
+    idx = np.array([int(b) % P for b in todo], dtype=np.int64)
+    gk, gv, ok, ov = _gather_bufs(pool_k, len(idx), O.row_bytes(c["type_k"], E),
+                                  O.row_bytes(c["type_v"], E))
+    for j, b in enumerate(idx):             # gather: [L, n, T, E] F16 (the slab copy)
+        gk[:, j] = pool_k[:, b]
+        gv[:, j] = pool_v[:, b]
+    O.quantize_rows_f16(c["type_k"], gk.reshape(-1, E), n_threads=q_threads, out=ok)
+    O.quantize_rows_f16(c["type_v"], gv.reshape(-1, E), n_threads=q_threads, out=ov)
     t3 = time.perf_counter()
     scale = len(staged) / max(1, len(todo))
     return dict(score=t1 - t0, plan=t2 - t1, stagein=(t3 - t2) * scale, n_staged=len(staged),
                 n_sampled=len(todo))
+
+
+_GATHER = {}
+
+
+def _gather_bufs(pool, n, rb_k, rb_v):
+    """Gather and output buffers for n blocks of every layer, allocated and
+    touched once per shape (like the reference's reused staging slab)."""
+    shape = (pool.shape[0], n) + pool.shape[2:]
+    key = (shape, rb_k, rb_v)
+    if _GATHER.get("key") != key:
+        rows = shape[0] * shape[1] * shape[2]
+        _GATHER["key"] = key
+        _GATHER["bufs"] = (np.zeros(shape, pool.dtype), np.zeros(shape, pool.dtype),
+                           np.zeros((rows, rb_k), np.uint8), np.zeros((rows, rb_v), np.uint8))
+    return _GATHER["bufs"]
+
+
+def cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks, sample_blocks=8):
+    """The same step on one host thread (the reference runs score_retrieval
+    and the quantizer on one thread): full score and select + diff, gather +
+    quantize of `sample_blocks` staged blocks scaled to all."""
+    r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, 1, ref, blocks,
+                 sample_blocks=sample_blocks, q_threads=1)
+    return {"cores": 1, "ms_per_step": round((r["score"] + r["plan"] + r["stagein"]) * 1e3, 2),
+            "stage_ms": {k: round(r[k] * 1e3, 2) for k in ("score", "plan", "stagein")},
+            "sample": f"score of every block, select+diff, gather+quantize of {r['n_sampled']} of "
+                      f"{r['n_staged']} staged blocks scaled to all; 1 thread"}
 
 
 def cpu_inputs(O, c, seed, pool_blocks=64, sums=None):
@@ -490,8 +542,21 @@ def cpu_inputs(O, c, seed, pool_blocks=64, sums=None):
     return sums, cnt, has, pool_k, pool_v
 
 
+def _ref_store(O, c):
+    if not O.have_ref():
+        return None
+    B, T = c["n_blocks"], c["block_tokens"]
+    ref = O.RefStore(block_tokens=T, select_budget=c["budget_tokens"],
+                     sink_blocks=c["sink_blocks"], recent_blocks=c["recent_blocks"])
+    ref.register_append(B * T)
+    for b in range(B):
+        ref.set_block_tier(b, O.TIER_CPU, -1, -1)
+    return ref
+
+
 def cpu_baseline(torch, c, hk, hv, qs, qc, sess, n_staged):
-    """Oracle port timed on this box's host cores (bounded sample of one step)."""
+    """Oracle port timed on this box's host cores (bounded sample of one
+    step), all cores and one thread."""
     import oracle as O
     O.build()
     L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
@@ -502,32 +567,30 @@ def cpu_baseline(torch, c, hk, hv, qs, qc, sess, n_staged):
     pool_v = hv[:, :64].cpu().numpy()
     q = qs[0].cpu().numpy()
     threads = host_cores()
-    ref = None
-    if O.have_ref():
-        ref = O.RefStore(block_tokens=T, select_budget=c["budget_tokens"],
-                         sink_blocks=c["sink_blocks"], recent_blocks=c["recent_blocks"])
-        ref.register_append(B * T)
-        for b in range(B):
-            ref.set_block_tier(b, O.TIER_CPU, -1, -1)
+    ref = _ref_store(O, c)
     blocks = O.Blocks.appended(B * T, T, tier=O.TIER_CPU)
     r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref, blocks,
-                 sample_blocks=32)
+                 sample_blocks=64)
     step_s = r["score"] + r["plan"] + r["stagein"]
     score_b, stage_b, _ = algo_bytes(c, r["n_staged"])
+    one = cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks)
     return {"value": round((score_b + stage_b) / step_s / 1e9, 3), "unit": "GB/s",
             "ms_per_step": round(step_s * 1e3, 2), "cores": threads, "kind": "port",
             "stage_ms": {k: round(r[k] * 1e3, 2) for k in ("score", "plan", "stagein")},
-            "sample": (f"one config-{'2' if L > 1 else '1'} step: score of all {B} blocks x {L} layer(s), "
-                       f"select+diff "
-                       f"({'reference libkvmem' if ref else 'oracle'}), gather+quantize of "
-                       f"{r['n_sampled']} of {r['n_staged']} staged blocks x {L} layer(s) x K,V "
-                       f"scaled to all; {threads} threads")}
+            "sample": (f"one config-{'2' if L > 1 else '1'} step: score of all {B} blocks x {L} layer(s) "
+                       f"on {threads} threads, select+diff "
+                       f"({'reference libkvmem' if ref else 'oracle'}, 1 thread), gather+quantize of "
+                       f"{r['n_sampled']} of {r['n_staged']} staged blocks x {L} layer(s) x K,V in one "
+                       f"call per K/V on {threads} threads, scaled to all"),
+            "single_thread": one}
 
 
 def run_reference(args):
     """--impl reference: the reference's CPU path (score_retrieval restated,
-    libkvmem select+diff compiled from the reference, CPU quantize) on all
-    host cores, same config/metric/unit; rank 0 only."""
+    libkvmem select+diff compiled from the reference, CPU quantize of every
+    staged block) on all host cores, same config/metric/unit and the
+    driver's --steps / --warmup; a one-thread step is timed beside it.  Rank
+    0 only."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -536,34 +599,27 @@ def run_reference(args):
     O.build()
     c = dict(CFG2)
     L, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
-    E = c["n_head_kv"] * c["head_dim"]
     sums, cnt, has, pool_k, pool_v = cpu_inputs(O, c, args.seed)
     threads = host_cores()
-    ref = None
-    if O.have_ref():
-        ref = O.RefStore(block_tokens=T, select_budget=c["budget_tokens"],
-                         sink_blocks=c["sink_blocks"], recent_blocks=c["recent_blocks"])
-        ref.register_append(B * T)
-        for b in range(B):
-            ref.set_block_tier(b, O.TIER_CPU, -1, -1)
+    ref = _ref_store(O, c)
     blocks = O.Blocks.appended(B * T, T, tier=O.TIER_CPU)
     rng = np.random.default_rng(args.seed + 3)
     qc = np.ones(L, np.uint32)
-    steps = max(1, min(args.steps, 10))
-    warm = max(0, min(args.warmup, 2))
     times, stages = [], []
-    for i in range(warm + steps):
+    q = None
+    for i in range(args.warmup + args.steps):
         q = O.synth_f16(rng, (L, c["n_head_q"] * c["head_dim"]), c["head_dim"]).astype(np.float32)
         r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref, blocks)
-        if i >= warm:
+        if i >= args.warmup:
             times.append(r["score"] + r["plan"] + r["stagein"])
             stages.append(r)
+    one = cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks)
     step_s = statistics.mean(times)
     score_b, stage_b, _ = algo_bytes(c, stages[0]["n_staged"])
     v = round((score_b + stage_b) / step_s / 1e9, 3)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
-        "steps": len(times), "warmup": warm, "ms_per_step": round(step_s * 1e3, 2),
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16->q8_0",
         "data": "synthetic: seeded N(0,1) F16 K/V, 1% outlier channels x20",
         "config": {"workload": "config 2 (see kvm arm), CPU path on host cores"},
@@ -571,10 +627,12 @@ def run_reference(args):
                      for k in ("score", "plan", "stagein")},
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads,
                          "kind": "reference" if ref else "port",
-                         "sample": ("full config-2 steps: restated score_retrieval, the "
-                                    "reference's own libkvmem pick_topk+set_selection, CPU "
-                                    "q8_0 quantization of all 256 staged blocks; F16 rows from a "
-                                    "64-block host pool")},
+                         "sample": ("full config-2 steps: restated score_retrieval on "
+                                    f"{threads} threads, the reference's own libkvmem "
+                                    "pick_topk+set_selection (1 thread), gather + CPU q8_0 "
+                                    f"quantization of all 256 staged blocks on {threads} threads; "
+                                    "F16 rows from a 64-block host pool per layer"),
+                         "single_thread": one},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -783,21 +841,18 @@ def run_incremental(args):
         dist.destroy_process_group()
 
 
-def run_multi_session(args):
+def config5_phase(args, torch, kvm, dist, world, rank, local, dev, steps, warmup):
     """Config 5: 64 independent sessions of 131072 tokens (1024 blocks x 16
-    layers, q8_0, budget 32768), split evenly over the GPUs; every session
+    layers, q8_0, budget 32768), split evenly over the ranks; every session
     steps on its own stream (cold window, new query per step).  The sessions of
-    a GPU read one shared seeded F16 history (8.6 GB) -- the traffic per
-    session is the same as with private histories, which would need 550 GB."""
-    import torch
-    import kvm
-    world, rank, local, dev, dist = _dist_init(torch)
+    a rank read one shared seeded F16 history (8.6 GB) -- the traffic per
+    session is the same as with private histories, which would need 550 GB.
+    Returns the same dict on every rank (times are the max over ranks)."""
     c = dict(CFG2)
     B, L, T = 1024, c["n_layer"], c["block_tokens"]
     c["n_blocks"] = B
     E = c["n_head_kv"] * c["head_dim"]
     n_sess = max(1, 64 // world)
-    steps = 5 if args.steps == 200 else args.steps
     seed = args.seed + 1000 * rank
     hk, hv = gen_history(torch, c, seed, dev)
     src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
@@ -809,7 +864,7 @@ def run_multi_session(args):
         sessions.append(s)
         streams.append(torch.cuda.Stream(device=dev))
         wins.append(_window(torch, c, s.n_slots, dev))
-        queries.append(gen_queries(torch, c, args.warmup + steps, seed + 7 * i, dev))
+        queries.append(gen_queries(torch, c, warmup + steps, seed + 7 * i, dev))
     qc = np.ones(L, np.uint32)
     main = torch.cuda.current_stream()
     torch.cuda.synchronize()
@@ -826,53 +881,198 @@ def run_multi_session(args):
             done.record(st)
             main.wait_event(done)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     n_staged = int(sessions[0].plan()["cold_block"].size)
     if dist:
         dist.barrier()
+    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = sum(s.kernel_launches for s in sessions)
     t0.record(main)
     for i in range(steps):
-        step(args.warmup + i)
+        step(warmup + i)
     t1.record(main)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     launches = sum(s.kernel_launches for s in sessions) - launches0
     ms = _max_over_ranks(torch, dist, dev, t0.elapsed_time(t1) / steps)
     score_b, stage_b, _ = algo_bytes(c, n_staged)
     total_sessions = n_sess * world
-    if rank == 0:
-        print(json.dumps({
-            "metric": METRIC,
-            "value": round(total_sessions * (score_b + stage_b) / (ms * 1e-3) / 1e9, 2),
-            "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16->q8_0",
-            "data": "synthetic; the sessions of a GPU share one seeded F16 history",
-            "config": {"workload": f"config 5: {total_sessions} sessions x 131072 tokens (1024 "
-                                   "blocks) x 16 layers, q8_0 K+V, budget 32768, cold window",
-                       "sessions_per_gpu": n_sess, "parallelism": f"sessions over {world} GPU(s)"},
-            "session_steps_per_s": round(total_sessions / (ms * 1e-3), 1),
-            "ms_per_session_step": round(ms / n_sess, 4),
-            "gpu_launches": int(launches)}), flush=True)
+    peak, peak_src = load_peak()
+    agg = total_sessions * (score_b + stage_b) / (ms * 1e-3) / 1e9
     for s in sessions:
         s.close()
+    del hk, hv, wins, queries
+    torch.cuda.empty_cache()
+    return {"workload": f"config 5: {total_sessions} sessions x 131072 tokens (1024 blocks) x 16 layers, "
+                        "q8_0 K+V, budget 32768, cold window, one stream per session",
+            "sessions_per_gpu": n_sess, "steps": steps, "warmup": warmup,
+            "ms_per_step_all_sessions": round(ms, 4),
+            "ms_per_session_step": round(ms / n_sess, 4),
+            "session_steps_per_s": round(total_sessions / (ms * 1e-3), 1),
+            "aggregate_gbs": round(agg, 1), "frac_of_n_peak": round(agg / (world * peak), 4),
+            "peak_source": peak_src, "scaling": "strong (64 sessions in total)",
+            "gpu_launches": int(launches)}
+
+
+def run_multi_session(args):
+    """--mode multi-session: config 5 alone, one JSON line."""
+    import torch
+    import kvm
+    world, rank, local, dev, dist = _dist_init(torch)
+    steps = 5 if args.steps == 200 else args.steps
+    r = config5_phase(args, torch, kvm, dist, world, rank, local, dev, steps, args.warmup)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": r["aggregate_gbs"], "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step_all_sessions"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16->q8_0",
+            "data": "synthetic; the sessions of a GPU share one seeded F16 history",
+            "config": {"workload": r["workload"], "sessions_per_gpu": r["sessions_per_gpu"],
+                       "parallelism": f"sessions over {world} GPU(s)"},
+            "session_steps_per_s": r["session_steps_per_s"],
+            "ms_per_session_step": r["ms_per_session_step"],
+            "gpu_launches": r["gpu_launches"]}), flush=True)
     if dist:
         dist.destroy_process_group()
 
 
-def run_layer_split(args):
+def layer_split_phase(args, torch, kvm, dist, world, rank, local, dev, steps, warmup,
+                      modes=("allgather", "allreduce"), parity=True):
     """One session of 1048576 tokens (8192 blocks) x 16 layers, layers split
     over the ranks; per step every rank scores its layers, the terms meet in
     one NCCL collective, every rank selects identically and stages in its own
-    layers (cold window, q8_0)."""
+    layers (cold window, q8_0).  Each combine mode in `modes` is timed.  With
+    `parity`, the combined scores and selected ids of each mode are then
+    checked on rank 0 against one kvm_score + kvm_select over all 16 layers of
+    the same summaries (gathered from the ranks into a full session)."""
+    from kvm.dist import LayerSplit, layer_split_scores
+    c = dict(CFG2)
+    c["n_blocks"] = 8192
+    L_all = c["n_layer"]
+    split0 = LayerSplit(L_all, rank, world)
+    c_loc = dict(c, n_layer=split0.n_local)
+    L, B, T = split0.n_local, c["n_blocks"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    hk, hv = gen_history(torch, c_loc, args.seed + 17 * split0.l0, dev)
+    sess = _make_session(kvm, c_loc, B, local)
+    stream = torch.cuda.current_stream()
+    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
+    sess.register_append(B * T)
+    sess.summarize(src)
+    wk, wv, kb, vb = _window(torch, c_loc, sess.n_slots, dev)
+    qs_all = gen_queries(torch, c, warmup + steps, args.seed, dev)      # all layers
+    qs = qs_all[:, split0.l0:split0.l1].contiguous()
+    qc = np.ones(L, np.uint32)
+    terms = torch.zeros((L, B), dtype=torch.float64, device=dev)
+    acc = torch.zeros(B, dtype=torch.float64, device=dev)
+    out = {"workload": "config 5 single session: 1048576 tokens (8192 blocks) x 16 layers, q8_0 K+V, "
+                       f"budget 32768, cold window, layers split over {world} GPU(s) "
+                       f"({split0.n_local} on rank 0)", "steps": steps, "warmup": warmup}
+    score_b, stage_b, _ = algo_bytes(c, 256)          # whole session, all 16 layers
+    for mode in modes:
+        split = LayerSplit(L_all, rank, world, mode)
+
+        def one_step(i):
+            sess.reset_window(stream)
+            sess.set_query(qs[i].data_ptr(), qc, stream)
+            layer_split_scores(sess, split, terms, acc, L_all, stream=stream)
+            sess.select(stream=stream)
+            sess.diff(stream=stream)
+            sess.stagein(src, kb, vb, stream=stream)
+
+        for i in range(warmup):
+            one_step(i)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = sess.kernel_launches
+        t0.record(stream)
+        for i in range(steps):
+            one_step(warmup + i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        ms = _max_over_ranks(torch, dist, dev, t0.elapsed_time(t1) / steps)
+        out[mode] = {"ms_per_step": round(ms, 4),
+                     "value_gbs": round((score_b + stage_b) / (ms * 1e-3) / 1e9, 1),
+                     "gpu_launches_per_step": round((sess.kernel_launches - launches0) / steps, 2)}
+    if parity:
+        out["parity"] = _layer_split_parity(torch, kvm, dist, world, rank, local, dev, sess, split0,
+                                            qs_all, qs, qc, terms, acc, c, modes)
+    sess.close()
+    del hk, hv, wk, wv
+    torch.cuda.empty_cache()
+    return out
+
+
+def _layer_split_parity(torch, kvm, dist, world, rank, local, dev, sess, split0, qs_all, qs, qc,
+                        terms, acc, c, modes):
+    """Scores and selected ids of the layer-split session (each combine mode)
+    against one full-session kvm_score + kvm_select on rank 0."""
+    from kvm.dist import LayerSplit, layer_split_scores
+    L_all, B, T = c["n_layer"], c["n_blocks"], c["block_tokens"]
+    E = c["n_head_kv"] * c["head_dim"]
+    stream = torch.cuda.current_stream()
+    got = {}
+    for mode in modes:
+        split = LayerSplit(L_all, rank, world, mode)
+        sess.set_query(qs[0].data_ptr(), qc, stream)
+        layer_split_scores(sess, split, terms, acc, L_all, stream=stream)
+        sess.select(stream=stream)
+        got[mode] = (sess.scores(), sess.plan()["selected"])
+    # every rank's summaries, in global layer order, on every rank
+    rows = max(split0.counts)
+    mine = torch.zeros((rows, B, E), dtype=torch.float32, device=dev)
+    for li in range(split0.n_local):
+        sess.download_summaries_to(li, mine[li], stream=stream)
+    if dist and world > 1:
+        allr = torch.empty((world * rows, B, E), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(allr, mine)
+        full = torch.cat([allr[r * rows:r * rows + n] for r, n in enumerate(split0.counts)])
+        del allr
+    else:
+        full = mine[:split0.n_local]
+    torch.cuda.synchronize()
+    res = {}
+    if rank == 0:
+        fs = _make_session(kvm, c, B, local)
+        fs.register_append(B * T)
+        cnt = torch.full((B,), T, dtype=torch.int32, device=dev)
+        for l in range(L_all):
+            fs.upload_summaries(l, 0, full[l], cnt, stream=stream)
+        fs.set_query(qs_all[0].data_ptr(), np.ones(L_all, np.uint32), stream)
+        fs.score(stream=stream)
+        fs.select(stream=stream)
+        ref_scores, ref_sel = fs.scores(), fs.plan()["selected"]
+        fs.close()
+        for mode, (sc, sel) in got.items():
+            rel = np.abs(sc - ref_scores) / np.maximum(np.abs(ref_scores), 1e-300)
+            res[mode] = {"scores_bitexact": bool(sc.tobytes() == ref_scores.tobytes()),
+                         "max_rel_diff": float(rel.max()) if rel.size else 0.0,
+                         "ids_equal": bool(np.array_equal(sel, ref_sel)),
+                         "n_selected": int(sel.size)}
+        res["reference"] = "one kvm_score + kvm_select over all 16 layers on rank 0"
+    del full, mine
+    torch.cuda.empty_cache()
+    if dist:
+        dist.barrier()
+    return res
+
+
+def run_layer_split(args):
+    """--mode layer-split: the layer-split session alone (one combine mode,
+    --combine), one JSON line; at world size 1 a gloo group stands in."""
     import datetime
     import torch
     import torch.distributed as dist
     import kvm
-    from kvm.dist import LayerSplit, layer_split_scores
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -883,76 +1083,19 @@ def run_layer_split(args):
                             rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=300),
                             **({"device_id": dev} if world > 1 else {}))
-    c = dict(CFG2)
-    c["n_blocks"] = 8192
-    L_all = c["n_layer"]
-    split = LayerSplit(L_all, rank, world, args.combine)
-    c_loc = dict(c)
-    c_loc["n_layer"] = split.n_local
-    L, B, T = split.n_local, c["n_blocks"], c["block_tokens"]
-    E = c["n_head_kv"] * c["head_dim"]
-    hk, hv = gen_history(torch, c_loc, args.seed + 17 * split.l0, dev)
-    cfg = kvm.default_config(block_tokens=T, select_budget=c["budget_tokens"],
-                             gen_reserve=c["gen_reserve"], sink_blocks=c["sink_blocks"],
-                             n_layer=L, n_head_kv=c["n_head_kv"], head_dim=c["head_dim"],
-                             n_head_q=c["n_head_q"], max_blocks=B, type_k=c["type_k"],
-                             type_v=c["type_v"])
-    sess = kvm.Session(cfg, local)
-    stream = torch.cuda.current_stream()
-    src = kvm.make_source(hk.data_ptr(), hv.data_ptr(), B * T * E * 2, T * E * 2, E * 2)
-    sess.register_append(B * T)
-    sess.summarize(src)
-    rbk, rbv = row_bytes(c["type_k"], E), row_bytes(c["type_v"], E)
-    win_k = torch.empty((L, sess.n_slots * T * rbk), dtype=torch.uint8, device=dev)
-    win_v = torch.empty((L, sess.n_slots * T * rbv), dtype=torch.uint8, device=dev)
-    kb = [win_k[l].data_ptr() for l in range(L)]
-    vb = [win_v[l].data_ptr() for l in range(L)]
-    qs_all = gen_queries(torch, c, args.warmup + args.steps, args.seed, dev)   # all layers
-    qs = qs_all[:, split.l0:split.l1].contiguous()
-    qc = np.ones(L, np.uint32)
-    terms = torch.zeros((L, B), dtype=torch.float64, device=dev)
-    acc = torch.zeros(B, dtype=torch.float64, device=dev)
-
-    def one_step(i):
-        sess.reset_window(stream)
-        sess.set_query(qs[i].data_ptr(), qc, stream)
-        layer_split_scores(sess, split, terms, acc, L_all, stream=stream)
-        sess.select(stream=stream)
-        sess.diff(stream=stream)
-        sess.stagein(src, kb, vb, stream=stream)
-
-    for i in range(args.warmup):
-        one_step(i)
-    torch.cuda.synchronize()
-    n_staged = int(sess.plan()["cold_block"].size)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = sess.kernel_launches
-    dist.barrier()
-    torch.cuda.synchronize()
-    t0.record(stream)
-    for i in range(args.steps):
-        one_step(args.warmup + i)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    ms = t0.elapsed_time(t1) / args.steps
-    t = torch.tensor([ms], dtype=torch.float64, device=dev if world > 1 else "cpu")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    score_b, stage_b, _ = algo_bytes(c, n_staged)     # whole session, all 16 layers
-    value = (score_b + stage_b) / (ms * 1e-3) / 1e9
+    r = layer_split_phase(args, torch, kvm, dist if world > 1 else None, world, rank, local, dev,
+                          args.steps, args.warmup, modes=(args.combine,), parity=world > 1)
     if rank == 0:
+        ms = r[args.combine]["ms_per_step"]
         print(json.dumps({
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "metric": METRIC, "value": r[args.combine]["value_gbs"], "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16->q8_0", "data": "synthetic (as the sessions mode)",
-            "config": {"workload": "config 5 single session: 1048576 tokens (8192 blocks) x 16 "
-                                   "layers, q8_0 K+V, budget 32768, cold window, layers split "
-                                   f"over {world} GPU(s), {args.combine} of per-layer terms",
+            "config": {"workload": r["workload"] + f", {args.combine} of per-layer terms",
                        "parallelism": f"layer split x{world}"},
-            "gpu_launches": int(sess.kernel_launches - launches0)}), flush=True)
-    sess.close()
+            "parity": r.get("parity"),
+            "gpu_launches_per_step": r[args.combine]["gpu_launches_per_step"]}), flush=True)
     dist.destroy_process_group()
 
 
@@ -1106,6 +1249,10 @@ def run_kernels(args):
 
 def main():
     args = parse()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # communicator set-up lines (rank count per communicator) in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     if args.mode == "layer-split":
         run_layer_split(args)
     elif args.mode == "incremental":

@@ -331,6 +331,15 @@ class Session:
         self.wait(stream=stream)
         return sums[:n], counts[:n]
 
+    def download_summaries_to(self, layer, d_sums, d_counts=None, block0=0, n=None, stream=None):
+        """Stream-ordered copy of one layer's sums ([n, E] f32) and counts to the
+        given device (or pinned) pointers; no host wait."""
+        n = self.block_count - block0 if n is None else n
+        self._check(lib().kvm_download_summaries(self.h, _stream(stream), layer, block0, n,
+                                                  _ptr(d_sums), _ptr(d_counts) if d_counts is not None
+                                                  else None),
+                    "download_summaries")
+
     def summarize(self, src: Source, layer0=0, n_layers=None, block0=0, n=None, stream=None):
         n_layers = self.cfg.n_layer if n_layers is None else n_layers
         n = self.block_count if n is None else n

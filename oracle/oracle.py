@@ -212,11 +212,15 @@ def quantize(type_: int, x: np.ndarray) -> np.ndarray:
     return out
 
 
-def quantize_rows_f16(type_: int, rows: np.ndarray, n_threads: int = 1) -> np.ndarray:
-    """F16 rows [n, E] (as float16 or uint16) -> quantized bytes [n, row_bytes]."""
+def quantize_rows_f16(type_: int, rows: np.ndarray, n_threads: int = 1, out=None) -> np.ndarray:
+    """F16 rows [n, E] (as float16 or uint16) -> quantized bytes [n, row_bytes]
+    (into `out` when given: a C-contiguous uint8 array of that shape)."""
     r = np.ascontiguousarray(rows).view(np.uint16)
     n, e = r.shape
-    out = np.empty((n, row_bytes(type_, e)), dtype=np.uint8)
+    if out is None:
+        out = np.empty((n, row_bytes(type_, e)), dtype=np.uint8)
+    elif out.shape != (n, row_bytes(type_, e)) or out.dtype != np.uint8 or not out.flags.c_contiguous:
+        raise ValueError("out must be C-contiguous uint8 [n, row_bytes]")
     rc = lib().ora_quantize_rows_f16(type_, r, n, e, out, n_threads)
     if rc != 0:
         raise ValueError("unsupported type or width")
