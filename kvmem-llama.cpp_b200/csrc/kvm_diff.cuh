@@ -34,10 +34,35 @@ namespace kvm {
 // already set now[i] != 0 exactly for the selected blocks.  With
 // a.reset_window the block table is first reset as kvm_reset_window does
 // (nothing in the working set, GPU-tier blocks drop to the CPU tier, no
-// slots), in the same pass that reads it.
+// slots): the reset is applied to the values as they are read and written
+// back with the new layout.
+//
+// Three phases.  A: every thread reads its block chunk and its selection
+// chunk and counts (stage_out, overlap | tokens, stage_in, moves, cold); one
+// block-wide scan of the six counts gives every list offset.  B: the lists,
+// the remaps and the working-set / bake updates, with the remaining four
+// counters summed in shared memory.  C: the new layout (tier and slot of
+// every block) and the plan header.
+struct DiffView {                  // a block's table entry as the diff sees it
+    uint8_t in_ws;
+    uint8_t tier;
+    int32_t slot;
+};
+
+__device__ __forceinline__ DiffView diff_view(const BlockTable &bt, uint32_t id, bool reset) {
+    DiffView v{bt.in_ws[id], bt.tier[id], bt.gpu_slot[id]};
+    if (reset) {
+        v.in_ws = 0;
+        if (v.tier == KVM_TIER_GPU) v.tier = KVM_TIER_CPU;
+        v.slot = -1;
+    }
+    return v;
+}
+
 static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, uint8_t *was,
                                  bool now_ready) {
-    __shared__ uint4 scratch4[kDiffThreads / 32 + 1];
+    __shared__ uint4 scratch8[2 * (kDiffThreads / 32 + 1)];
+    __shared__ uint32_t s_cnt[4];      // stable, moved, reused, errors
     const uint32_t n = a.n_blocks;
     PlanHeader *hdr = a.plan.hdr;
     const uint32_t tid = threadIdx.x;
@@ -57,73 +82,61 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
         }
         __syncthreads();
     }
+    if (tid < 4) s_cnt[tid] = 0u;
 
-    // ---- pass over every block: overlap, stage_out
+    // ---- A: counts over this thread's block chunk and selection chunk
     const uint32_t per = (n + kDiffThreads - 1u) / kDiffThreads;
     const uint32_t lo = min(n, tid * per);
     const uint32_t hi = min(n, lo + per);
-    uint32_t overlap = 0, n_out = 0;
-    for (uint32_t i = lo; i < hi; ++i) {
-        uint8_t w = bt.in_ws[i];
-        uint8_t t = bt.tier[i];
-        if (reset) {
-            if (w) bt.in_ws[i] = 0;
-            w = 0;
-            if (t == KVM_TIER_GPU) {
-                t = KVM_TIER_CPU;
-                bt.tier[i] = t;
-            }
-            bt.gpu_slot[i] = -1;
-        }
-        was[i] = w;
-        overlap += (w && now[i]) ? 1u : 0u;
-        n_out += (t == KVM_TIER_GPU && (!now[i] || ffr)) ? 1u : 0u;
-    }
-    uint4 tot1;
-    const uint4 off1 = block_exclusive_scan4<kDiffThreads>(make_uint4(n_out, overlap, 0u, 0u), scratch4, &tot1);
-    uint32_t off_out = off1.x;
-    const uint32_t tot_out = tot1.x;
-    const uint32_t tot_overlap = tot1.y;
-    for (uint32_t i = lo; i < hi; ++i) {
-        if (bt.tier[i] == KVM_TIER_GPU && (!now[i] || ffr)) {
-            a.plan.stage_out[off_out++] = i;
-            bt.in_ws[i] = 0;
-        }
-    }
-    __syncthreads();
-
-    // ---- pass over the selection: window positions, stage_in, remaps, layout
     const uint32_t sper = (k + kDiffThreads - 1u) / kDiffThreads;
     const uint32_t slo = min(k, tid * sper);
     const uint32_t shi = min(k, slo + sper);
+    uint32_t overlap = 0, n_out = 0;
+    for (uint32_t i = lo; i < hi; ++i) {
+        const DiffView v = diff_view(bt, i, reset);
+        was[i] = v.in_ws;
+        overlap += (v.in_ws && now[i]) ? 1u : 0u;
+        n_out += (v.tier == KVM_TIER_GPU && (!now[i] || ffr)) ? 1u : 0u;
+    }
     uint32_t tok = 0, n_in = 0, n_mv = 0, n_cold = 0;
     for (uint32_t s = slo; s < shi; ++s) {
         const uint32_t id = sel[s];
+        const DiffView v = diff_view(bt, id, reset);
+        // a selected GPU block also leaves the working set when every GPU
+        // block is staged out (optimize_stage_in off)
+        const bool ws = v.in_ws && !(ffr && v.tier == KVM_TIER_GPU);
         tok += bt.n_tokens[id];
-        n_in += bt.in_ws[id] ? 0u : 1u;
-        const bool resident = !ffr && bt.tier[id] == KVM_TIER_GPU && bt.gpu_slot[id] >= 0;
-        if (resident) n_mv += bt.gpu_slot[id] != static_cast<int32_t>(s) ? 1u : 0u;
+        n_in += ws ? 0u : 1u;
+        const bool resident = !ffr && v.tier == KVM_TIER_GPU && v.slot >= 0;
+        if (resident) n_mv += v.slot != static_cast<int32_t>(s) ? 1u : 0u;
         else ++n_cold;
     }
-    uint4 tot2;
-    const uint4 off2 = block_exclusive_scan4<kDiffThreads>(make_uint4(tok, n_in, n_mv, n_cold), scratch4, &tot2);
-    uint32_t wpos = off2.x, off_in = off2.y, off_mv = off2.z, off_cold = off2.w;
-    const uint32_t tot_tok = tot2.x, tot_in = tot2.y, tot_mv = tot2.z, tot_cold = tot2.w;
+    uint4 c1 = make_uint4(n_out, overlap, tok, n_in), c2 = make_uint4(n_mv, n_cold, 0u, 0u);
+    uint4 t1, t2;
+    block_exclusive_scan8<kDiffThreads>(c1, c2, scratch8, &t1, &t2);   // was[] visible after it
+
+    // ---- B: lists, remaps, working-set and bake updates
+    uint32_t off_out = c1.x;
+    for (uint32_t i = lo; i < hi; ++i) {
+        const uint8_t t = bt.tier[i];
+        if (t == KVM_TIER_GPU && !reset && (!now[i] || ffr)) a.plan.stage_out[off_out++] = i;
+    }
+    uint32_t wpos = c1.z, off_in = c1.w, off_mv = c2.x, off_cold = c2.y;
     uint32_t stable = 0, moved = 0, reused = 0, err = 0;
     for (uint32_t s = slo; s < shi; ++s) {
         const uint32_t id = sel[s];
-        const uint8_t tier = bt.tier[id];
-        const int32_t slot_before = bt.gpu_slot[id];
+        const DiffView v = diff_view(bt, id, reset);
         const int64_t baked = bt.baked_pos[id];
         const uint32_t ntok = bt.n_tokens[id];
-        const bool reusable = was[id] && tier == KVM_TIER_GPU;
+        const bool reusable = was[id] && v.tier == KVM_TIER_GPU;
         if (reusable) {
             if (baked == static_cast<int64_t>(wpos)) ++stable;
             else ++moved;
             if (!ffr) ++reused;
         }
-        const bool cold = tier != KVM_TIER_GPU || ffr;
-        if (!bt.in_ws[id]) a.plan.stage_in[off_in++] = id;
+        const bool cold = v.tier != KVM_TIER_GPU || ffr;
+        const bool ws = v.in_ws && !(ffr && v.tier == KVM_TIER_GPU);
+        if (!ws) a.plan.stage_in[off_in++] = id;
         const bool wkr = !cold;
         const bool same = baked == static_cast<int64_t>(wpos);
         const bool skip = same && (!imm || wkr) && !a.force_raw_refresh;
@@ -151,11 +164,11 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
         a.plan.rm_skip[s] = skip ? 1 : 0;
         a.plan.rm_raw[s] = raw ? 1 : 0;
         // layout
-        const bool resident = !ffr && tier == KVM_TIER_GPU && slot_before >= 0;
+        const bool resident = !ffr && v.tier == KVM_TIER_GPU && v.slot >= 0;
         if (resident) {
-            if (slot_before != static_cast<int32_t>(s)) {
+            if (v.slot != static_cast<int32_t>(s)) {
                 a.plan.mv_block[off_mv] = id;
-                a.plan.mv_from[off_mv] = slot_before;
+                a.plan.mv_from[off_mv] = v.slot;
                 a.plan.mv_to[off_mv] = static_cast<int32_t>(s);
                 ++off_mv;
             }
@@ -179,13 +192,29 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
         bt.baked_pos[id] = static_cast<int64_t>(wpos);
         wpos += ntok;
     }
-    uint4 tot3;
-    (void)block_exclusive_scan4<kDiffThreads>(make_uint4(stable, moved, reused, err), scratch4, &tot3);
-    const uint32_t tot_stable = tot3.x, tot_moved = tot3.y, tot_reused = tot3.z, tot_err = tot3.w;
-    // every selected block's old slot was read above; now install the layout
+    // the four counters: warp sums, one shared atomic each per warp
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        stable += __shfl_xor_sync(0xffffffffu, stable, o);
+        moved += __shfl_xor_sync(0xffffffffu, moved, o);
+        reused += __shfl_xor_sync(0xffffffffu, reused, o);
+        err += __shfl_xor_sync(0xffffffffu, err, o);
+    }
+    if ((tid & 31u) == 0u && (stable | moved | reused | err)) {
+        atomicAdd(&s_cnt[0], stable);
+        atomicAdd(&s_cnt[1], moved);
+        atomicAdd(&s_cnt[2], reused);
+        atomicAdd(&s_cnt[3], err);
+    }
+    __syncthreads();   // every entry was read above; now install the layout
+
+    // ---- C: the layout and the header
     for (uint32_t i = lo; i < hi; ++i) {
         if (now[i]) continue;
-        if (bt.tier[i] == KVM_TIER_GPU) bt.tier[i] = KVM_TIER_CPU;
+        // unselected GPU blocks are staged out (or dropped by the reset)
+        const bool gpu = bt.tier[i] == KVM_TIER_GPU;
+        if (reset || gpu) bt.in_ws[i] = 0;
+        if (gpu) bt.tier[i] = KVM_TIER_CPU;
         bt.gpu_slot[i] = -1;
     }
     for (uint32_t s = slo; s < shi; ++s) {
@@ -194,19 +223,19 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
         bt.gpu_slot[id] = static_cast<int32_t>(s);
     }
     if (tid == 0) {
-        hdr->n_stage_in = tot_in;
-        hdr->n_stage_out = tot_out;
+        hdr->n_stage_in = t1.w;
+        hdr->n_stage_out = t1.x;
         hdr->n_remaps = k;
-        hdr->total_window_tokens = tot_tok;
-        hdr->selection_overlap_blocks = tot_overlap;
-        hdr->gpu_reused_blocks = tot_reused;
-        hdr->retained_position_stable = tot_stable;
-        hdr->retained_position_moved = tot_moved;
-        hdr->n_moves = tot_mv;
-        hdr->n_cold = tot_cold;
+        hdr->total_window_tokens = t1.z;
+        hdr->selection_overlap_blocks = t1.y;
+        hdr->gpu_reused_blocks = s_cnt[2];
+        hdr->retained_position_stable = s_cnt[0];
+        hdr->retained_position_moved = s_cnt[1];
+        hdr->n_moves = t2.x;
+        hdr->n_cold = t2.y;
         hdr->n_blocks = n;
-        if (tot_err & 0xffffu) set_status(a.status, kErrConfig);
-        if (tot_err >> 16) set_status(a.status, kErrSlot);
+        if (s_cnt[3] & 0xffffu) set_status(a.status, kErrConfig);
+        if (s_cnt[3] >> 16) set_status(a.status, kErrSlot);
     }
 }
 

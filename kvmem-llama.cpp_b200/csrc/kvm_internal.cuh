@@ -266,6 +266,62 @@ __device__ __forceinline__ uint4 block_exclusive_scan4(uint4 v, uint4 *scratch, 
     return make_uint4(wp.x + x.x - v.x, wp.y + x.y - v.y, wp.z + x.z - v.z, wp.w + x.w - v.w);
 }
 
+// Eight independent exclusive prefix sums (two uint4) in one pass, same
+// contract as block_exclusive_scan4; `scratch` holds >= 2 * (NT/32 + 1) uint4.
+template <int NT>
+__device__ __forceinline__ void block_exclusive_scan8(uint4 &a, uint4 &b, uint4 *scratch, uint4 *tot_a,
+                                                      uint4 *tot_b) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    constexpr int NW = NT / 32;
+    uint4 xa = a, xb = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint4 ya = u4_shfl_up(xa, o);
+        const uint4 yb = u4_shfl_up(xb, o);
+        if (lane >= o) {
+            xa = u4_add(xa, ya);
+            xb = u4_add(xb, yb);
+        }
+    }
+    if (lane == 31) {
+        scratch[warp] = xa;
+        scratch[NW + 1 + warp] = xb;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        uint4 wa = lane < NW ? scratch[lane] : z;
+        uint4 wb = lane < NW ? scratch[NW + 1 + lane] : z;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint4 ya = u4_shfl_up(wa, o);
+            const uint4 yb = u4_shfl_up(wb, o);
+            if (lane >= o) {
+                wa = u4_add(wa, ya);
+                wb = u4_add(wb, yb);
+            }
+        }
+        if (lane < NW) {
+            scratch[lane] = wa;
+            scratch[NW + 1 + lane] = wb;
+        }
+        if (lane == NW - 1) {
+            scratch[NW] = wa;
+            scratch[2 * NW + 1] = wb;
+        }
+    }
+    __syncthreads();
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    const uint4 pa = warp > 0 ? scratch[warp - 1] : z;
+    const uint4 pb = warp > 0 ? scratch[NW + warp] : z;
+    *tot_a = scratch[NW];
+    *tot_b = scratch[2 * NW + 1];
+    __syncthreads();
+    a = make_uint4(pa.x + xa.x - a.x, pa.y + xa.y - a.y, pa.z + xa.z - a.z, pa.w + xa.w - a.w);
+    b = make_uint4(pb.x + xb.x - b.x, pb.y + xb.y - b.y, pb.z + xb.z - b.z, pb.w + xb.w - b.w);
+}
+
 // Block-wide sum of one value per thread (all threads get the result).
 template <int NT>
 __device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t *scratch) {

@@ -50,17 +50,29 @@ __device__ uint32_t compact_flags(const uint8_t *flags, uint32_t n, uint32_t *ou
 // The selection into kept[] (n bytes of shared memory: nonzero = selected)
 // and a.selected (ascending); returns the selected count to every thread.
 // Called by every thread of a kSelectThreads CTA.
+//
+// The radix select starts at the highest bit in which the smallest and the
+// largest candidate key differ (the bits above it are common to every
+// candidate), then resolves 8 bits a pass.  Histogram counts are aggregated
+// per warp (__match_any_sync: early passes put most keys in one bin), and
+// the histogram is double-buffered so a pass needs two barriers.  The taken
+// candidates and the ascending compaction come out of one block scan: the
+// candidates equal to the threshold key that are taken are the `rem` with the
+// highest ids, i.e. the equal ones after the first (equal total - rem).
 static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
-    __shared__ uint32_t scratch[40];
-    __shared__ uint32_t hist[256];
+    __shared__ uint4 scratch4[kSelectThreads / 32 + 1];
+    __shared__ uint32_t hist[2][256];
+    __shared__ uint64_t s_wmin[kSelectThreads / 32];
+    __shared__ uint64_t s_wmax[kSelectThreads / 32];
     __shared__ uint32_t s_kc;
     __shared__ uint32_t s_remaining;
     __shared__ uint64_t s_prefix;
     __shared__ uint64_t s_mask;
-    __shared__ uint32_t s_done;
+    __shared__ int32_t s_hi;           // highest unresolved key bit, -1 when none
     const uint32_t n = a.n_blocks;
     const uint32_t budget = a.budget;
     const uint32_t tid = threadIdx.x;
+    const uint32_t lane = tid & 31u;
     if (n == 0) {
         if (tid == 0) a.hdr->n_selected = 0;
         return 0u;
@@ -75,6 +87,7 @@ static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
         return n;
     }
     for (uint32_t i = tid; i < n; i += kSelectThreads) kept[i] = 0;
+    for (uint32_t i = tid; i < 512u; i += kSelectThreads) (&hist[0][0])[i] = 0u;
     __syncthreads();
     if (tid == 0) {
         uint32_t kc = 0;
@@ -96,66 +109,106 @@ static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
     const uint32_t kc = s_kc;
     const uint32_t need = budget - kc;
     const uint32_t n_cand = n - kc;
-    if (need > 0 && need >= n_cand) {
-        for (uint32_t i = tid; i < n; i += kSelectThreads)
-            if (!kept[i]) kept[i] = 2;
-        __syncthreads();
-    } else if (need > 0) {
-        // Each thread owns the contiguous ids [lo, hi); up to kKeysCached keys
-        // stay in registers across the passes.
-        constexpr uint32_t kKeysCached = 8;
-        const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
-        const uint32_t lo = min(n, tid * per);
-        const uint32_t hi = min(n, lo + per);
-        const bool cached = per <= kKeysCached;
-        uint64_t kc[kKeysCached];
-        uint32_t live = 0;                        // bit j: id lo + j is a candidate
+    const bool take_all = need > 0 && need >= n_cand;
+    const bool radix = need > 0 && !take_all;
+    // Each thread owns the contiguous ids [lo, hi); up to kKeysCached keys
+    // stay in registers across the passes.
+    constexpr uint32_t kKeysCached = 8;
+    const uint32_t per = (n + kSelectThreads - 1u) / kSelectThreads;
+    const uint32_t lo = min(n, tid * per);
+    const uint32_t hi = min(n, lo + per);
+    const bool cached = per <= kKeysCached;
+    uint64_t kcache[kKeysCached];
+    uint32_t live = 0;                        // bit j: id lo + j is a candidate
 #pragma unroll
-        for (uint32_t j = 0; j < kKeysCached; ++j) {
-            kc[j] = 0ull;
-            if (cached && lo + j < hi && !kept[lo + j]) {
-                kc[j] = score_key(a.scores[lo + j]);
-                live |= 1u << j;
+    for (uint32_t j = 0; j < kKeysCached; ++j) {
+        kcache[j] = 0ull;
+        if (radix && cached && lo + j < hi && !kept[lo + j]) {
+            kcache[j] = score_key(a.scores[lo + j]);
+            live |= 1u << j;
+        }
+    }
+    // f(j, live, key) for every owned slot j < per: a count uniform over the
+    // CTA (warp-wide intrinsics in f see every lane); live is false past hi.
+    // Cached keys are indexed with compile-time j (registers, no select chain).
+    auto for_keys = [&](auto &&f) {
+        if (cached) {
+#pragma unroll
+            for (uint32_t j = 0; j < kKeysCached; ++j)
+                if (j < per) f(j, ((live >> j) & 1u) != 0u, kcache[j]);
+        } else {
+            for (uint32_t j = 0; j < per; ++j) {
+                const bool lv = radix && lo + j < hi && !kept[lo + j];
+                f(j, lv, lv ? score_key(a.scores[lo + j]) : 0ull);
             }
         }
-        auto key_of = [&](uint32_t j) -> uint64_t {
-            if (cached) {
-                uint64_t k = 0ull;
+    };
+    uint64_t thr = 0ull, msk = 0ull;
+    uint32_t rem = 0;
+    if (radix) {
+        // smallest and largest candidate key: their common leading bits are
+        // every candidate's
+        uint64_t kmin = ~0ull, kmax = 0ull;
+        for_keys([&](uint32_t, bool lv, uint64_t k) {
+            if (!lv) return;
+            kmin = k < kmin ? k : kmin;
+            kmax = k > kmax ? k : kmax;
+        });
 #pragma unroll
-                for (uint32_t q = 0; q < kKeysCached; ++q)
-                    if (q == j) k = kc[q];
-                return k;
-            }
-            return score_key(a.scores[lo + j]);
-        };
-        auto is_live = [&](uint32_t j) -> bool {
-            return cached ? ((live >> j) & 1u) != 0u : !kept[lo + j];
-        };
-        if (tid == 0) {
-            s_prefix = 0ull;
-            s_mask = 0ull;
-            s_remaining = need;
-            s_done = 0u;
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t a1 = __shfl_xor_sync(0xffffffffu, kmin, o);
+            const uint64_t b1 = __shfl_xor_sync(0xffffffffu, kmax, o);
+            kmin = a1 < kmin ? a1 : kmin;
+            kmax = b1 > kmax ? b1 : kmax;
+        }
+        if (lane == 0) {
+            s_wmin[tid >> 5] = kmin;
+            s_wmax[tid >> 5] = kmax;
         }
         __syncthreads();
-        for (int pass = 0; pass < 8 && !s_done; ++pass) {
-            const int shift = 56 - 8 * pass;
-            for (uint32_t i = tid; i < 256u; i += kSelectThreads) hist[i] = 0u;
-            __syncthreads();
+        if (tid < 32) {
+            uint64_t m0 = lane < kSelectThreads / 32 ? s_wmin[lane] : ~0ull;
+            uint64_t m1 = lane < kSelectThreads / 32 ? s_wmax[lane] : 0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t a1 = __shfl_xor_sync(0xffffffffu, m0, o);
+                const uint64_t b1 = __shfl_xor_sync(0xffffffffu, m1, o);
+                m0 = a1 < m0 ? a1 : m0;
+                m1 = b1 > m1 ? b1 : m1;
+            }
+            if (lane == 0) {
+                const uint64_t x = m0 ^ m1;
+                const int hb = x ? 63 - __clzll(static_cast<long long>(x)) : -1;
+                const uint64_t common = hb < 0 ? ~0ull : (hb == 63 ? 0ull : ~((2ull << hb) - 1ull));
+                s_prefix = m0 & common;
+                s_mask = common;
+                s_hi = hb;
+                s_remaining = need;
+            }
+        }
+        __syncthreads();
+        for (uint32_t pass = 0; s_hi >= 0; ++pass) {
+            const int hib = s_hi;
+            const int lob = hib >= 7 ? hib - 7 : 0;
+            const uint32_t dmask = (1u << (hib - lob + 1)) - 1u;
             const uint64_t prefix = s_prefix;
             const uint64_t mask = s_mask;
-            for (uint32_t j = 0; j < hi - lo; ++j) {
-                if (!is_live(j)) continue;
-                const uint64_t k = key_of(j);
-                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
-            }
+            uint32_t *H = hist[pass & 1u];
+            for_keys([&](uint32_t, bool lv, uint64_t k) {
+                const uint32_t d = (lv && (k & mask) == prefix) ? static_cast<uint32_t>(k >> lob) & dmask
+                                                                : 0xffffffffu;
+                const uint32_t peers = __match_any_sync(0xffffffffu, d);
+                if (d != 0xffffffffu && lane == static_cast<uint32_t>(__ffs(peers) - 1))
+                    atomicAdd(&H[d], static_cast<uint32_t>(__popc(peers)));
+            });
+            uint32_t *Hn = hist[(pass + 1u) & 1u];
+            for (uint32_t i = tid; i < 256u; i += kSelectThreads) Hn[i] = 0u;
             __syncthreads();
             if (tid < 32) {
                 // lane l owns bins 255-8l .. 248-8l (highest digits first)
-                const uint32_t lane = tid;
-                const uint32_t rem = s_remaining;   // read before any lane writes it
+                const uint32_t r0 = s_remaining;   // read before any lane writes it
                 uint32_t local = 0;
-                for (int j = 0; j < 8; ++j) local += hist[255u - 8u * lane - j];
+                for (int q = 0; q < 8; ++q) local += H[255u - 8u * lane - q];
                 uint32_t cum = local;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
@@ -163,19 +216,18 @@ static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
                     if (lane >= static_cast<uint32_t>(o)) cum += y;
                 }
                 const uint32_t ex = cum - local;
-                const bool hit = ex < rem && rem <= cum;
-                if (hit) {
+                if (ex < r0 && r0 <= cum) {
                     uint32_t acc = ex;
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t bin = 255u - 8u * lane - j;
-                        const uint32_t hc = hist[bin];
-                        if (acc + hc >= rem) {
-                            s_remaining = rem - acc;
-                            s_prefix = prefix | (static_cast<uint64_t>(bin) << shift);
-                            s_mask = mask | (255ull << shift);
+                    for (int q = 0; q < 8; ++q) {
+                        const uint32_t bin = 255u - 8u * lane - q;
+                        const uint32_t hc = H[bin];
+                        if (acc + hc >= r0) {
+                            s_remaining = r0 - acc;
+                            s_prefix = prefix | (static_cast<uint64_t>(bin) << lob);
+                            s_mask = mask | (static_cast<uint64_t>(dmask) << lob);
                             // the whole bin is needed: every candidate with this
                             // prefix is taken, no further digit matters
-                            if (acc + hc == rem) s_done = 1u;
+                            s_hi = (acc + hc == r0) ? -1 : lob - 1;
                             break;
                         }
                         acc += hc;
@@ -184,31 +236,43 @@ static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
             }
             __syncthreads();
         }
-        // take every candidate above the threshold prefix, and the `rem`
-        // highest-id candidates equal to it
-        const uint64_t thr = s_prefix;
-        const uint64_t msk = s_mask;
-        const uint32_t rem = s_remaining;
-        uint32_t eq = 0;
-        for (uint32_t j = 0; j < hi - lo; ++j)
-            if (is_live(j) && (key_of(j) & msk) == thr) ++eq;
-        uint32_t total_eq;
-        const uint32_t before = block_exclusive_scan<kSelectThreads>(eq, scratch, &total_eq);
-        uint32_t seen = before;   // equal candidates with id < i, running
-        for (uint32_t j = 0; j < hi - lo; ++j) {
-            if (!is_live(j)) continue;
-            const uint64_t k = key_of(j) & msk;
-            if (k > thr) {
-                kept[lo + j] = 2;
-            } else if (k == thr) {
-                ++seen;
-                const uint32_t above = total_eq - seen;   // equal candidates with id > i
-                if (above < rem) kept[lo + j] = 2;
-            }
-        }
-        __syncthreads();
+        thr = s_prefix;
+        msk = s_mask;
+        rem = s_remaining;
     }
-    const uint32_t m = compact_flags(kept, n, a.selected, scratch);
+    // pins, candidates above the threshold, and the `rem` highest-id
+    // candidates equal to it; one scan gives every offset of the ascending list
+    uint32_t above = 0, eq = 0;
+    for_keys([&](uint32_t j, bool lv, uint64_t k) {
+        if (lo + j >= hi) return;
+        if (kept[lo + j] || take_all) {
+            ++above;
+        } else if (lv) {
+            k &= msk;
+            if (k > thr) ++above;
+            else if (k == thr) ++eq;
+        }
+    });
+    uint4 tot;
+    const uint4 off = block_exclusive_scan4<kSelectThreads>(make_uint4(above, eq, 0u, 0u), scratch4, &tot);
+    const uint32_t e0 = tot.y > rem ? tot.y - rem : 0u;    // equal candidates not taken (lowest ids)
+    uint32_t seen = off.y;
+    uint32_t o = off.x + (off.y > e0 ? off.y - e0 : 0u);
+    for_keys([&](uint32_t j, bool lv, uint64_t k) {
+        const uint32_t i = lo + j;
+        if (i >= hi) return;
+        bool take = kept[i] != 0 || take_all;
+        if (!take && lv) {
+            k &= msk;
+            if (k > thr) take = true;
+            else if (k == thr) take = seen++ >= e0;
+        }
+        if (take) {
+            if (!kept[i]) kept[i] = 2;
+            a.selected[o++] = i;
+        }
+    });
+    const uint32_t m = tot.x + (tot.y > e0 ? tot.y - e0 : 0u);
     if (tid == 0) a.hdr->n_selected = m;
     __syncthreads();
     return m;
@@ -223,9 +287,29 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectArgs a) {
 // shared memory as the diff's block flags, and the selected list is read
 // back from the plan (written by this CTA, visible after the barrier).
 static_assert(kSelectThreads == kDiffThreads, "one CTA runs both");
+
+// L2 prefetch of [p, p + bytes), one 128-byte line a thread a round.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(127);
+    const uintptr_t b1 = reinterpret_cast<uintptr_t>(p) + bytes;
+    for (uintptr_t a = b0 + 128u * threadIdx.x; a < b1; a += 128u * blockDim.x)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+
 __global__ void __launch_bounds__(kSelectThreads) select_diff_kernel(SelectArgs sa, DiffArgs da) {
     extern __shared__ uint8_t fl[];
     const uint32_t n = sa.n_blocks;
+    // the scores and the block table were usually evicted from L2 by the
+    // previous stage-in: start fetching all of them now, so the dependent
+    // reads of the selection and the diff phases hit L2
+    prefetch_l2(sa.scores, sizeof(double) * n);
+    prefetch_l2(da.bt.in_ws, n);
+    prefetch_l2(da.bt.tier, n);
+    prefetch_l2(da.bt.gpu_slot, sizeof(int32_t) * n);
+    prefetch_l2(da.bt.n_tokens, sizeof(uint32_t) * n);
+    prefetch_l2(da.bt.baked_pos, sizeof(int64_t) * n);
+    prefetch_l2(da.bt.remap_count, sizeof(uint32_t) * n);
+    prefetch_l2(da.bt.remap_abs_delta, sizeof(uint64_t) * n);
     uint8_t *kept = fl;
     uint8_t *was = fl + (n ? n : 1u);
     const uint32_t m = select_core(sa, kept);
