@@ -113,6 +113,27 @@ __host__ __device__ inline uint32_t stagein_theta_bytes(const StageinArgs &a) {
     return (a.xform && a.rope_n_rot) ? ((a.rope_n_rot / 2u) * 4u + 127u) & ~127u : 0u;
 }
 
+// RoPE angle table of one consumer warp (transform mode with RoPE): the
+// (cos, sin) of every (row, frequency) its warp-iteration needs -- the rows
+// of its (row, head) units x rope_n_rot / 2 frequencies -- each computed once
+// and read by the lanes of every head and of both rotation halves.  Row r,
+// frequency i at float2 index r * stride + i + 2 * (i / 32): 16 bytes of
+// padding per 32 entries keep the four 256-byte lane segments of one read on
+// different banks.
+__host__ __device__ inline uint32_t rope_tab_rows(const StageinArgs &a) {
+    const uint32_t per_warp = 32u / (a.xform ? a.xform : 1u);
+    const uint32_t h = a.xf_heads ? a.xf_heads : 1u;
+    const uint32_t r = (per_warp - 1u) / h + 2u;        // rows a warp-iteration can touch
+    return r < per_warp ? r : per_warp;
+}
+__host__ __device__ inline uint32_t rope_tab_stride(const StageinArgs &a) {   // float2 entries a row
+    const uint32_t half = a.rope_n_rot / 2u;
+    return half + 2u * (half / 32u);
+}
+__host__ __device__ inline uint32_t rope_tab_warp_bytes(const StageinArgs &a) {
+    return (a.xform && a.rope_n_rot) ? ((rope_tab_rows(a) * rope_tab_stride(a) * 8u + 127u) & ~127u) : 0u;
+}
+
 // Pipeline depth: transform tiles are ALU-heavier, so their loads run further
 // ahead -- except with RoPE, whose sincosf wants the L1 that a deeper
 // pipeline's shared memory would take.
@@ -342,7 +363,7 @@ __device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, ui
 template <int CW>
 __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
                                                uint8_t *ob, int warp, int lane, uint32_t sub, uint32_t j,
-                                               uint32_t per_warp, const float *theta_s) {
+                                               uint32_t per_warp, const float *theta_s, float2 *tab) {
     const bool is_v = (ts.meta >> 31) != 0u;
     const uint32_t pos0 = ts.meta & 0x7fffffffu;
     const uint32_t nrot = is_v ? a.rot_v : a.rot_k;
@@ -356,12 +377,29 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
     const float pre = is_v ? a.xf_pre_v : a.xf_pre_k;
     const float fs = is_v ? a.xf_post_v : a.xf_post_k;
     const uint32_t units = ts.rows * H;
+    const uint32_t tstride = rope_tab_stride(a);
     for (uint32_t u0 = static_cast<uint32_t>(warp) * per_warp; u0 < units;
          u0 += CW * per_warp) {
         const uint32_t u = u0 + sub;
         const bool valid = sub < per_warp && u < units;
         const uint32_t row = !valid ? 0u : (H == 1u ? u : __umulhi(u, a.xf_heads_magic));
         const uint32_t h = valid ? u - row * H : 0u;
+        // RoPE: the (cos, sin) of this warp-iteration's rows, each angle once
+        const uint32_t r0 = H == 1u ? u0 : __umulhi(u0, a.xf_heads_magic);
+        if (n_rope) {
+            const uint32_t ul = min(units, u0 + per_warp) - 1u;
+            const uint32_t nr = (H == 1u ? ul : __umulhi(ul, a.xf_heads_magic)) - r0 + 1u;
+            __syncwarp();                      // the previous iteration's reads are done
+            for (uint32_t rr = 0; rr < nr; ++rr) {
+                const float pos = __uint2float_rn(pos0 + r0 + rr);
+                for (uint32_t i = static_cast<uint32_t>(lane); i < half; i += 32u) {
+                    float sn, cs;
+                    sincosf(__fmul_rn(pos, theta_s[i]), &sn, &cs);
+                    tab[rr * tstride + i + 2u * (i / 32u)] = make_float2(cs, sn);
+                }
+            }
+            __syncwarp();
+        }
         float2 P[16];
         const __half *x = reinterpret_cast<const __half *>(ib + static_cast<size_t>(row) * a.n_embd * 2u) + h * D;
         // a lane past the last unit reads row 0 and stores nothing; the lanes
@@ -369,24 +407,29 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
         load32(x + 32u * j, lane, P);
         const uint32_t i0 = 32u * j;
         if (valid && i0 < n_rope) {
-            // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i];
-            // the partner half is read 8 values at a time
+            // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i]
+            // (cos, sin from the table); the partner half is read 8 values at a time
             const bool lo = i0 < half;
             const __half *xp = x + (lo ? i0 + half : i0 - half);
-            const float pos = __uint2float_rn(pos0 + row);
-            const float *th = theta_s + (lo ? i0 : i0 - half);
+            const uint32_t ti = lo ? i0 : i0 - half;            // a multiple of 32
+            const float4 *tr = reinterpret_cast<const float4 *>(tab + (row - r0) * tstride + ti + 2u * (ti / 32u));
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const uint4 raw = *reinterpret_cast<const uint4 *>(xp + 8 * c);
                 const __half2 *hw = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    float sn, cs;
-                    sincosf(__fmul_rn(pos, th[8 * c + m]), &sn, &cs);
-                    float &v = (m & 1) ? P[4 * c + (m >> 1)].y : P[4 * c + (m >> 1)].x;
-                    const float w = (m & 1) ? __high2float(hw[m >> 1]) : __low2float(hw[m >> 1]);
-                    v = lo ? __fsub_rn(__fmul_rn(v, cs), __fmul_rn(w, sn))
-                           : __fadd_rn(__fmul_rn(w, sn), __fmul_rn(v, cs));
+                for (int m2 = 0; m2 < 4; ++m2) {
+                    const float4 t2 = tr[4 * c + m2];           // (cos, sin) of values 8c+2m2, +1
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int m = 2 * m2 + e;
+                        const float cs = e ? t2.z : t2.x;
+                        const float sn = e ? t2.w : t2.y;
+                        float &v = e ? P[4 * c + m2].y : P[4 * c + m2].x;
+                        const float w = e ? __high2float(hw[m >> 1]) : __low2float(hw[m >> 1]);
+                        v = lo ? __fsub_rn(__fmul_rn(v, cs), __fmul_rn(w, sn))
+                               : __fadd_rn(__fmul_rn(w, sn), __fmul_rn(v, cs));
+                    }
                 }
             }
         }
@@ -424,7 +467,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
     uint64_t *ofree = done + NS;   // phase k of ofree[s]: the store of tile s + k*NS has read out[s]
     TileSlot *slot = reinterpret_cast<TileSlot *>(smem + 128);
     float *theta_s = reinterpret_cast<float *>(smem + kStageinHeader);   // RoPE frequencies
-    uint8_t *in_buf = smem + kStageinHeader + stagein_theta_bytes(a);
+    float2 *rope_tab = reinterpret_cast<float2 *>(smem + kStageinHeader + stagein_theta_bytes(a));
+    uint8_t *in_buf = smem + kStageinHeader + stagein_theta_bytes(a) + CW * rope_tab_warp_bytes(a);
     uint8_t *out_buf = in_buf + NS * a.tile_in_bytes;
 
     const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
@@ -566,7 +610,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
         if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
-                transform_tile<CW>(a, ts, ib, ob, warp, lane, xsub, xj, xper, theta_s);
+                transform_tile<CW>(a, ts, ib, ob, warp, lane, xsub, xj, xper, theta_s,
+                                   rope_tab + warp * (rope_tab_warp_bytes(a) / 8u));
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done[s]);
@@ -642,6 +687,7 @@ void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, u
 
 size_t stagein_smem_bytes(const StageinArgs &a) {
     return kStageinHeader + stagein_theta_bytes(a) +
+           static_cast<size_t>(stagein_consumer_warps(a)) * rope_tab_warp_bytes(a) +
            static_cast<size_t>(stagein_stages(a)) * (a.tile_in_bytes + a.tile_out_bytes);
 }
 
