@@ -10,6 +10,7 @@
 
 #include <atomic>
 #include <stdint.h>
+#include <utility>
 
 #include "../../include/kvm.h"
 
@@ -186,6 +187,16 @@ __device__ __forceinline__ void bulk_wait_all() {
     asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch (sm_90+ PTX).  launch_dependents lets the
+// next grid of the stream, launched with programmatic stream serialization,
+// start its CTAs now; wait blocks until the grids this one depends on have
+// completed and their writes are visible.  Without a programmatic launch
+// both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void set_status(uint32_t *status, uint32_t bits) {
     if (status) atomicOr(status, bits);
 }
@@ -331,6 +342,25 @@ __device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t *scratch) {
 }
 
 // ---------------------------------------------------------- host helpers --
+
+// A launch whose CTAs may start while the previous kernel of the stream is
+// still running (programmatic stream serialization); the kernel calls
+// pdl_wait() before it reads anything an earlier launch writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_after_prev(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // SM count of the current device (cached per host thread and device).
 inline int num_sms() {

@@ -84,12 +84,6 @@ __device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
 
 // ----------------------------------------------------------------- query --
 
-// Programmatic dependent launch (sm_90+ PTX): let the next grid of the
-// stream launch now / wait until the grids this one depends on are complete
-// and their writes visible.  Without a programmatic launch both are no-ops.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 // One CTA = (layer, KV head), one thread per channel:
 //   qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq,
 //   invq = 1.0f / (q_count * g); nq[l][h] = sum over d of qv*qv in order.
@@ -249,6 +243,10 @@ __global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
         rr = __fdiv_rn(dot, __fadd_rn(__fmul_rn(__fsqrt_rn(nq_s[h]), __fsqrt_rn(nk)), 1e-6f));
     r_s[h * 32u + lane] = rr;
     __syncthreads();
+    // only now may the dependent selection launch: every CTA of this grid
+    // is resident by the time the last one gets here, so the dependent can
+    // never hold an SM a CTA of this grid still waits for
+    pdl_launch_dependents();
     if (h == 0 && mine) {
         // layer term: the heads' results summed in head order (double) / H
         double term = 0.0;

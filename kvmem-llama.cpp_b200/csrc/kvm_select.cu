@@ -310,9 +310,13 @@ __global__ void __launch_bounds__(kSelectThreads) select_diff_kernel(SelectArgs 
     prefetch_l2(da.bt.baked_pos, sizeof(int64_t) * n);
     prefetch_l2(da.bt.remap_count, sizeof(uint32_t) * n);
     prefetch_l2(da.bt.remap_abs_delta, sizeof(uint64_t) * n);
+    pdl_wait();                  // the scores (and any earlier write) are complete
     uint8_t *kept = fl;
     uint8_t *was = fl + (n ? n : 1u);
     const uint32_t m = select_core(sa, kept);
+    // the stage-in's CTAs may now take SMs for their set-up (this grid's one
+    // CTA is running); they wait for this kernel to finish before reading the plan
+    pdl_launch_dependents();
     diff_core(da, min(m, n), kept, was, true);
 }
 
@@ -350,8 +354,7 @@ cudaError_t launch_select_diff(const SelectArgs &sa, const DiffArgs &da, cudaStr
                                                    static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    select_diff_kernel<<<1, kSelectThreads, smem, stream>>>(sa, da);
-    return cudaGetLastError();
+    return launch_after_prev(select_diff_kernel, dim3(1), dim3(kSelectThreads), smem, stream, sa, da);
 }
 
 cudaError_t launch_canon_ids(const uint32_t *ids, uint32_t n_ids, uint32_t n_blocks,

@@ -471,15 +471,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
     uint8_t *in_buf = smem + kStageinHeader + stagein_theta_bytes(a) + CW * rope_tab_warp_bytes(a);
     uint8_t *out_buf = in_buf + NS * a.tile_in_bytes;
 
-    const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
-    const uint32_t n_items = min(n_items_raw, a.max_items);
-    const uint32_t tiles = (a.block_tokens + a.rows_per_tile - 1) / a.rows_per_tile;
-    const uint64_t total = static_cast<uint64_t>(n_items) * a.n_layer * a.n_kv * tiles;
-    if (static_cast<uint64_t>(blockIdx.x) >= total) return;
-
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    // set-up that needs nothing of the previous launch runs before the wait
     if (XF && a.rope_n_rot) {
         for (uint32_t i = static_cast<uint32_t>(tid); i < a.rope_n_rot / 2u; i += blockDim.x)
             theta_s[i] = a.theta[i];
@@ -493,6 +488,13 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
         fence_mbar_init();
     }
     __syncthreads();   // the only CTA-wide barrier
+    pdl_wait();        // the plan (cold list and its count) is complete
+
+    const uint32_t n_items_raw = a.n_items_dev ? *a.n_items_dev : a.n_items_host;
+    const uint32_t n_items = min(n_items_raw, a.max_items);
+    const uint32_t tiles = (a.block_tokens + a.rows_per_tile - 1) / a.rows_per_tile;
+    const uint64_t total = static_cast<uint64_t>(n_items) * a.n_layer * a.n_kv * tiles;
+    if (static_cast<uint64_t>(blockIdx.x) >= total) return;
 
     if (warp == CW) {
         // ---------------------------------------------------------- producer
@@ -710,8 +712,7 @@ static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, u
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    stagein_kernel<NS, XF, CW><<<grid, threads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_after_prev(stagein_kernel<NS, XF, CW>, dim3(grid), dim3(threads), smem, stream, a);
 }
 
 static std::atomic<uint64_t> g_xform_attr{0};
