@@ -21,9 +21,10 @@
  * the next kvm_diff performs both inside its own launch (one kernel for
  * select + diff).  Any other call that depends on that work -- one that
  * rewrites the scores or the plan, reads or writes the block table, appends
- * blocks, waits or reads results -- launches it first, on the stream it was
- * recorded on, so every sequence of calls has the effect of running them in
- * order.
+ * blocks, waits or reads results -- launches it first, on that call's own
+ * stream.  A correct program orders such a call after kvm_select /
+ * kvm_reset_window anyway (same stream, or a wait between streams), so every
+ * sequence of calls has the effect of running them in order.
  *
  * Reference interfaces this ABI replaces (paths in CrKcel/kvmem-llama.cpp):
  *   - llama_memory_kvmem::score_retrieval        src/adapter/llama-memory-kvmem.cpp:2869-2916

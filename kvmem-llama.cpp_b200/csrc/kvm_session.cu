@@ -71,9 +71,7 @@ struct kvm_session {
     // so the order of the calls keeps its meaning.
     bool select_pending = false;
     uint32_t select_n_mandatory = 0;
-    cudaStream_t select_stream = nullptr;
     bool reset_pending = false;
-    cudaStream_t reset_stream = nullptr;
 
     // device state
     SummaryLayout sum{};
@@ -231,40 +229,44 @@ SelectArgs select_args(kvm_session *s, uint32_t n_mandatory) {
     return a;
 }
 
-// Launch the deferred select / window reset, each on the stream of the call
-// that recorded it.  An entry point flushes what it depends on: the
-// selection before anything that rewrites the scores, the plan or the block
-// count; the reset before anything that reads or writes the block table.
-kvm_status flush_select(kvm_session *s) {
+// Launch the deferred select / window reset on the stream of the call that
+// needs it.  A call that depends on the selection or the reset is ordered
+// after kvm_select / kvm_reset_window by the caller (same stream, or a wait
+// between streams), so that stream is where the work belongs: the mandatory
+// list the select reads was uploaded before that point.  An entry point
+// flushes what it depends on: the selection before anything that rewrites
+// the scores, the plan or the block count; the reset before anything that
+// reads or writes the block table.
+kvm_status flush_select(kvm_session *s, cudaStream_t st) {
     if (!s->select_pending) return KVM_OK;
     s->select_pending = false;
-    KVM_CUDA(s, launch_select(select_args(s, s->select_n_mandatory), s->select_stream), "select launch");
+    KVM_CUDA(s, launch_select(select_args(s, s->select_n_mandatory), st), "select launch");
     s->launches++;
     return KVM_OK;
 }
 
-kvm_status flush_reset(kvm_session *s) {
+kvm_status flush_reset(kvm_session *s, cudaStream_t st) {
     if (!s->reset_pending) return KVM_OK;
     s->reset_pending = false;
-    KVM_CUDA(s, launch_reset_window(s->bt, s->n_blocks, s->reset_stream), "reset launch");
+    KVM_CUDA(s, launch_reset_window(s->bt, s->n_blocks, st), "reset launch");
     s->launches++;
     return KVM_OK;
 }
 
-#define KVM_FLUSH_SEL(s)                               \
-    do {                                               \
-        const kvm_status f__ = flush_select(s);        \
-        if (f__ != KVM_OK) return f__;                 \
+#define KVM_FLUSH_SEL(s)                                           \
+    do {                                                           \
+        const kvm_status f__ = flush_select(s, as_stream(stream)); \
+        if (f__ != KVM_OK) return f__;                             \
     } while (0)
-#define KVM_FLUSH_RESET(s)                             \
-    do {                                               \
-        const kvm_status f__ = flush_reset(s);         \
-        if (f__ != KVM_OK) return f__;                 \
+#define KVM_FLUSH_RESET(s)                                         \
+    do {                                                           \
+        const kvm_status f__ = flush_reset(s, as_stream(stream));  \
+        if (f__ != KVM_OK) return f__;                             \
     } while (0)
-#define KVM_FLUSH(s)                                   \
-    do {                                               \
-        KVM_FLUSH_SEL(s);                              \
-        KVM_FLUSH_RESET(s);                            \
+#define KVM_FLUSH(s)                                               \
+    do {                                                           \
+        KVM_FLUSH_SEL(s);                                          \
+        KVM_FLUSH_RESET(s);                                        \
     } while (0)
 
 kvm_status upload_window(kvm_session *s, cudaStream_t st, const kvm_window *win) {
@@ -912,11 +914,10 @@ kvm_status kvm_reset_window(kvm_session *s, kvm_stream stream) {
     if (!s) return KVM_EINVAL;
     DeviceGuard g(s->device);
     // a pending select does not read the block table: it may stay pending
-    // and fuse with the next diff, which also applies this reset
-    if (s->n_blocks) {
-        s->reset_pending = true;
-        s->reset_stream = as_stream(stream);
-    }
+    // and fuse with the next diff, which also applies this reset (the
+    // stream argument orders nothing until a later call launches the reset)
+    (void)stream;
+    if (s->n_blocks) s->reset_pending = true;
     std::fill(s->h_slot.begin(), s->h_slot.end(), -1);
     s->slots_known = true;
     s->window_empty = true;
@@ -1352,7 +1353,6 @@ kvm_status kvm_select(kvm_session *s, kvm_stream stream, const uint32_t *mandato
     // with whatever entry point comes first
     s->select_pending = true;
     s->select_n_mandatory = n_mandatory;
-    s->select_stream = st;
     s->have_selection = true;
     return KVM_OK;
 }
@@ -1427,9 +1427,7 @@ kvm_status kvm_diff(kvm_session *s, kvm_stream stream, int force_raw_refresh) {
     if (!s->have_selection) return fail(s, KVM_ESTATE, "kvm_diff needs a selection (kvm_select)");
     DeviceGuard g(s->device);
     cudaStream_t st = as_stream(stream);
-    // a pending select or reset recorded on another stream runs there first
-    if (s->select_pending && s->select_stream != st) KVM_FLUSH_SEL(s);
-    if (s->reset_pending && s->reset_stream != st) KVM_FLUSH_RESET(s);
+    // a pending select and reset run inside this launch, on this stream
     DiffArgs a{};
     a.bt = s->bt;
     a.n_blocks = s->n_blocks;
