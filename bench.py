@@ -394,10 +394,10 @@ def run_kvm(args):
                                           args.steps, args.warmup)
         result["layer_split"] = layer_split_phase(args, torch, kvm, dist, world, rank, local, dev,
                                                   args.steps, args.warmup)
+    if dist:
+        dist.destroy_process_group()       # its NCCL log lines come before the result
     if rank == 0:
         print(json.dumps(result), flush=True)
-    if dist:
-        dist.destroy_process_group()
 
 
 def run_e2e(args, torch, kvm, sess, c, hk, hv, qs, qc, kb, vb, dev, stream, step_bytes, world,
@@ -1287,9 +1287,14 @@ def run_kernels(args):
 def main():
     args = parse()
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        # communicator set-up lines (rank count per communicator) in the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # communicator set-up lines (rank count per communicator) in rank 0's
+        # log; the other ranks write theirs to files so rank 0's JSON line
+        # stays the last line of the output
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        if int(os.environ.get("RANK", "0")) != 0:
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/kvm_bench_nccl.%h.%p.log")
     if args.mode == "layer-split":
         run_layer_split(args)
     elif args.mode == "incremental":
