@@ -196,25 +196,28 @@ __device__ __forceinline__ float2 mul_add_off(float2 x, float id, float2 off) {
     return f2_add_rn(make_float2(__fmul_rn(x.x, id), __fmul_rn(x.y, id)), off);
 }
 
-// Nibble / 5-bit code of one value: min(maxq, (int)(x*id + off)).  The
-// plain path keeps the float-to-int conversion: its q4_0 / q5_0 kernels are
-// bound by the integer pipe, which codes4's byte fix-ups would load further.
-__device__ __forceinline__ uint32_t code_q(float x, float id, float off, int maxq) {
-    const int q = __float2int_rz(__fadd_rn(__fmul_rn(x, id), off));
-    return static_cast<uint32_t>(q > maxq ? maxq : q);
-}
-
-// The 8 codes of one chunk as bytes: word p holds values 4p .. 4p+3.
+// The 8 codes of one chunk as bytes, min(MAXQ, (int)(x*id + off)) each:
+// word p holds values 4p .. 4p+3.  The products are scalar and rounded, the
+// adds packed (per component the same IEEE add).  x*id lies in [-h, h] for
+// vmax = -h*d (h = 8 or 16), so t = x*id + off is in [0.5, MAXQ + 1.5] and
+// (int)t is at most MAXQ + 1; the clamp is then one subtraction per 4
+// codes of each byte's bit log2(MAXQ + 1).  A NaN t (a NaN or infinite
+// input) converts to code 0, as before.
 template <int MAXQ>
 __device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, uint32_t (&w)[2]) {
+    static_assert(MAXQ == 15 || MAXQ == 31, "MAXQ");
     const __half2 *h = halves(r);
+    const float2 o2 = make_float2(off, off);
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
         const float2 x0 = __half22float2(h[2 * p]);
         const float2 x1 = __half22float2(h[2 * p + 1]);
-        const uint32_t c0 = code_q(x0.x, id, off, MAXQ), c1 = code_q(x0.y, id, off, MAXQ);
-        const uint32_t c2 = code_q(x1.x, id, off, MAXQ), c3 = code_q(x1.y, id, off, MAXQ);
-        w[p] = __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
+        const float2 t0 = f2_add_rn(make_float2(__fmul_rn(x0.x, id), __fmul_rn(x0.y, id)), o2);
+        const float2 t1 = f2_add_rn(make_float2(__fmul_rn(x1.x, id), __fmul_rn(x1.y, id)), o2);
+        const uint32_t c0 = __float2uint_rz(t0.x), c1 = __float2uint_rz(t0.y);
+        const uint32_t c2 = __float2uint_rz(t1.x), c3 = __float2uint_rz(t1.y);
+        const uint32_t v = __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
+        w[p] = v - ((v >> (MAXQ == 15 ? 4 : 5)) & 0x01010101u);
     }
 }
 
