@@ -252,6 +252,23 @@ __device__ __forceinline__ float signed_absmax(const Block32 &b, float *amax_out
     return first_of_absmax(b, amax);
 }
 
+// A ggml block of a 2-byte header (F16 d) followed by NW payload words (4*NW
+// bytes), at a 2-byte aligned address: NW word stores and one half-word store.
+// At a 4-byte aligned address the words are shifted by two bytes.
+template <int NW>
+__device__ __forceinline__ void store_block(uint8_t *blk, uint32_t hdr, const uint32_t (&w)[NW]) {
+    const bool odd = (reinterpret_cast<uintptr_t>(blk) & 2u) != 0u;
+    const uint32_t sel = odd ? 0x7654u : 0x5432u;
+    uint32_t *wp = reinterpret_cast<uint32_t *>(blk + (odd ? 2 : 0));
+    uint32_t prev = hdr << 16;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        wp[k] = __byte_perm(prev, w[k], sel);
+        prev = w[k];
+    }
+    st_u16(blk + (odd ? 0 : 4 * NW), odd ? hdr : (w[NW - 1] >> 16));
+}
+
 // q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes).  d = vmax /
 // -8 (-16) is computed as vmax * -0.125 (-0.0625): division and
 // multiplication by a power of two return the same correctly rounded value.
@@ -265,22 +282,26 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
     uint32_t w[4][2];
 #pragma unroll
     for (int k = 0; k < 4; ++k) chunk_code_bytes<Q5 ? 31 : 15>(b.raw[k], id, off, w[k]);
-    st_u16(blk, f16_bits(d));
-    uint8_t *qs = blk + (Q5 ? 6 : 2);
+    // chunks k and k+2 are a nibble pair: value j of the lower chunk index
+    // takes the low nibble of byte j, its partner 16 values on the high one.
+    // Pair k = 0 and pair k = 1 land on nibble words 0-1 and 2-3 or the
+    // other way round, by the lane's chunk rotation.
+    uint32_t nib[2][2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        // chunks k and k+2 are a nibble pair: value j of the lower chunk index
-        // takes the low nibble of byte j, its partner 16 values on the high one
         const bool a_low = chunk_of(b, k) < 2;
         const uint32_t *lo = a_low ? w[k] : w[k + 2];
         const uint32_t *hi = a_low ? w[k + 2] : w[k];
-        uint8_t *q = qs + 8 * (a_low ? chunk_of(b, k) : chunk_of(b, k + 2));
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-            const uint32_t by = (lo[p] & 0x0f0f0f0fu) | ((hi[p] << 4) & 0xf0f0f0f0u);
-            st_u16(q + 4 * p, by & 0xffffu);
-            st_u16(q + 4 * p + 2, by >> 16);
-        }
+        for (int p = 0; p < 2; ++p) nib[k][p] = (lo[p] & 0x0f0f0f0fu) | ((hi[p] << 4) & 0xf0f0f0f0u);
+    }
+    const bool first0 = ((chunk_of(b, 0) < 2 ? chunk_of(b, 0) : chunk_of(b, 2)) == 0);
+    constexpr int NW = Q5 ? 5 : 4;
+    uint32_t o[NW];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        o[NW - 4 + p] = first0 ? nib[0][p] : nib[1][p];
+        o[NW - 2 + p] = first0 ? nib[1][p] : nib[0][p];
     }
     if (Q5) {
         uint32_t qh = 0;
@@ -289,9 +310,9 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
             const int c = chunk_of(b, k);
             qh |= (high_bits4(w[k][0]) | (high_bits4(w[k][1]) << 4)) << (8 * c);
         }
-        st_u16(blk + 2, qh & 0xffffu);
-        st_u16(blk + 4, qh >> 16);
+        o[0] = qh;
     }
+    store_block<NW>(blk, f16_bits(d), o);
 }
 
 // Load block `qb` of a tile (64 bytes per block in shared memory) with the

@@ -174,23 +174,6 @@ __device__ __forceinline__ uint32_t pack4(int q0, int q1, int q2, int q3) {
                        __byte_perm(static_cast<uint32_t>(q2), static_cast<uint32_t>(q3), 0x0040u), 0x5410u);
 }
 
-// A ggml block of a 2-byte header (F16 d) followed by NW payload words (4*NW
-// bytes), at a 2-byte aligned address: NW word stores and one half-word store.
-// At a 4-byte aligned address the words are shifted by two bytes.
-template <int NW>
-__device__ __forceinline__ void store_block(uint8_t *blk, uint32_t hdr, const uint32_t (&w)[NW]) {
-    const bool odd = (reinterpret_cast<uintptr_t>(blk) & 2u) != 0u;
-    const uint32_t sel = odd ? 0x7654u : 0x5432u;
-    uint32_t *wp = reinterpret_cast<uint32_t *>(blk + (odd ? 2 : 0));
-    uint32_t prev = hdr << 16;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-        wp[k] = __byte_perm(prev, w[k], sel);
-        prev = w[k];
-    }
-    st_u16(blk + (odd ? 0 : 4 * NW), odd ? hdr : (w[NW - 1] >> 16));
-}
-
 __device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
 
 // C roundf of both components, as integers (|x| < 2^23).  y must come from
