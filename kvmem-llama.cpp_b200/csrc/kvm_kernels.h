@@ -10,12 +10,16 @@
 namespace kvm {
 
 constexpr int kStageinConsumerWarps = 8;
-// Transform mode without RoPE: 7 consumer warps + the producer, so that two
-// CTAs (16 warps, four per scheduler) leave 128 registers a thread for the
-// packed butterflies.
-constexpr int kXfConsumerWarps = 7;
 constexpr int kStageinStages = 3;
-constexpr int kXfStages = 5;       // transform mode: ALU-heavier tiles, loads further ahead
+// Transform mode.  attn_rot alone: 7 consumer warps + the producer, three
+// CTAs an SM (80 registers a thread), three stages; with RoPE: 8 + 1 warps,
+// two CTAs an SM (sincosf wants the registers), four stages of input only.
+constexpr int kXfConsumerWarps = 7;
+constexpr int kXfMinBlocks = 3;
+constexpr int kXfStages = 3;
+constexpr int kXfRopeWarps = 8;
+constexpr int kXfRopeMinBlocks = 2;
+constexpr int kXfRopeStages = 4;
 constexpr int kPermuteThreads = 512;
 constexpr uint32_t kSumGroup = 32;                 // blocks per summary tile
 constexpr uint32_t kScoreRange = 32;               // blocks per scorer CTA (a warp's lanes)

@@ -148,7 +148,7 @@ __device__ __forceinline__ float first_of_absmax(const Block32 &b, float amax) {
 __device__ __forceinline__ void quant_q8_0(const Block32 &b, uint8_t *blk) {
     const float amax = absmax32(b);
     const float d = div127(amax);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     st_u16(blk, f16_bits(d));
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -221,11 +221,21 @@ __device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float
     }
 }
 
-// Bit 4 of each of the 4 byte codes of `w`, as bits 0..3: the masked bytes
-// sit at bits 0, 8, 16, 24 and the multiply by 0x01020408 lands them on bits
-// 24..27 (every partial product on its own bit, so no carries).
-__device__ __forceinline__ uint32_t high_bits4(uint32_t w) {
-    return (((w >> 4) & 0x01010101u) * 0x01020408u) >> 24;
+// Bit 4 of each of the 8 byte codes (at most 31) of words a (values 0..3)
+// and b (values 4..7), as the top byte of the result: value i's bit on bit
+// 24 + i.  One select puts a's bits on bits 8i and b's on bits 8i + 4 (a's
+// code bytes shifted down by 4 leave their bit 4 alone in the low nibble,
+// b's bits 5..7 are zero); the multiply by 2^24 + 2^17 + 2^10 + 2^3 moves
+// byte i's bits to 24 + i and 28 + i, and every other partial product lands
+// either above bit 31 or on its own bit below 24, so nothing carries.
+__device__ __forceinline__ uint32_t high_bits8(uint32_t a, uint32_t b) {
+    const uint32_t x = ((a >> 4) & 0x0f0f0f0fu) | (b & 0xf0f0f0f0u);
+    return x * 0x01020408u;
+}
+
+// The top bytes of p0..p3 as one word (byte i = top byte of p_i).
+__device__ __forceinline__ uint32_t top_bytes4(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3) {
+    return __byte_perm(__byte_perm(p0, p1, 0x0073u), __byte_perm(p2, p3, 0x0073u), 0x5410u);
 }
 
 // vmax of q4_0 / q5_0 -- the first value (block order) of largest magnitude --
@@ -277,7 +287,7 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
     float amax;
     const float vmax = signed_absmax(b, &amax);
     const float d = __fmul_rn(vmax, Q5 ? -0.0625f : -0.125f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     const float off = Q5 ? 16.5f : 8.5f;
     uint32_t w[4][2];
 #pragma unroll
@@ -304,13 +314,10 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
         o[NW - 2 + p] = first0 ? nib[1][p] : nib[0][p];
     }
     if (Q5) {
-        uint32_t qh = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int c = chunk_of(b, k);
-            qh |= (high_bits4(w[k][0]) | (high_bits4(w[k][1]) << 4)) << (8 * c);
-        }
-        o[0] = qh;
+        // byte k of t is chunk (c0 + k) & 3's: rotate it to byte c0 + k
+        const uint32_t t = top_bytes4(high_bits8(w[0][0], w[0][1]), high_bits8(w[1][0], w[1][1]),
+                                      high_bits8(w[2][0], w[2][1]), high_bits8(w[3][0], w[3][1]));
+        o[0] = __funnelshift_l(t, t, 8 * b.c0);
     }
     store_block<NW>(blk, f16_bits(d), o);
 }
@@ -324,7 +331,10 @@ __device__ __forceinline__ void load_block(const uint8_t *tile, uint32_t qb, int
     for (int k = 0; k < 4; ++k) b.raw[k] = *reinterpret_cast<const uint4 *>(p + 16 * ((b.c0 + k) & 3));
 }
 
-// One 32-value block of `type` into out_tile (block qb).
+// One 32-value block of `type` into out_tile (block qb).  F16 blocks are
+// written as 16-byte chunks when out_tile is 16-byte aligned (A16), else as
+// 2-byte halves.
+template <bool A16 = true>
 __device__ __forceinline__ void quant_block(int type, const Block32 &b, uint8_t *out_tile, uint32_t qb) {
     if (type == KVM_TYPE_Q8_0) {
         quant_q8_0(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ8);
@@ -335,8 +345,18 @@ __device__ __forceinline__ void quant_block(int type, const Block32 &b, uint8_t 
     } else {
         uint8_t *o = out_tile + static_cast<size_t>(qb) * 64u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            *reinterpret_cast<uint4 *>(o + 16 * chunk_of(b, k)) = b.raw[k];
+        for (int k = 0; k < 4; ++k) {
+            if (A16) {
+                *reinterpret_cast<uint4 *>(o + 16 * chunk_of(b, k)) = b.raw[k];
+            } else {
+                const uint32_t w[4] = {b.raw[k].x, b.raw[k].y, b.raw[k].z, b.raw[k].w};
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    st_u16(o + 16 * chunk_of(b, k) + 4 * m, w[m] & 0xffffu);
+                    st_u16(o + 16 * chunk_of(b, k) + 4 * m + 2, w[m] >> 16);
+                }
+            }
+        }
     }
 }
 

@@ -103,9 +103,11 @@ struct TileSlot {
 };
 static_assert(sizeof(TileSlot) == 24, "TileSlot");
 
-// Shared memory: [0,128) barriers (full[NS], done[NS], ofree[NS]); [128,384)
-// tile slots; then NS input tiles and NS output tiles.
-constexpr uint32_t kStageinHeader = 384;
+// Shared memory: [0,192) barriers (full[NS], done[NS], ofree[NS]); [192,512)
+// tile slots; then NS input tiles and, except in the RoPE kernel (which
+// stores the window from registers), NS output tiles.
+constexpr uint32_t kStageinBarBytes = 192;
+constexpr uint32_t kStageinHeader = 512;
 
 // Shared-memory copy of the RoPE frequencies (transform mode), between the
 // header and the tiles; a multiple of 128 bytes so the tiles stay aligned.
@@ -134,16 +136,15 @@ __host__ __device__ inline uint32_t rope_tab_warp_bytes(const StageinArgs &a) {
     return (a.xform && a.rope_n_rot) ? ((rope_tab_rows(a) * rope_tab_stride(a) * 8u + 127u) & ~127u) : 0u;
 }
 
-// Pipeline depth: transform tiles are ALU-heavier, so their loads run further
-// ahead -- except with RoPE, whose sincosf wants the L1 that a deeper
-// pipeline's shared memory would take.
+// Pipeline depth (measured at config 2): attn_rot at three CTAs an SM fits
+// three stages; the RoPE kernel's stages hold no output tile.
 __host__ __device__ inline int stagein_stages(const StageinArgs &a) {
-    return !a.xform ? kStageinStages : (a.rope_n_rot ? kStageinStages : kXfStages);
+    return !a.xform ? kStageinStages : (a.rope_n_rot ? kXfRopeStages : kXfStages);
 }
 
 // Consumer warps of a launch (see stagein_kernel).
 __host__ __device__ inline int stagein_consumer_warps(const StageinArgs &a) {
-    return (a.xform && !a.rope_n_rot) ? kXfConsumerWarps : kStageinConsumerWarps;
+    return !a.xform ? kStageinConsumerWarps : (a.rope_n_rot ? kXfRopeWarps : kXfConsumerWarps);
 }
 
 // ------------------------------------------------------- transform mode --
@@ -252,10 +253,8 @@ __device__ __forceinline__ void quant_q4q5_pairs(const float2 (&P)[16], float fs
 #pragma unroll
     for (int k = 0; k < 4; ++k) w[NW - 4 + k] = (c[k] & 0x0f0f0f0fu) | ((c[k + 4] << 4) & 0xf0f0f0f0u);
     if (Q5) {
-        uint32_t qh = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) qh |= high_bits4(c[k]) << (4 * k);
-        w[0] = qh;
+        w[0] = top_bytes4(high_bits8(c[0], c[1]), high_bits8(c[2], c[3]), high_bits8(c[4], c[5]),
+                          high_bits8(c[6], c[7]));
     }
     store_block<NW>(blk, f16_bits(d), w);
 }
@@ -271,26 +270,22 @@ __device__ __forceinline__ void store_f16_pairs(const float2 (&P)[16], float fs,
 }
 
 // 32 consecutive F16 values of a tile row (64 bytes), widened.  The four
-// 16-byte chunks are read in the order k ^ r, r = (lane >> 1) & 3, so that a
-// quarter warp reading 8 neighbouring blocks hits 8 different bank groups,
-// then put back in order with two conditional swaps.
+// 16-byte chunks are read in the order k ^ r, r = (lane >> 1) & 1, so that a
+// quarter warp reading 8 neighbouring blocks spreads over 4 bank groups (two
+// lanes a group instead of four), then put back in order with one
+// conditional swap.  Rotating over all four chunks removes the last 2-way
+// conflict but costs a second swap, which measured slower.
 __device__ __forceinline__ void load32(const __half *p, int lane, float2 (&P)[16]) {
-    const uint32_t r = static_cast<uint32_t>(lane >> 1) & 3u;
+    const uint32_t r = static_cast<uint32_t>(lane >> 1) & 1u;
     uint4 c[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) c[k] = *reinterpret_cast<const uint4 *>(p + 8u * (static_cast<uint32_t>(k) ^ r));
-    // c[k] = chunk k ^ r: swap by bit 0 of r, then by bit 1
+    // c[k] = chunk k ^ r
 #pragma unroll
     for (int k = 0; k < 4; k += 2) {
         const uint4 a = c[k], b = c[k + 1];
-        c[k] = (r & 1u) ? b : a;
-        c[k + 1] = (r & 1u) ? a : b;
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const uint4 a = c[k], b = c[k + 2];
-        c[k] = (r & 2u) ? b : a;
-        c[k + 2] = (r & 2u) ? a : b;
+        c[k] = r ? b : a;
+        c[k + 1] = r ? a : b;
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -343,7 +338,7 @@ __device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, ui
 
 // (sub, j): the lane's unit within the warp and its block within the head;
 // per_warp = 32 / xform units a warp-iteration.
-template <int CW>
+template <int CW, bool ROPE>
 __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileSlot &ts, const uint8_t *ib,
                                                uint8_t *ob, int warp, int lane, uint32_t sub, uint32_t j,
                                                uint32_t per_warp, const float *theta_s, float2 *tab) {
@@ -369,7 +364,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
         const uint32_t h = valid ? u - row * H : 0u;
         // RoPE: the (cos, sin) of this warp-iteration's rows, each angle once
         const uint32_t r0 = H == 1u ? u0 : __umulhi(u0, a.xf_heads_magic);
-        if (n_rope) {
+        if (ROPE && n_rope) {
             const uint32_t ul = min(units, u0 + per_warp) - 1u;
             const uint32_t nr = (H == 1u ? ul : __umulhi(ul, a.xf_heads_magic)) - r0 + 1u;
             __syncwarp();                      // the previous iteration's reads are done
@@ -389,7 +384,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
         // of one unit share validity, so its values never reach a valid lane
         load32(x + 32u * j, lane, P);
         const uint32_t i0 = 32u * j;
-        if (valid && i0 < n_rope) {
+        if (ROPE && valid && i0 < n_rope) {
             // rope_neox: (x0, x1) = (v[i], v[i + half]) turned by pos * theta[i]
             // (cos, sin from the table); the partner half is read 8 values at a time
             const bool lo = i0 < half;
@@ -441,14 +436,20 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
 // thread), two for the transform variants: 7 consumer warps for attn_rot (16
 // warps an SM leave 128 registers a thread, which keep the packed float pairs
 // in place), 8 with RoPE, whose sincosf latencies want the extra warps more.
-template <int NS, bool XF, int CW>
-__global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(StageinArgs a) {
-    static_assert(3 * NS * 8 <= 128 && 128 + NS * sizeof(TileSlot) <= kStageinHeader, "stage-in header");
+template <int NS, bool XF, int CW, bool ROPE = false>
+__global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : kXfMinBlocks) : 3) stagein_kernel(StageinArgs a) {
+    // RoPE tiles are bound by sincosf, not by their stores: that kernel's
+    // consumers store the window from registers, which leaves its shared
+    // memory to a deeper input pipeline.  The others stage each output tile
+    // in shared memory and the producer writes it with one bulk copy.
+    constexpr bool DS = XF && ROPE;
+    static_assert(3 * NS * 8 <= kStageinBarBytes && kStageinBarBytes + NS * sizeof(TileSlot) <= kStageinHeader,
+                  "stage-in header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
     uint64_t *ofree = done + NS;   // phase k of ofree[s]: the store of tile s + k*NS has read out[s]
-    TileSlot *slot = reinterpret_cast<TileSlot *>(smem + 128);
+    TileSlot *slot = reinterpret_cast<TileSlot *>(smem + kStageinBarBytes);
     float *theta_s = reinterpret_cast<float *>(smem + kStageinHeader);   // RoPE frequencies
     float2 *rope_tab = reinterpret_cast<float2 *>(smem + kStageinHeader + stagein_theta_bytes(a));
     uint8_t *in_buf = smem + kStageinHeader + stagein_theta_bytes(a) + CW * rope_tab_warp_bytes(a);
@@ -458,7 +459,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
     const int warp = tid >> 5;
     const int lane = tid & 31;
     // set-up that needs nothing of the previous launch runs before the wait
-    if (XF && a.rope_n_rot) {
+    if (XF && ROPE) {
         for (uint32_t i = static_cast<uint32_t>(tid); i < a.rope_n_rot / 2u; i += blockDim.x)
             theta_s[i] = a.theta[i];
     }
@@ -528,7 +529,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
             }
             const TileSlot ts = slot[s];
             const uint8_t *ob = out_buf + s * a.tile_out_bytes;
-            if (a.bulk_store) {
+            if (DS) {
+                // the consumers stored this tile from their registers
+            } else if (a.bulk_store) {
                 if (lane == 0) {
                     fence_proxy_async_smem();
                     bulk_s2g(ts.dst, ob, ts.out_bytes);
@@ -545,7 +548,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
                 // the consumers are done with in[s]: refill it right away; the
                 // output buffer is released separately through ofree[]
                 if (!ended) arm_next();
-                if (a.bulk_store && j >= 1) {
+                if (!DS && a.bulk_store && j >= 1) {
                     bulk_wait_read<1>();                  // the store of tile j - 1 has read its buffer
                     mbar_arrive(&ofree[(j - 1) % NS]);
                 }
@@ -565,7 +568,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
                         (void)mbar_wait_bounded(&full[s], (last / NS) & 1u);
                 }
             }
-            if (a.bulk_store) bulk_wait_all<0>();
+            if (!DS && a.bulk_store) bulk_wait_all<0>();
         }
         return;
     }
@@ -586,16 +589,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
         const TileSlot ts = slot[s];
         if (ts.rows == 0) break;
         // out[s] was last written for tile j - NS: its store must have read it
-        if (j >= static_cast<uint32_t>(NS) && !mbar_wait_bounded(&ofree[s], ((j / NS) - 1u) & 1u)) {
+        if (!DS && j >= static_cast<uint32_t>(NS) && !mbar_wait_bounded(&ofree[s], ((j / NS) - 1u) & 1u)) {
             set_status(a.status, kErrTimeout);
             break;
         }
         const uint8_t *ib = in_buf + s * a.tile_in_bytes;
-        uint8_t *ob = out_buf + s * a.tile_out_bytes;
+        // direct-store kernels write the window itself (2-byte aligned stores)
+        uint8_t *ob = DS ? ts.dst : out_buf + s * a.tile_out_bytes;
         if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
-                transform_tile<CW>(a, ts, ib, ob, warp, lane, xsub, xj, xper, theta_s,
+                transform_tile<CW, ROPE>(a, ts, ib, ob, warp, lane, xsub, xj, xper, theta_s,
                                    rope_tab + warp * (rope_tab_warp_bytes(a) / 8u));
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -608,7 +612,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? 2 : 3) stagein_kernel(Stage
              qb += CW * 32u) {
             Block32 b;
             load_block(ib, qb, lane, b);
-            quant_block(ts.type, b, ob, qb);
+            quant_block<!DS>(ts.type, b, ob, qb);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -673,29 +677,30 @@ void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, u
 size_t stagein_smem_bytes(const StageinArgs &a) {
     return kStageinHeader + stagein_theta_bytes(a) +
            static_cast<size_t>(stagein_consumer_warps(a)) * rope_tab_warp_bytes(a) +
-           static_cast<size_t>(stagein_stages(a)) * (a.tile_in_bytes + a.tile_out_bytes);
+           static_cast<size_t>(stagein_stages(a)) *
+               (a.tile_in_bytes + ((a.xform && a.rope_n_rot) ? 0u : a.tile_out_bytes));
 }
 
 
 static std::atomic<uint64_t> g_stagein_attr{0};
 
-template <int NS, bool XF, int CW>
+template <int NS, bool XF, int CW, bool ROPE>
 static cudaError_t launch_stagein_t(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap,
                                     std::atomic<uint64_t> &attr) {
     const size_t smem = stagein_smem_bytes(a);
     if (smem > 200u * 1024u || stagein_stages(a) != NS || stagein_consumer_warps(a) != CW)
         return cudaErrorInvalidValue;
-    const void *fn = reinterpret_cast<const void *>(stagein_kernel<NS, XF, CW>);
+    const void *fn = reinterpret_cast<const void *>(stagein_kernel<NS, XF, CW, ROPE>);
     if (!attr_once(attr, fn, 200 * 1024)) return cudaErrorInvalidValue;
     int per_sm = 1;
     const int threads = CW * 32 + 32;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<NS, XF, CW>,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stagein_kernel<NS, XF, CW, ROPE>,
                                                   threads, smem);
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = static_cast<uint32_t>(num_sms() * per_sm);
     if (grid_cap && grid > grid_cap) grid = grid_cap;
     if (grid == 0) grid = 1;
-    return launch_after_prev(stagein_kernel<NS, XF, CW>, dim3(grid), dim3(threads), smem, stream, a);
+    return launch_after_prev(stagein_kernel<NS, XF, CW, ROPE>, dim3(grid), dim3(threads), smem, stream, a);
 }
 
 static std::atomic<uint64_t> g_xform_attr{0};
@@ -703,14 +708,14 @@ static std::atomic<uint64_t> g_xform_rope_attr{0};
 
 cudaError_t launch_stagein(const StageinArgs &a, cudaStream_t stream, uint32_t grid_cap) {
     if (a.xform == 0)
-        return launch_stagein_t<kStageinStages, false, kStageinConsumerWarps>(a, stream, grid_cap, g_stagein_attr);
+        return launch_stagein_t<kStageinStages, false, kStageinConsumerWarps, false>(a, stream, grid_cap, g_stagein_attr);
     // lanes of a (row, head) must tile the warp's xor pairs: head_dim / 32 in
     // 1 .. 32 and, for every Hadamard size, a multiple of size / 32
     if (a.xform > 32u || (a.rot_k && a.xform % (a.rot_k / 32u)) || (a.rot_v && a.xform % (a.rot_v / 32u)))
         return cudaErrorInvalidValue;
     if (a.rope_n_rot)
-        return launch_stagein_t<kStageinStages, true, kStageinConsumerWarps>(a, stream, grid_cap, g_xform_rope_attr);
-    return launch_stagein_t<kXfStages, true, kXfConsumerWarps>(a, stream, grid_cap, g_xform_attr);
+        return launch_stagein_t<kXfRopeStages, true, kXfRopeWarps, true>(a, stream, grid_cap, g_xform_rope_attr);
+    return launch_stagein_t<kXfStages, true, kXfConsumerWarps, false>(a, stream, grid_cap, g_xform_attr);
 }
 
 }  // namespace kvm
