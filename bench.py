@@ -65,6 +65,9 @@ def parse():
                          "--types K,V window formats")
     ap.add_argument("--types", default="8,8",
                     help="K,V ggml type ids of --profile-case stagein (8 q8_0, 2 q4_0, 6 q5_0, 1 f16)")
+    ap.add_argument("--transform", choices=("none", "attn_rot", "rope_attn_rot"), default="none",
+                    help="--profile-case stagein: the window transform (attn_rot = Hadamard 256 "
+                         "on K, 64 on V; rope_attn_rot adds NeoX RoPE on K first)")
     ap.add_argument("--mode", choices=("sessions", "layer-split", "incremental", "multi-session",
                                        "kernels"),
                     default="sessions",
@@ -87,6 +90,11 @@ def parse():
 
 def row_bytes(t, e):
     return {1: 2 * e, 8: e // 32 * 34, 2: e // 32 * 18, 6: e // 32 * 22}[t]
+
+
+# The window transforms timed by --mode kernels and --profile-case stagein.
+XFORMS = {"attn_rot": dict(rot_k=256, rot_v=64),
+          "rope_attn_rot": dict(rot_k=256, rot_v=64, rope_n_rot=256, rope_freq_base=1e6)}
 
 
 def algo_bytes(c, n_staged):
@@ -729,14 +737,16 @@ def run_profile_stagein(args):
     wk, wv, kb, vb = _window(torch, c, sess.n_slots, dev)
     q = gen_queries(torch, c, 1, args.seed, dev)[0]
     sess.set_query(q.data_ptr(), np.ones(L, np.uint32))
+    if args.transform != "none":
+        sess.set_transform(**XFORMS[args.transform])
     sess.reset_window()
     sess.score()
     sess.select()
     sess.diff()
     ms = _time_ms(torch, lambda: sess.stagein(src, kb, vb), reps=max(3, args.steps), warm=args.warmup)
     b = algo_bytes(c, 256)[1]
-    print(json.dumps({"profile_case": "stagein", "types": [tk, tv], "ms": round(ms, 4),
-                      "achieved_gbs": round(b / ms / 1e6, 1)}))
+    print(json.dumps({"profile_case": "stagein", "types": [tk, tv], "transform": args.transform,
+                      "ms": round(ms, 4), "achieved_gbs": round(b / ms / 1e6, 1)}))
     sess.close()
 
 
@@ -1204,8 +1214,8 @@ def run_kernels(args):
     sess.set_query(q.data_ptr(), np.ones(L, np.uint32))
     step_b = algo_bytes(c, 256)[1]
     xf = {}
-    for name, t in (("plain", None), ("attn_rot", dict(rot_k=256, rot_v=64)),
-                    ("rope_attn_rot", dict(rot_k=256, rot_v=64, rope_n_rot=256, rope_freq_base=1e6))):
+    for name, t in (("plain", None), ("attn_rot", XFORMS["attn_rot"]),
+                    ("rope_attn_rot", XFORMS["rope_attn_rot"])):
         if t:
             sess.set_transform(**t)
         else:

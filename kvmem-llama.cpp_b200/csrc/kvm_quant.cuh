@@ -296,14 +296,17 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
     // takes the low nibble of byte j, its partner 16 values on the high one.
     // Pair k = 0 and pair k = 1 land on nibble words 0-1 and 2-3 or the
     // other way round, by the lane's chunk rotation.
+    // (values selected, not pointers: a pointer into w would put w in local memory)
     uint32_t nib[2][2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
         const bool a_low = chunk_of(b, k) < 2;
-        const uint32_t *lo = a_low ? w[k] : w[k + 2];
-        const uint32_t *hi = a_low ? w[k + 2] : w[k];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) nib[k][p] = (lo[p] & 0x0f0f0f0fu) | ((hi[p] << 4) & 0xf0f0f0f0u);
+        for (int p = 0; p < 2; ++p) {
+            const uint32_t lo = a_low ? w[k][p] : w[k + 2][p];
+            const uint32_t hi = a_low ? w[k + 2][p] : w[k][p];
+            nib[k][p] = (lo & 0x0f0f0f0fu) | ((hi << 4) & 0xf0f0f0f0u);
+        }
     }
     const bool first0 = ((chunk_of(b, 0) < 2 ? chunk_of(b, 0) : chunk_of(b, 2)) == 0);
     constexpr int NW = Q5 ? 5 : 4;
