@@ -11,11 +11,10 @@
 // bit.
 //
 // Data arrive as four 16-byte chunks (8 halves each).  A lane loads the
-// chunks of its block in a lane-dependent rotation (chunk c[k] at step k) so
-// that the 128-bit shared-memory loads of a quarter warp hit 8 different
-// bank groups; the chunk index is then only used as an output offset --
-// the max is order-free, each value is coded independently, and the q4/q5
-// nibble partner of chunk c (c+2 mod 4) is always the register k+2 mod 4.
+// chunks of its block in a lane-dependent order (Block32) so that the
+// 128-bit shared-memory loads of a quarter warp spread over the banks; the
+// chunk index is then only used as an output offset -- the max is
+// order-free and each value is coded independently.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -96,12 +95,22 @@ __device__ __forceinline__ int round_half_away(float x) {
     return __float2int_rz(__fadd_rn(x, copysignf(0x1.fffffep-2f, x)));
 }
 
+// A lane's block as four 16-byte chunks in a lane-dependent order, so that
+// the 128-bit shared-memory reads of a quarter warp (8 neighbouring blocks)
+// spread over the banks:
+//   rotation (q8_0, F16): raw[k] = chunk (c0 + k) & 3, c0 = (lane >> 1) & 3,
+//     8 different bank groups;
+//   xor (q4_0, q5_0): raw[k] = chunk k ^ c0, c0 = (lane >> 1) & 1, 4 groups
+//     (two lanes a group) -- but the nibble partners (chunks c and c ^ 2)
+//     stay at registers k and k + 2 with the lower chunk first, so pairing
+//     them needs no selects.
 struct Block32 {
-    uint4 raw[4];      // raw[k] = chunk cidx(k) of the block (8 halves)
-    int c0;            // chunk index of raw[0]; raw[k] holds chunk (c0 + k) & 3
+    uint4 raw[4];      // raw[k] = chunk chunk_of<XOR>(b, k) of the block (8 halves)
+    int c0;
 };
 
-__device__ __forceinline__ int chunk_of(const Block32 &b, int k) { return (b.c0 + k) & 3; }
+template <bool XOR>
+__device__ __forceinline__ int chunk_of(const Block32 &b, int k) { return XOR ? (k ^ b.c0) : ((b.c0 + k) & 3); }
 
 __device__ __forceinline__ const __half2 *halves(const uint4 &r) {
     return reinterpret_cast<const __half2 *>(&r);
@@ -114,11 +123,14 @@ __device__ __forceinline__ float absmax32(const Block32 &b) {
 #pragma unroll
         for (int i = (k == 0 ? 1 : 0); i < 4; ++i) m = __hmax2(m, __habs2(halves(b.raw[k])[i]));
     }
-    return fmaxf(__low2float(m), __high2float(m));
+    // __hmax2 and fmaxf return the other operand of a NaN, as the reference's
+    // fmaxf scan from 0 does; only an all-NaN block leaves NaN, which it reads as 0
+    return fmaxf(fmaxf(__low2float(m), __high2float(m)), 0.0f);
 }
 
 // Signed value of the first element (in block order) whose magnitude equals
 // amax: the reference's strict `amax < |v|` scan.  +0.0 when amax is 0.
+template <bool XOR>
 __device__ __forceinline__ float first_of_absmax(const Block32 &b, float amax) {
     if (amax == 0.0f) return 0.0f;
     float best = 0.0f;
@@ -136,7 +148,7 @@ __device__ __forceinline__ float first_of_absmax(const Block32 &b, float amax) {
             v = hx ? x.x : v;
             hit = hit || hx || hy;
         }
-        const int c = chunk_of(b, k);
+        const int c = chunk_of<XOR>(b, k);
         const bool take = hit && c < best_c;
         best = take ? v : best;
         best_c = take ? c : best_c;
@@ -164,7 +176,7 @@ __device__ __forceinline__ void quant_q8_0(const Block32 &b, uint8_t *blk) {
             const uint32_t q3 = static_cast<uint32_t>(round_half_away(__fmul_rn(c.y, id))) & 0xffu;
             w[p] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
         }
-        uint8_t *qs = blk + 2 + 8 * chunk_of(b, k);
+        uint8_t *qs = blk + 2 + 8 * chunk_of<false>(b, k);
         st_u16(qs, w[0] & 0xffffu);
         st_u16(qs + 2, w[0] >> 16);
         st_u16(qs + 4, w[1] & 0xffffu);
@@ -201,10 +213,15 @@ __device__ __forceinline__ float2 mul_add_off(float2 x, float id, float2 off) {
 // adds packed (per component the same IEEE add).  x*id lies in [-h, h] for
 // vmax = -h*d (h = 8 or 16), so t = x*id + off is in [0.5, MAXQ + 1.5] and
 // (int)t is at most MAXQ + 1; the clamp is then one subtraction per 4
-// codes of each byte's bit log2(MAXQ + 1).  A NaN t (a NaN or infinite
-// input) converts to code 0, as before.
-template <int MAXQ>
-__device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, uint32_t (&w)[2]) {
+// codes of each byte's bit log2(MAXQ + 1).
+//   RZ: (int)t as the low byte of RZ(t + 2^23) (see codes4), two packed adds
+//     per 4 codes instead of 4 conversions.  Only a NaN t (a NaN or infinite
+//     input) gives a byte above MAXQ + 1 (0xff); `nan_bytes` collects the
+//     bytes so that the caller can redo such a block without RZ.
+//   without RZ: float-to-int conversions, which turn a NaN t into code 0.
+template <int MAXQ, bool RZ>
+__device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float off, uint32_t (&w)[2],
+                                                 uint32_t &nan_bytes) {
     static_assert(MAXQ == 15 || MAXQ == 31, "MAXQ");
     const __half2 *h = halves(r);
     const float2 o2 = make_float2(off, off);
@@ -214,9 +231,18 @@ __device__ __forceinline__ void chunk_code_bytes(const uint4 &r, float id, float
         const float2 x1 = __half22float2(h[2 * p + 1]);
         const float2 t0 = f2_add_rn(make_float2(__fmul_rn(x0.x, id), __fmul_rn(x0.y, id)), o2);
         const float2 t1 = f2_add_rn(make_float2(__fmul_rn(x1.x, id), __fmul_rn(x1.y, id)), o2);
-        const uint32_t c0 = __float2uint_rz(t0.x), c1 = __float2uint_rz(t0.y);
-        const uint32_t c2 = __float2uint_rz(t1.x), c3 = __float2uint_rz(t1.y);
-        const uint32_t v = __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
+        uint32_t v;
+        if (RZ) {
+            const float2 mg = make_float2(0x1p23f, 0x1p23f);
+            const float2 u0 = f2_add_rz(t0, mg), u1 = f2_add_rz(t1, mg);
+            v = __byte_perm(__byte_perm(__float_as_uint(u0.x), __float_as_uint(u0.y), 0x0040u),
+                            __byte_perm(__float_as_uint(u1.x), __float_as_uint(u1.y), 0x0040u), 0x5410u);
+            nan_bytes |= v;
+        } else {
+            const uint32_t c0 = __float2uint_rz(t0.x), c1 = __float2uint_rz(t0.y);
+            const uint32_t c2 = __float2uint_rz(t1.x), c3 = __float2uint_rz(t1.y);
+            v = __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
+        }
         w[p] = v - ((v >> (MAXQ == 15 ? 4 : 5)) & 0x01010101u);
     }
 }
@@ -242,6 +268,7 @@ __device__ __forceinline__ uint32_t top_bytes4(uint32_t p0, uint32_t p1, uint32_
 // from the block's signed max and min: when max > -min every value of that
 // magnitude is the max, when -min > max the min; only a +a / -a tie needs the
 // first occurrence.  +0.0 when every value is zero.  *amax_out gets amax.
+template <bool XOR>
 __device__ __forceinline__ float signed_absmax(const Block32 &b, float *amax_out) {
     __half2 mx = halves(b.raw[0])[0];
     __half2 mn = mx;
@@ -257,9 +284,9 @@ __device__ __forceinline__ float signed_absmax(const Block32 &b, float *amax_out
     const float lo = fminf(__low2float(mn), __high2float(mn));
     const float amax = fmaxf(hi, -lo);
     *amax_out = amax;
-    if (amax == 0.0f) return 0.0f;
+    if (!(amax > 0.0f)) return 0.0f;          // all zero, or all NaN (the reference's scan keeps 0)
     if (hi != -lo) return hi > -lo ? hi : lo;
-    return first_of_absmax(b, amax);
+    return first_of_absmax<XOR>(b, amax);
 }
 
 // A ggml block of a 2-byte header (F16 d) followed by NW payload words (4*NW
@@ -279,36 +306,36 @@ __device__ __forceinline__ void store_block(uint8_t *blk, uint32_t hdr, const ui
     st_u16(blk + (odd ? 0 : 4 * NW), odd ? hdr : (w[NW - 1] >> 16));
 }
 
-// q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes).  d = vmax /
-// -8 (-16) is computed as vmax * -0.125 (-0.0625): division and
-// multiplication by a power of two return the same correctly rounded value.
+// q4_0 (18 bytes) and q5_0 (22 bytes: d, qh, 16 nibble bytes) of a block
+// in the xor chunk order.  d = vmax / -8 (-16) is computed as vmax * -0.125
+// (-0.0625): division and multiplication by a power of two return the same
+// correctly rounded value.
 template <bool Q5>
 __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
     float amax;
-    const float vmax = signed_absmax(b, &amax);
+    const float vmax = signed_absmax<true>(b, &amax);
     const float d = __fmul_rn(vmax, Q5 ? -0.0625f : -0.125f);
     const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     const float off = Q5 ? 16.5f : 8.5f;
     uint32_t w[4][2];
+    uint32_t nan_bytes = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) chunk_code_bytes<Q5 ? 31 : 15>(b.raw[k], id, off, w[k]);
-    // chunks k and k+2 are a nibble pair: value j of the lower chunk index
-    // takes the low nibble of byte j, its partner 16 values on the high one.
-    // Pair k = 0 and pair k = 1 land on nibble words 0-1 and 2-3 or the
-    // other way round, by the lane's chunk rotation.
-    // (values selected, not pointers: a pointer into w would put w in local memory)
+    for (int k = 0; k < 4; ++k) chunk_code_bytes<Q5 ? 31 : 15, true>(b.raw[k], id, off, w[k], nan_bytes);
+    if (nan_bytes & 0xc0c0c0c0u) {        // a NaN or infinite input: codes by conversion
+#pragma unroll
+        for (int k = 0; k < 4; ++k) chunk_code_bytes<Q5 ? 31 : 15, false>(b.raw[k], id, off, w[k], nan_bytes);
+    }
+    // Registers k and k + 2 (k < 2) hold the nibble pair of chunks c0 ^ k and
+    // c0 ^ k ^ 2, the lower one first: value j of register k takes the low
+    // nibble of byte j, its partner 16 values on the high one.  Pair k = 0 is
+    // nibble words 0-1 when c0 = 0, else 2-3.
     uint32_t nib[2][2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const bool a_low = chunk_of(b, k) < 2;
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-            const uint32_t lo = a_low ? w[k][p] : w[k + 2][p];
-            const uint32_t hi = a_low ? w[k + 2][p] : w[k][p];
-            nib[k][p] = (lo & 0x0f0f0f0fu) | ((hi << 4) & 0xf0f0f0f0u);
-        }
+        for (int p = 0; p < 2; ++p) nib[k][p] = (w[k][p] & 0x0f0f0f0fu) | ((w[k + 2][p] << 4) & 0xf0f0f0f0u);
     }
-    const bool first0 = ((chunk_of(b, 0) < 2 ? chunk_of(b, 0) : chunk_of(b, 2)) == 0);
+    const bool first0 = b.c0 == 0;
     constexpr int NW = Q5 ? 5 : 4;
     uint32_t o[NW];
 #pragma unroll
@@ -317,46 +344,52 @@ __device__ __forceinline__ void quant_q4q5(const Block32 &b, uint8_t *blk) {
         o[NW - 2 + p] = first0 ? nib[1][p] : nib[0][p];
     }
     if (Q5) {
-        // byte k of t is chunk (c0 + k) & 3's: rotate it to byte c0 + k
+        // byte k of t is chunk k ^ c0's: swap the bytes of each half when c0 = 1
         const uint32_t t = top_bytes4(high_bits8(w[0][0], w[0][1]), high_bits8(w[1][0], w[1][1]),
                                       high_bits8(w[2][0], w[2][1]), high_bits8(w[3][0], w[3][1]));
-        o[0] = __funnelshift_l(t, t, 8 * b.c0);
+        o[0] = __byte_perm(t, 0u, first0 ? 0x3210u : 0x2301u);
     }
     store_block<NW>(blk, f16_bits(d), o);
 }
 
-// Load block `qb` of a tile (64 bytes per block in shared memory) with the
-// lane rotation, so a quarter warp reads 8 different 16-byte bank groups.
+// Block `qb` of a tile (64 bytes per block in shared memory) in the rotation
+// (XOR = false) or xor chunk order.
+template <bool XOR>
 __device__ __forceinline__ void load_block(const uint8_t *tile, uint32_t qb, int lane, Block32 &b) {
-    b.c0 = (lane >> 1) & 3;
+    b.c0 = XOR ? (lane >> 1) & 1 : (lane >> 1) & 3;
     const uint8_t *p = tile + static_cast<size_t>(qb) * 64u;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) b.raw[k] = *reinterpret_cast<const uint4 *>(p + 16 * ((b.c0 + k) & 3));
+    for (int k = 0; k < 4; ++k) b.raw[k] = *reinterpret_cast<const uint4 *>(p + 16 * chunk_of<XOR>(b, k));
 }
 
-// One 32-value block of `type` into out_tile (block qb).  F16 blocks are
-// written as 16-byte chunks when out_tile is 16-byte aligned (A16), else as
-// 2-byte halves.
+// One 32-value block of `type`: tile block qb into out_tile block qb.  F16
+// blocks are written as 16-byte chunks when out_tile is 16-byte aligned
+// (A16), else as 2-byte halves.
 template <bool A16 = true>
-__device__ __forceinline__ void quant_block(int type, const Block32 &b, uint8_t *out_tile, uint32_t qb) {
+__device__ __forceinline__ void quant_block(int type, const uint8_t *tile, uint32_t qb, int lane,
+                                            uint8_t *out_tile) {
+    Block32 b;
+    if (type == KVM_TYPE_Q4_0 || type == KVM_TYPE_Q5_0) {
+        load_block<true>(tile, qb, lane, b);
+        if (type == KVM_TYPE_Q4_0) quant_q4q5<false>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ4);
+        else quant_q4q5<true>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ5);
+        return;
+    }
+    load_block<false>(tile, qb, lane, b);
     if (type == KVM_TYPE_Q8_0) {
         quant_q8_0(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ8);
-    } else if (type == KVM_TYPE_Q4_0) {
-        quant_q4q5<false>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ4);
-    } else if (type == KVM_TYPE_Q5_0) {
-        quant_q4q5<true>(b, out_tile + static_cast<size_t>(qb) * kBlockBytesQ5);
     } else {
         uint8_t *o = out_tile + static_cast<size_t>(qb) * 64u;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             if (A16) {
-                *reinterpret_cast<uint4 *>(o + 16 * chunk_of(b, k)) = b.raw[k];
+                *reinterpret_cast<uint4 *>(o + 16 * chunk_of<false>(b, k)) = b.raw[k];
             } else {
                 const uint32_t w[4] = {b.raw[k].x, b.raw[k].y, b.raw[k].z, b.raw[k].w};
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
-                    st_u16(o + 16 * chunk_of(b, k) + 4 * m, w[m] & 0xffffu);
-                    st_u16(o + 16 * chunk_of(b, k) + 4 * m + 2, w[m] >> 16);
+                    st_u16(o + 16 * chunk_of<false>(b, k) + 4 * m, w[m] & 0xffffu);
+                    st_u16(o + 16 * chunk_of<false>(b, k) + 4 * m + 2, w[m] >> 16);
                 }
             }
         }

@@ -610,9 +610,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
         const uint32_t nqb = ts.rows * qb_per_row;
         for (uint32_t qb = static_cast<uint32_t>(warp * 32 + lane); qb < nqb;
              qb += CW * 32u) {
-            Block32 b;
-            load_block(ib, qb, lane, b);
-            quant_block<!DS>(ts.type, b, ob, qb);
+            quant_block<!DS>(ts.type, ib, qb, lane, ob);
         }
         fence_proxy_async_smem();
         __syncwarp();

@@ -167,10 +167,7 @@ void ora_quantize_q8_0(const float *x, int64_t n, uint8_t *y)
         const float *src = x + i * 32;
         uint8_t *blk = y + i * 34;
         float amax = 0.0f;
-        for (int j = 0; j < 32; ++j) {
-            const float a = fabsf(src[j]);
-            amax = amax > a ? amax : a;
-        }
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(src[j]));   /* NaN-blind */
         const float d = amax / 127.0f;
         const float id = d != 0.0f ? 1.0f / d : 0.0f;
         put_f16(blk, d);

@@ -104,6 +104,21 @@ def _edge_rows():
     blk = np.zeros(32, np.float32)
     blk[21], blk[26], blk[0] = -2.578125, -2.75, -2.263671875
     rows.append(np.tile(blk, E // 32).astype(f))
+    # non-finite inputs: the reference's NaN-blind max scans, d = inf / 127
+    # (or vmax = +-inf) with id = 0, and code 0 wherever x * id is NaN
+    base = ((np.arange(E) % 29) - 14).astype(np.float32) * 0.25
+    r = base.copy()
+    r[(np.arange(E // 32) * 32 + (np.arange(E // 32) * 7) % 32)] = np.where(np.arange(E // 32) % 2, np.inf, -np.inf)
+    rows.append(r.astype(f))
+    r = base.copy()
+    r[np.arange(E) % 32 == 3] = np.nan
+    r[np.arange(E) % 64 == 40] = np.nan
+    rows.append(r.astype(f))
+    rows.append(np.full(E, np.nan, f))                                    # all-NaN blocks: d = 0
+    r = np.full(E, np.nan, np.float32)
+    r[np.arange(E) % 32 == 5] = -np.inf
+    r[np.arange(E) % 64 == 9] = 2.0
+    rows.append(r.astype(f))
     return np.stack(rows)
 
 
