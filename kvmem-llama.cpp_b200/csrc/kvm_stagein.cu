@@ -157,10 +157,12 @@ __host__ __device__ inline int stagein_consumer_warps(const StageinArgs &a) {
 // v[2k+1]), so that all butterflies of span >= 2, the cross-lane stages and
 // the quantizer's adds run on sm_100's packed FP32x2 instructions (f2_add_rn,
 // f2_fma_rn: per component the same IEEE operation as the scalar one).  Every
-// product that an add consumes is a scalar __fmul_rn, so its rounding stays.  Every float operation rounds to nearest, so the
-// Hadamard and the quantizers match the CPU bit for bit; RoPE calls the CUDA
-// sincosf (as the reference's GPU kernel does) and agrees with the host cosf /
-// sinf to within their last-bit errors.
+// product that an add consumes is a scalar __fmul_rn, so its rounding stays.
+// Every float operation rounds to nearest, so the Hadamard and the
+// quantizers match the CPU bit for bit.  RoPE turns each pair by the sin and
+// cos of the same float angle as the reference (pos * theta, rounded), from
+// rope_sincos, and agrees with the host cosf / sinf to within their last-bit
+// errors.
 //
 // The Hadamard's scale 1/sqrt(n) is a power of two when log2(n) is even (64,
 // 256, 1024).  Multiplying by a power of two then commutes exactly with every
@@ -336,6 +338,39 @@ __device__ __forceinline__ void fwht_cross_stage(float2 (&P)[16], uint32_t j, ui
     }
 }
 
+// sin and cos of a RoPE angle x (a float, |x| < 2^31), each within 2 ulp of
+// the true value -- the bound CUDA documents for sinf / cosf -- with no slow
+// path for large angles, so every lane runs the same instructions.  The
+// reduction by pi/2 follows Cody and Waite (W. J. Cody, W. Waite, "Software
+// Manual for the Elementary Functions", 1980) in double precision: x is exact
+// as a double, k = rint(x * 2/pi), and r = x - k*pi/2 with pi/2 split into
+// two doubles P1 + P2 (together within 2^-107 of pi/2) through two FMAs, so r
+// is good to about 2^-53 absolute for every such x.  sin r and cos r (|r| at
+// most pi/4 and a rounding) are Taylor polynomials of degree 9 and 10 in
+// single precision (truncation below 2e-9 and 2e-10), and k mod 4 picks the
+// quadrant: x = k*pi/2 + r.
+__device__ __forceinline__ void rope_sincos(float x, float *sn, float *cs) {
+    const double xd = static_cast<double>(x);
+    const double k = rint(xd * 0x1.45f306dc9c883p-1);                              // 2/pi
+    const double rd = fma(-k, 0x1.1a62633145c07p-54, fma(-k, 0x1.921fb54442d18p+0, xd));   // P2, P1
+    const float r = __double2float_rn(rd);
+    const float r2 = __fmul_rn(r, r);
+    float ps = fmaf(r2, 1.0f / 362880.0f, -1.0f / 5040.0f);
+    ps = fmaf(ps, r2, 1.0f / 120.0f);
+    ps = fmaf(ps, r2, -1.0f / 6.0f);
+    const float s = fmaf(ps, __fmul_rn(r2, r), r);
+    float pc = fmaf(r2, -1.0f / 3628800.0f, 1.0f / 40320.0f);
+    pc = fmaf(pc, r2, -1.0f / 720.0f);
+    pc = fmaf(pc, r2, 1.0f / 24.0f);
+    pc = fmaf(pc, r2, -0.5f);
+    const float c = fmaf(pc, r2, 1.0f);
+    const int q = static_cast<int>(static_cast<long long>(k)) & 3;
+    const float s1 = (q & 1) ? c : s;              // sin(r + pi/2) = cos r, cos(r + pi/2) = -sin r
+    const float c1 = (q & 1) ? s : c;
+    *sn = (q & 2) ? -s1 : s1;
+    *cs = ((q + 1) & 2) ? -c1 : c1;
+}
+
 // (sub, j): the lane's unit within the warp and its block within the head;
 // per_warp = 32 / xform units a warp-iteration.
 template <int CW, bool ROPE>
@@ -372,7 +407,7 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
                 const float pos = __uint2float_rn(pos0 + r0 + rr);
                 for (uint32_t i = static_cast<uint32_t>(lane); i < half; i += 32u) {
                     float sn, cs;
-                    sincosf(__fmul_rn(pos, theta_s[i]), &sn, &cs);
+                    rope_sincos(__fmul_rn(pos, theta_s[i]), &sn, &cs);
                     tab[rr * tstride + i + 2u * (i / 32u)] = make_float2(cs, sn);
                 }
             }
@@ -433,12 +468,12 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
 
 // CW consumer warps + the producer.  Resident CTAs per SM: three for the
 // plain kernel (its shared memory allows three; at most 72 registers a
-// thread), two for the transform variants: 7 consumer warps for attn_rot (16
-// warps an SM leave 128 registers a thread, which keep the packed float pairs
-// in place), 8 with RoPE, whose sincosf latencies want the extra warps more.
+// thread) and for attn_rot (7 consumer warps, at most 80 registers a thread:
+// 24 warps an SM measured faster than 16 at 128 registers), two with RoPE (8
+// consumer warps, 96 registers).
 template <int NS, bool XF, int CW, bool ROPE = false>
 __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : kXfMinBlocks) : 3) stagein_kernel(StageinArgs a) {
-    // RoPE tiles are bound by sincosf, not by their stores: that kernel's
+    // RoPE tiles are bound by the angle table and the rotation, not by their stores: that kernel's
     // consumers store the window from registers, which leaves its shared
     // memory to a deeper input pipeline.  The others stage each output tile
     // in shared memory and the producer writes it with one bulk copy.
