@@ -82,6 +82,26 @@ struct PlanArrays {
     int32_t  *cold_to;
 };
 
+// ------------------------------------------------------- division by d --
+// floor(t / d) for a divisor fixed per launch, as a multiply-high by
+// m = ceil(2^32 / d).  With m*d = 2^32 + e, 0 <= e < d, t*m / 2^32 = t/d +
+// t*e / (d*2^32), and the error term stays below 1/d -- so the floor is exact
+// -- whenever t*e < 2^32, in particular whenever t*d <= 2^32.  The task
+// decoders below take this path when every dividend times its divisor is
+// within that bound and divide otherwise.
+struct FastDiv {
+    uint32_t d;
+    uint64_t m;
+};
+
+__device__ __forceinline__ FastDiv make_fastdiv(uint32_t d) {
+    return FastDiv{d, ((1ull << 32) + d - 1u) / d};
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t t, const FastDiv &f) {
+    return static_cast<uint32_t>((static_cast<uint64_t>(t) * f.m) >> 32);
+}
+
 // ------------------------------------------------------------ PTX wrappers --
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -37,16 +37,45 @@ struct TaskDesc {
     bool valid;
 };
 
-__device__ __forceinline__ TaskDesc decode_task(const StageinArgs &a, uint64_t t,
-                                                uint32_t tiles, uint32_t n_items) {
+// Task t of a launch is (item, layer, K|V, tile), tile fastest.  Its three
+// divisions run as multiply-highs (FastDiv) when total * per_item <= 2^32:
+// every dividend times its divisor is then within the bound.
+struct TaskIndex {
+    FastDiv per_item, per_layer, tiles;
+    bool magic;
+};
+
+__device__ __forceinline__ TaskIndex make_task_index(const StageinArgs &a, uint32_t tiles, uint64_t total) {
+    const uint32_t per_layer = a.n_kv * tiles;
+    const uint32_t per_item = a.n_layer * per_layer;
+    TaskIndex ti;
+    ti.per_item = make_fastdiv(per_item);
+    ti.per_layer = make_fastdiv(per_layer);
+    ti.tiles = make_fastdiv(tiles);
+    ti.magic = total < (1ull << 32) && total * per_item <= (1ull << 32);
+    return ti;
+}
+
+__device__ __forceinline__ TaskDesc decode_task(const StageinArgs &a, uint64_t t, const TaskIndex &ti,
+                                                uint32_t n_items) {
     TaskDesc d{nullptr, nullptr, 0u, 0u, 0u, false};
-    const uint64_t per_item = static_cast<uint64_t>(a.n_layer) * a.n_kv * tiles;
-    const uint32_t item = static_cast<uint32_t>(t / per_item);
-    uint32_t r = static_cast<uint32_t>(t % per_item);
-    const uint32_t layer = r / (a.n_kv * tiles);
-    r %= a.n_kv * tiles;
-    const uint32_t kv = r / tiles;
-    const uint32_t tile = r % tiles;
+    uint32_t item, layer, kv, tile;
+    if (ti.magic) {
+        const uint32_t t32 = static_cast<uint32_t>(t);
+        item = fast_div(t32, ti.per_item);
+        uint32_t r = t32 - item * ti.per_item.d;
+        layer = fast_div(r, ti.per_layer);
+        r -= layer * ti.per_layer.d;
+        kv = fast_div(r, ti.tiles);
+        tile = r - kv * ti.tiles.d;
+    } else {
+        item = static_cast<uint32_t>(t / ti.per_item.d);
+        uint32_t r = static_cast<uint32_t>(t % ti.per_item.d);
+        layer = r / ti.per_layer.d;
+        r %= ti.per_layer.d;
+        kv = r / ti.tiles.d;
+        tile = r % ti.tiles.d;
+    }
     if (item >= n_items) return d;
     const uint32_t idx = a.item0 + item;
     const uint32_t block = a.cold_block[idx];
@@ -520,12 +549,16 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
         uint64_t ptask = blockIdx.x;
         uint32_t issued = 0;      // tiles armed with data
         bool ended = false;       // end marker placed
-        // Arm the stage of tile index `issued` with the next task, or with
-        // the end marker when none is left.  Lane 0 only.
+        TaskIndex ti;
+        // Arm the stage of tile index `issued` with this CTA's next valid
+        // task, or with the end marker when none is left.  Lane 0 only.
+        // (Decoding one task ahead, so that a freed stage is refilled without
+        // the decode's global reads, measured faster for q4_0/q5_0 windows but
+        // slower for q8_0, the HBM-bound case.)
         auto arm_next = [&]() {
             const uint32_t s = issued % NS;
             while (ptask < total) {
-                const TaskDesc d = decode_task(a, ptask, tiles, n_items);
+                const TaskDesc d = decode_task(a, ptask, ti, n_items);
                 ptask += gridDim.x;
                 if (!d.valid) continue;
                 if (a.test_skip && blockIdx.x == 0 && issued == 0) {
@@ -547,6 +580,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
             ended = true;
         };
         if (lane == 0) {
+            ti = make_task_index(a, tiles, total);
             while (!ended && issued < static_cast<uint32_t>(NS)) arm_next();
         }
         __syncwarp();   // slot[] written by lane 0 is read by every producer lane

@@ -41,15 +41,52 @@ struct Piece {
     uint32_t bytes;
 };
 
-// Unit u = ((j * L + l) * 2 + kv) * pieces + p.  bytes == 0: nothing to move.
-__device__ __forceinline__ Piece decode_piece(const StageoutArgs &a, uint64_t u, uint32_t pieces) {
+// Unit u = ((j * L + l) * 2 + kv) * pieces + p of a launch of `total` units:
+// (j, l, kv, p) by multiply-highs (FastDiv) when total * max(pieces, L) <= 2^32
+// (every dividend times its divisor is then within the bound), else by
+// division.
+struct UnitIndex {
+    FastDiv pieces, layers;
+    bool magic;
+};
+
+__device__ __forceinline__ UnitIndex make_unit_index(uint32_t pieces, uint32_t n_layer, uint64_t total) {
+    UnitIndex ui;
+    ui.pieces = make_fastdiv(pieces);
+    ui.layers = make_fastdiv(n_layer);
+    ui.magic = total < (1ull << 32) && total * (pieces > n_layer ? pieces : n_layer) <= (1ull << 32);
+    return ui;
+}
+
+struct Unit {
+    uint32_t j, l, kv, p;
+};
+
+__device__ __forceinline__ Unit split_unit(uint64_t u, const UnitIndex &ui) {
+    Unit x;
+    uint32_t r;
+    if (ui.magic) {
+        const uint32_t q = fast_div(static_cast<uint32_t>(u), ui.pieces);
+        x.p = static_cast<uint32_t>(u) - q * ui.pieces.d;
+        x.kv = q & 1u;
+        r = q >> 1;
+        x.j = fast_div(r, ui.layers);
+        x.l = r - x.j * ui.layers.d;
+    } else {
+        x.p = static_cast<uint32_t>(u % ui.pieces.d);
+        const uint64_t q = u / ui.pieces.d;
+        x.kv = static_cast<uint32_t>(q & 1u);
+        x.l = static_cast<uint32_t>((q >> 1) % ui.layers.d);
+        x.j = static_cast<uint32_t>((q >> 1) / ui.layers.d);
+    }
+    return x;
+}
+
+// bytes == 0: nothing to move.
+__device__ __forceinline__ Piece decode_piece(const StageoutArgs &a, uint64_t u, const UnitIndex &ui) {
     Piece pc{nullptr, nullptr, 0u};
-    const uint32_t p = static_cast<uint32_t>(u % pieces);
-    uint64_t r = u / pieces;
-    const uint32_t kv = static_cast<uint32_t>(r & 1u);
-    r >>= 1;
-    const uint32_t l = static_cast<uint32_t>(r % a.n_layer);
-    const uint32_t j = static_cast<uint32_t>(r / a.n_layer);
+    const Unit x = split_unit(u, ui);
+    const uint32_t p = x.p, kv = x.kv, l = x.l, j = x.j;
     const uint32_t b = a.ids[j];
     const bool ok = b < a.n_blocks;
     const int32_t slot = ok ? a.gpu_slot[b] : -1;
@@ -91,24 +128,39 @@ __device__ __forceinline__ void copy_pieces(uint64_t total, bool bulk, uint32_t 
     if (lane != 0) return;
     for (int s = 0; s < kOutStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
+    uint64_t u = blockIdx.x;
+    // the next piece with bytes to move, or false at the end
+    auto next_piece = [&](Piece &pc) {
+        for (; u < total; u += gridDim.x) {
+            pc = decode(u);
+            if (pc.bytes != 0u) {
+                u += gridDim.x;
+                return true;
+            }
+        }
+        return false;
+    };
+    Piece cur{nullptr, nullptr, 0u};
+    bool have = next_piece(cur);
     uint32_t k = 0;
     bool ok = true;
-    for (uint64_t u = blockIdx.x; u < total; u += gridDim.x) {
-        const Piece pc = decode(u);
-        if (pc.bytes == 0) continue;
+    while (have) {
         const uint32_t s = k % kOutStages;
         // the store that last read stage s was issued kOutStages pieces ago
         if (k >= static_cast<uint32_t>(kOutStages)) bulk_wait_read<kOutStages - 1>();
-        mbar_arrive_expect_tx(&full[s], pc.bytes);
-        bulk_g2s(buf + s * kPiece, pc.src, pc.bytes, &full[s]);
+        mbar_arrive_expect_tx(&full[s], cur.bytes);
+        bulk_g2s(buf + s * kPiece, cur.src, cur.bytes, &full[s]);
+        Piece nxt{nullptr, nullptr, 0u};
+        have = next_piece(nxt);           // the next decode (global reads) overlaps this load
         if (!mbar_wait_bounded(&full[s], (k / kOutStages) & 1u)) {
             set_status(status, kErrTimeout);
             ok = false;
             break;
         }
-        bulk_s2g(pc.dst, buf + s * kPiece, pc.bytes);
+        bulk_s2g(cur.dst, buf + s * kPiece, cur.bytes);
         bulk_commit();
         ++k;
+        cur = nxt;
     }
     if (!ok) {
         // bounded wait for the load still landing in this CTA's shared memory
@@ -125,20 +177,17 @@ __device__ __forceinline__ uint32_t pieces_per_span(uint32_t block_tokens, uint3
 __global__ void __launch_bounds__(32) stageout_kernel(StageoutArgs a) {
     const uint32_t pieces = pieces_per_span(a.block_tokens, a.row_bytes_k, a.row_bytes_v);
     const uint64_t total = static_cast<uint64_t>(a.n) * a.n_layer * 2u * pieces;
-    copy_pieces(total, a.bulk != 0u, a.status, [&](uint64_t u) { return decode_piece(a, u, pieces); });
+    const UnitIndex ui = make_unit_index(pieces, a.n_layer, total);
+    copy_pieces(total, a.bulk != 0u, a.status, [&](uint64_t u) { return decode_piece(a, u, ui); });
 }
 
 // Unit u = ((j * L + l) * 2 + kv) * pieces + p over the cold items of this
 // launch: block cold_block[item0 + j]'s rows go to window slot cold_to[...].
 __device__ __forceinline__ Piece decode_packed_in(const PackedInArgs &a, uint32_t n_items, uint64_t u,
-                                                  uint32_t pieces) {
+                                                  const UnitIndex &ui) {
     Piece pc{nullptr, nullptr, 0u};
-    const uint32_t p = static_cast<uint32_t>(u % pieces);
-    uint64_t r = u / pieces;
-    const uint32_t kv = static_cast<uint32_t>(r & 1u);
-    r >>= 1;
-    const uint32_t l = static_cast<uint32_t>(r % a.n_layer);
-    const uint32_t j = static_cast<uint32_t>(r / a.n_layer);
+    const Unit x = split_unit(u, ui);
+    const uint32_t p = x.p, kv = x.kv, l = x.l, j = x.j;
     if (j >= n_items) return pc;
     const uint32_t idx = a.item0 + j;
     const uint32_t b = a.cold_block[idx];
@@ -167,8 +216,9 @@ __global__ void __launch_bounds__(32) packed_stagein_kernel(PackedInArgs a) {
     const uint32_t n_items = min(a.n_items_dev ? *a.n_items_dev : a.n_items_host, a.max_items);
     const uint32_t pieces = pieces_per_span(a.block_tokens, a.row_bytes_k, a.row_bytes_v);
     const uint64_t total = static_cast<uint64_t>(n_items) * a.n_layer * 2u * pieces;
+    const UnitIndex ui = make_unit_index(pieces, a.n_layer, total);
     copy_pieces(total, a.bulk != 0u, a.status,
-                [&](uint64_t u) { return decode_packed_in(a, n_items, u, pieces); });
+                [&](uint64_t u) { return decode_packed_in(a, n_items, u, ui); });
 }
 
 }  // namespace
