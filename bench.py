@@ -280,9 +280,9 @@ def run_kvm(args):
 
     def one_step(i, evs=None):
         sess.reset_window(stream)
-        sess.set_query(qs[i].data_ptr(), qc, stream)
         if evs:
             evs[0].record(stream)
+        sess.set_query(qs[i].data_ptr(), qc, stream)     # a device query: the prep runs here
         sess.score(stream=stream)
         if evs:
             evs[1].record(stream)

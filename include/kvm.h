@@ -327,7 +327,11 @@ kvm_status kvm_query_add(kvm_session *s, kvm_stream stream, uint32_t layer, uint
  * Captured query (harvest_from_host 'q', llama-memory-kvmem.cpp:2157-2173):
  * q_sum [n_layer][n_head_q*head_dim] F32 sums of pre-RoPE Q (host or device
  * pointer), q_count [n_layer] host array of tokens summed (0 = layer has no
- * query and does not vote).
+ * query and does not vote).  Either way q_sum is read in stream order at
+ * this call: a host query is copied; a query in this device's memory (and at
+ * most 64 layers) is read by the query prep, which this call launches on
+ * `stream` (one kernel, no copy), so the following kvm_score starts with the
+ * scorer.  The caller may reuse its buffer for work ordered after the call.
  */
 kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum,
                          const uint32_t *q_count);

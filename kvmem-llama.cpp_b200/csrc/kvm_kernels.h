@@ -262,6 +262,21 @@ struct QueryState {
     float *nq;             // [n_layer][n_head_kv] its squared norm
 };
 
+// kvm_set_query with a device-resident q_sum: the prep reads it in stream
+// order at that call, keeps a copy in QueryState::q_sum (for later
+// kvm_query_add) and takes q_count from the launch parameters.
+constexpr uint32_t kQueryInlineLayers = 64;
+struct QueryLoad {
+    const float *src;                       // [n_layer][n_head_q*head_dim]
+    uint32_t count[kQueryInlineLayers];     // q_count of each layer
+};
+
+// The query prep alone, as the programmatic dependent launch of whatever
+// precedes it on the stream: it waits (griddepcontrol) before it reads
+// `ld.src`, then lets a following scorer start.
+cudaError_t launch_query_load(const QueryState &q, const QueryLoad &ld, uint32_t n_layer, uint32_t n_head_kv,
+                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream);
+
 // -------------------------------------------------------------- scorer --
 struct ScoreArgs {
     SummaryLayout sum;
@@ -285,10 +300,12 @@ struct ScoreArgs {
 };
 
 // The query prep (when `prep`, qv / nq from q_sum for every layer), then the
-// scorer.  After a prep the scorer is a programmatic dependent launch: its
-// CTAs start their summary loads while the prep runs and wait for it
-// (griddepcontrol) before they read the query.
-cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream);
+// scorer.  After a prep -- this one, or launch_query_load as the stream's
+// previous kernel (`after_prep_load`) -- the scorer is a programmatic
+// dependent launch: its CTAs start their summary loads while the prep runs
+// and wait for it (griddepcontrol) before they read the query and q_count.
+cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream,
+                         bool after_prep_load = false);
 cudaError_t launch_reduce_terms(const double *terms, uint32_t n_layers, uint32_t ldt,
                                 uint32_t n_blocks, double *acc, cudaStream_t stream);
 cudaError_t launch_scores_from_sum(const SummaryLayout &s, uint32_t n_blocks, const double *acc,

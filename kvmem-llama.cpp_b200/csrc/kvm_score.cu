@@ -87,19 +87,38 @@ __device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
 // One CTA = (layer, KV head), one thread per channel:
 //   qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq,
 //   invq = 1.0f / (q_count * g); nq[l][h] = sum over d of qv*qv in order.
-__global__ void query_prep_kernel(QueryState q, uint32_t n_head_kv, uint32_t n_head_q, uint32_t head_dim) {
+// With ld.src (kvm_set_query of a device query) the CTA first copies its
+// group's rows -- the last KV head's CTA also any heads past H * g -- into
+// q.q_sum, and q_count comes from the launch parameters.
+__global__ void query_prep_kernel(QueryState q, QueryLoad ld, uint32_t n_head_kv, uint32_t n_head_q,
+                                  uint32_t head_dim) {
     extern __shared__ float qv_s[];
-    pdl_launch_dependents();     // the scorer may start its summary loads now
     const uint32_t l = blockIdx.x;
     const uint32_t h = blockIdx.y;
     const uint32_t D = head_dim;
-    const uint32_t cnt = q.q_count[l];
-    if (cnt == 0) return;        // the scorer skips a layer without query
     const uint32_t g = n_head_kv == 0 ? 1u : n_head_q / n_head_kv;
+    const size_t row0 = static_cast<size_t>(l) * n_head_q * D;
+    uint32_t cnt;
+    if (ld.src) {
+        // the source was written by earlier work on the stream, and a scorer
+        // launched after this prep reads nothing of it before it waits
+        pdl_wait();
+        pdl_launch_dependents();
+        cnt = ld.count[l];
+        if (h == 0 && threadIdx.x == 0) q.q_count[l] = cnt;
+        const uint32_t c0 = h * g;
+        const uint32_t c1 = h + 1u == n_head_kv ? n_head_q : min(n_head_q, c0 + g);
+        for (size_t i = static_cast<size_t>(c0) * D + threadIdx.x; i < static_cast<size_t>(c1) * D; i += blockDim.x)
+            q.q_sum[row0 + i] = ld.src[row0 + i];
+    } else {
+        pdl_launch_dependents();     // the scorer may start its summary loads now
+        cnt = q.q_count[l];
+    }
+    if (cnt == 0) return;        // the scorer skips a layer without query
     const uint32_t gg = g > 1u ? g : 1u;
     const float invq = __fdiv_rn(1.0f, __uint2float_rn(cnt * gg));
     const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
-    const float *qs = q.q_sum + static_cast<size_t>(l) * n_head_q * D + static_cast<size_t>(h) * g * D;
+    const float *qs = (ld.src ? ld.src : q.q_sum) + row0 + static_cast<size_t>(h) * g * D;
     for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
         float qh = 0.0f;
         for (uint32_t g0 = 0; g0 < n_in; g0 += 8u) {
@@ -160,13 +179,14 @@ __global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
     const uint32_t l = a.layer0 + blockIdx.y;
     const uint32_t b = blockIdx.x * kScoreRange + lane;
     const bool mine = b < a.n_blocks;
-    const bool active = a.q_count[l] > 0;
     float4 *ring = reinterpret_cast<float4 *>(sm);                 // [H][S][32]
     float *qv_s = sm + static_cast<size_t>(H) * S * 128u;          // [H][D]
     float *r_s = qv_s + static_cast<size_t>(H) * D;                // [H][32]
     float *nq_s = r_s + H * 32u;                                   // [H]
-    const float inv = (mine && active) ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
-    const bool go = inv != 0.0f;
+    // before the wait only the summaries are read (q_count may still be
+    // written by the prep): loads start for every block with statistics
+    const float inv0 = mine ? a.sum.inv_tok[static_cast<size_t>(l) * ldb + b] : 0.0f;
+    const bool load = inv0 != 0.0f;
 
     // summary vectors of (block b, head h): channel quad c of the head is at
     // vec[c * kSumGroup]; ring stage c % S of this lane at slot[(c % S) * 32]
@@ -175,14 +195,18 @@ __global__ void __launch_bounds__(1024) score_kernel(ScoreArgs a) {
                         ((static_cast<size_t>(l) * (ldb / kSumGroup) + b / kSumGroup) * (a.sum.n_embd / 4u) +
                          (VEC ? h * n4 : 0u)) * kSumGroup + (b % kSumGroup);
     float4 *slot = ring + static_cast<size_t>(h) * S * 32u + lane;
-    if (VEC && go) {
+    if (VEC && load) {
 #pragma unroll
         for (int c = 0; c < S; ++c) {
             if (static_cast<uint32_t>(c) < n4) cp_async16(slot + c * 32, vec + static_cast<size_t>(c) * kSumGroup);
             cp_async_commit();
         }
     }
-    pdl_wait();                  // the query prep's qv / nq are complete
+    pdl_wait();                  // the query prep's qv / nq / q_count are complete
+    const bool active = a.q_count[l] > 0;
+    const float inv = active ? inv0 : 0.0f;
+    const bool go = load && active;
+    if (VEC && load && !active) cp_async_wait<0>();   // a layer without query: drain the ring
     if (active) {
         const float *qg = a.qv + (static_cast<size_t>(l) * H + h) * D;
         for (uint32_t d = lane; d < D; d += 32u) qv_s[h * D + d] = qg[d];
@@ -397,20 +421,32 @@ static cudaError_t launch_score_t(const ScoreArgs &a, bool after_prep, cudaStrea
     return cudaLaunchKernelEx(&cfg, score_kernel<VEC, S>, a);
 }
 
-cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream) {
+cudaError_t launch_query_load(const QueryState &q, const QueryLoad &ld, uint32_t n_layer, uint32_t n_head_kv,
+                              uint32_t n_head_q, uint32_t head_dim, cudaStream_t stream) {
+    if (n_layer == 0 || n_layer > kQueryInlineLayers || n_head_kv == 0 || head_dim == 0 || head_dim > 1024u ||
+        ld.src == nullptr)
+        return cudaErrorInvalidValue;
+    return launch_after_prev(query_prep_kernel, dim3(n_layer, n_head_kv), dim3(head_dim),
+                             static_cast<size_t>(head_dim) * sizeof(float), stream, q, ld, n_head_kv, n_head_q,
+                             head_dim);
+}
+
+cudaError_t launch_score(const ScoreArgs &a, const QueryState *prep, uint32_t n_layer_all, cudaStream_t stream,
+                         bool after_prep_load) {
     if (a.n_blocks == 0 || a.n_layers == 0) return cudaSuccess;
     if (a.n_head_kv == 0 || a.n_head_kv > 32u || a.head_dim == 0 || a.head_dim > 1024u)
         return cudaErrorInvalidValue;
     if (prep) {
         const size_t smem = static_cast<size_t>(a.head_dim) * sizeof(float);
-        query_prep_kernel<<<dim3(n_layer_all, a.n_head_kv), a.head_dim, smem, stream>>>(*prep, a.n_head_kv,
+        const QueryLoad none{};
+        query_prep_kernel<<<dim3(n_layer_all, a.n_head_kv), a.head_dim, smem, stream>>>(*prep, none, a.n_head_kv,
                                                                                           a.n_head_q, a.head_dim);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     // ring depth: kScoreStages vectors a lane while the ring stays within
     // 48 KiB a CTA (up to 8 KV heads), 3 beyond
-    const bool after = prep != nullptr;
+    const bool after = prep != nullptr || after_prep_load;
     if (a.head_dim % 4u != 0u) return launch_score_t<false, 1>(a, after, stream);
     if (a.n_head_kv <= 8u) return launch_score_t<true, kScoreStages>(a, after, stream);
     return launch_score_t<true, 3>(a, after, stream);

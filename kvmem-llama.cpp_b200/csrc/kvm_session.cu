@@ -99,6 +99,11 @@ struct kvm_session {
     kvm_transform xf{};                // stage-in transforms (all zero = off)
     float *d_theta = nullptr;          // RoPE frequencies [head_dim / 2]
     bool q_dirty = false;              // q_sum / q_count changed since the last query prep
+    // kvm_set_query's own prep launch: `launches` right after it and its
+    // stream, so that a scorer launched next on that stream can follow it
+    // as a programmatic dependent launch
+    uint64_t prep_load_mark = ~0ull;
+    cudaStream_t prep_load_stream = nullptr;
     void *d_base = nullptr;            // one allocation for the small arrays
 
     // pinned ring for small host uploads / plan reads
@@ -1229,9 +1234,29 @@ kvm_status kvm_set_query(kvm_session *s, kvm_stream stream, const float *q_sum, 
     DeviceGuard g(s->device);
     cudaStream_t st = as_stream(stream);
     const uint32_t L = s->cfg.n_layer;
+    s->h_q_count.assign(q_count, q_count + L);
+    // A query in this device's memory is read by the prep itself, in stream
+    // order here: no copy or count upload of its own, and the prep runs as
+    // the programmatic dependent launch of the stream's previous kernel.
+    cudaPointerAttributes pa{};
+    const bool known = cudaPointerGetAttributes(&pa, q_sum) == cudaSuccess;
+    if (!known) (void)cudaGetLastError();      // not a CUDA pointer: plain host memory
+    const bool on_device = known && (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) &&
+                           pa.device == s->device;
+    if (on_device && L <= kQueryInlineLayers) {
+        QueryLoad ld{};
+        ld.src = q_sum;
+        for (uint32_t l = 0; l < L; ++l) ld.count[l] = q_count[l];
+        KVM_CUDA(s, launch_query_load(s->q, ld, L, s->cfg.n_head_kv, s->cfg.n_head_q, s->cfg.head_dim, st),
+                 "query prep launch");
+        s->launches++;
+        s->q_dirty = false;
+        s->prep_load_mark = s->launches;
+        s->prep_load_stream = st;
+        return KVM_OK;
+    }
     KVM_CUDA(s, cudaMemcpyAsync(s->q.q_sum, q_sum, sizeof(float) * L * s->cfg.n_head_q * s->cfg.head_dim,
                                 cudaMemcpyDefault, st), "query copy");
-    s->h_q_count.assign(q_count, q_count + L);
     s->q_dirty = true;
     return KVM_OK;
 }
@@ -1258,7 +1283,9 @@ static ScoreArgs score_args(kvm_session *s) {
 // covers every layer; nothing runs when there are no blocks or layers).
 static kvm_status run_score(kvm_session *s, const ScoreArgs &a, bool prep, cudaStream_t st) {
     if (s->n_blocks == 0 || a.n_layers == 0) return KVM_OK;
-    KVM_CUDA(s, launch_score(a, prep ? &s->q : nullptr, s->cfg.n_layer, st), "score launch");
+    // kvm_set_query's prep was this session's last launch, on this stream
+    const bool after_load = !prep && s->launches == s->prep_load_mark && st == s->prep_load_stream;
+    KVM_CUDA(s, launch_score(a, prep ? &s->q : nullptr, s->cfg.n_layer, st, after_load), "score launch");
     s->launches += prep ? 2u : 1u;
     if (prep) s->q_dirty = false;
     return KVM_OK;
