@@ -12,11 +12,14 @@ namespace kvm {
 constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinStages = 3;
 // Transform mode.  attn_rot alone: 7 consumer warps + the producer, three
-// CTAs an SM (80 registers a thread), three stages; with RoPE: 8 + 1 warps,
-// two CTAs an SM (sincosf wants the registers), four stages of input only.
+// CTAs an SM (80 registers a thread), three stages and three output tiles
+// (four stages with two output tiles measured no faster); with RoPE: 8 + 1
+// warps, two CTAs an SM (its sin/cos want the registers), four stages of
+// input only.
 constexpr int kXfConsumerWarps = 7;
 constexpr int kXfMinBlocks = 3;
 constexpr int kXfStages = 3;
+constexpr int kXfOutStages = 3;
 constexpr int kXfRopeWarps = 8;
 constexpr int kXfRopeMinBlocks = 2;
 constexpr int kXfRopeStages = 4;

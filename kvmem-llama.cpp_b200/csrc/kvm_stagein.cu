@@ -132,7 +132,7 @@ struct TileSlot {
 };
 static_assert(sizeof(TileSlot) == 24, "TileSlot");
 
-// Shared memory: [0,192) barriers (full[NS], done[NS], ofree[NS]); [192,512)
+// Shared memory: [0,192) barriers (full[NS], done[NS], ofree[NO]); [192,512)
 // tile slots; then NS input tiles and, except in the RoPE kernel (which
 // stores the window from registers), NS output tiles.
 constexpr uint32_t kStageinBarBytes = 192;
@@ -169,6 +169,12 @@ __host__ __device__ inline uint32_t rope_tab_warp_bytes(const StageinArgs &a) {
 // three stages; the RoPE kernel's stages hold no output tile.
 __host__ __device__ inline int stagein_stages(const StageinArgs &a) {
     return !a.xform ? kStageinStages : (a.rope_n_rot ? kXfRopeStages : kXfStages);
+}
+
+// Output tiles in shared memory: none for the RoPE kernel (it stores from
+// registers), kXfOutStages for attn_rot, one per stage otherwise.
+__host__ __device__ inline int stagein_out_stages(const StageinArgs &a) {
+    return !a.xform ? kStageinStages : (a.rope_n_rot ? 0 : kXfOutStages);
 }
 
 // Consumer warps of a launch (see stagein_kernel).
@@ -507,12 +513,16 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
     // memory to a deeper input pipeline.  The others stage each output tile
     // in shared memory and the producer writes it with one bulk copy.
     constexpr bool DS = XF && ROPE;
-    static_assert(3 * NS * 8 <= kStageinBarBytes && kStageinBarBytes + NS * sizeof(TileSlot) <= kStageinHeader,
+    // output tiles: NO of them (tile j uses out[j % NO]), fewer than the input
+    // stages where shared memory is short
+    constexpr int NO = (XF && !ROPE) ? kXfOutStages : NS;
+    static_assert(NO >= 1 && NO <= NS, "output tiles");
+    static_assert((2 * NS + NO) * 8 <= kStageinBarBytes && kStageinBarBytes + NS * sizeof(TileSlot) <= kStageinHeader,
                   "stage-in header");
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *done = full + NS;
-    uint64_t *ofree = done + NS;   // phase k of ofree[s]: the store of tile s + k*NS has read out[s]
+    uint64_t *ofree = done + NS;   // phase k of ofree[o]: the store of tile o + k*NO has read out[o]
     TileSlot *slot = reinterpret_cast<TileSlot *>(smem + kStageinBarBytes);
     float *theta_s = reinterpret_cast<float *>(smem + kStageinHeader);   // RoPE frequencies
     float2 *rope_tab = reinterpret_cast<float2 *>(smem + kStageinHeader + stagein_theta_bytes(a));
@@ -531,8 +541,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&done[s], CW);
-            mbar_init(&ofree[s], 1);
         }
+        for (int o = 0; o < NO; ++o) mbar_init(&ofree[o], 1);
         fence_mbar_init();
     }
     __syncthreads();   // the only CTA-wide barrier
@@ -597,7 +607,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
                 break;
             }
             const TileSlot ts = slot[s];
-            const uint8_t *ob = out_buf + s * a.tile_out_bytes;
+            const uint8_t *ob = out_buf + (j % NO) * a.tile_out_bytes;
             if (DS) {
                 // the consumers stored this tile from their registers
             } else if (a.bulk_store) {
@@ -611,15 +621,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
                     *reinterpret_cast<uint16_t *>(ts.dst + o) =
                         *reinterpret_cast<const uint16_t *>(ob + o);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&ofree[s]);
+                if (lane == 0) mbar_arrive(&ofree[j % NO]);
             }
             if (lane == 0) {
                 // the consumers are done with in[s]: refill it right away; the
                 // output buffer is released separately through ofree[]
                 if (!ended) arm_next();
-                if (!DS && a.bulk_store && j >= 1) {
-                    bulk_wait_read<1>();                  // the store of tile j - 1 has read its buffer
-                    mbar_arrive(&ofree[(j - 1) % NS]);
+                if (!DS && a.bulk_store) {
+                    // release out[j % NO] as soon as the store of tile j has
+                    // read it (not one tile later, behind the next done wait)
+                    bulk_wait_read<0>();
+                    mbar_arrive(&ofree[j % NO]);
                 }
             }
             __syncwarp();
@@ -657,14 +669,14 @@ __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : 
         }
         const TileSlot ts = slot[s];
         if (ts.rows == 0) break;
-        // out[s] was last written for tile j - NS: its store must have read it
-        if (!DS && j >= static_cast<uint32_t>(NS) && !mbar_wait_bounded(&ofree[s], ((j / NS) - 1u) & 1u)) {
+        // out[j % NO] was last written for tile j - NO: its store must have read it
+        if (!DS && j >= static_cast<uint32_t>(NO) && !mbar_wait_bounded(&ofree[j % NO], ((j / NO) - 1u) & 1u)) {
             set_status(a.status, kErrTimeout);
             break;
         }
         const uint8_t *ib = in_buf + s * a.tile_in_bytes;
         // direct-store kernels write the window itself (2-byte aligned stores)
-        uint8_t *ob = DS ? ts.dst : out_buf + s * a.tile_out_bytes;
+        uint8_t *ob = DS ? ts.dst : out_buf + (j % NO) * a.tile_out_bytes;
         if (XF) {
             const bool is_v = (ts.meta >> 31) != 0u;
             if (is_v ? a.rot_v != 0u : (a.rot_k != 0u || a.rope_n_rot != 0u)) {
@@ -744,8 +756,8 @@ void stagein_set_transform(StageinArgs &a, uint32_t head_dim, uint32_t n_embd, u
 size_t stagein_smem_bytes(const StageinArgs &a) {
     return kStageinHeader + stagein_theta_bytes(a) +
            static_cast<size_t>(stagein_consumer_warps(a)) * rope_tab_warp_bytes(a) +
-           static_cast<size_t>(stagein_stages(a)) *
-               (a.tile_in_bytes + ((a.xform && a.rope_n_rot) ? 0u : a.tile_out_bytes));
+           static_cast<size_t>(stagein_stages(a)) * a.tile_in_bytes +
+           static_cast<size_t>(stagein_out_stages(a)) * a.tile_out_bytes;
 }
 
 
