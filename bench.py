@@ -126,8 +126,8 @@ def load_peak():
 # Reads equal the algorithmic F16 bytes; writes are 97 % of the algorithmic
 # q8_0 bytes (the rest is still in L2 when the kernel ends).
 DRAM_PER_LAUNCH_CONFIG2 = {
-    "stagein_kernel": {"read": 2147734784, "write": 1107444480},
-    "score_kernel": {"read": 134577152, "write": 3422464},
+    "stagein_kernel": {"read": 2147721984, "write": 1106360576},
+    "score_kernel": {"read": 134577152, "write": 3209984},
 }
 
 
