@@ -87,9 +87,10 @@ __device__ __forceinline__ double div_exact_pow2(double x, uint32_t d) {
 // One CTA = (layer, KV head), one thread per channel:
 //   qv[l][h][d] = (sum over the GQA group of q_sum, in group order) * invq,
 //   invq = 1.0f / (q_count * g); nq[l][h] = sum over d of qv*qv in order.
-// With ld.src (kvm_set_query of a device query) the CTA first copies its
+// With ld.src (kvm_set_query of a device query) the CTA also copies its
 // group's rows -- the last KV head's CTA also any heads past H * g -- into
-// q.q_sum, and q_count comes from the launch parameters.
+// q.q_sum, each value as it is summed, and q_count comes from the launch
+// parameters.
 __global__ void query_prep_kernel(QueryState q, QueryLoad ld, uint32_t n_head_kv, uint32_t n_head_q,
                                   uint32_t head_dim) {
     extern __shared__ float qv_s[];
@@ -106,19 +107,24 @@ __global__ void query_prep_kernel(QueryState q, QueryLoad ld, uint32_t n_head_kv
         pdl_launch_dependents();
         cnt = ld.count[l];
         if (h == 0 && threadIdx.x == 0) q.q_count[l] = cnt;
-        const uint32_t c0 = h * g;
-        const uint32_t c1 = h + 1u == n_head_kv ? n_head_q : min(n_head_q, c0 + g);
-        for (size_t i = static_cast<size_t>(c0) * D + threadIdx.x; i < static_cast<size_t>(c1) * D; i += blockDim.x)
-            q.q_sum[row0 + i] = ld.src[row0 + i];
     } else {
         pdl_launch_dependents();     // the scorer may start its summary loads now
         cnt = q.q_count[l];
     }
+    const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
+    if (ld.src) {
+        // rows this CTA does not sum below: all of them for a layer without
+        // query, and the last KV head's heads past H * g
+        const uint32_t c0 = h * g + (cnt == 0 ? 0u : n_in);
+        const uint32_t c1 = h + 1u == n_head_kv ? n_head_q : min(n_head_q, h * g + g);
+        for (size_t i = static_cast<size_t>(c0) * D + threadIdx.x; i < static_cast<size_t>(c1) * D; i += blockDim.x)
+            q.q_sum[row0 + i] = ld.src[row0 + i];
+    }
     if (cnt == 0) return;        // the scorer skips a layer without query
     const uint32_t gg = g > 1u ? g : 1u;
     const float invq = __fdiv_rn(1.0f, __uint2float_rn(cnt * gg));
-    const uint32_t n_in = min(g, n_head_q > h * g ? n_head_q - h * g : 0u);
-    const float *qs = (ld.src ? ld.src : q.q_sum) + row0 + static_cast<size_t>(h) * g * D;
+    const size_t grp = row0 + static_cast<size_t>(h) * g * D;
+    const float *qs = (ld.src ? ld.src : q.q_sum) + grp;
     for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
         float qh = 0.0f;
         for (uint32_t g0 = 0; g0 < n_in; g0 += 8u) {
@@ -127,8 +133,12 @@ __global__ void query_prep_kernel(QueryState q, QueryLoad ld, uint32_t n_head_kv
             for (uint32_t k = 0; k < 8u; ++k)
                 x[k] = g0 + k < n_in ? qs[static_cast<size_t>(g0 + k) * D + d] : 0.0f;
 #pragma unroll
-            for (uint32_t k = 0; k < 8u; ++k)
-                if (g0 + k < n_in) qh = __fadd_rn(qh, x[k]);
+            for (uint32_t k = 0; k < 8u; ++k) {
+                if (g0 + k < n_in) {
+                    qh = __fadd_rn(qh, x[k]);
+                    if (ld.src) q.q_sum[grp + static_cast<size_t>(g0 + k) * D + d] = x[k];   // the kept copy
+                }
+            }
         }
         const float v = __fmul_rn(qh, invq);
         q.qv[(static_cast<size_t>(l) * n_head_kv + h) * D + d] = v;

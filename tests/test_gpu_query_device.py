@@ -73,13 +73,16 @@ def test_device_query_layer_without_query(kvm_lib, oracle):
     assert np.array_equal(dev, om.score(q, qc))
 
 
-def test_device_query_then_query_add(kvm_lib, oracle):
-    """kvm_query_add after a device kvm_set_query adds to the copied sum."""
+@pytest.mark.parametrize("counts", [(1, 1), (2, 0)])
+def test_device_query_then_query_add(kvm_lib, oracle, counts):
+    """kvm_query_add after a device kvm_set_query adds to the copied sum (also
+    of a layer the set query left without tokens)."""
     torch = _torch()
     import kvm
     shape = Shape(n_layer=2, n_blocks=24, block_tokens=32, budget_blocks=6, gen_blocks=2)
     rig = make_rig(shape, seed=67)
-    q, qc = make_query(shape, np.random.default_rng(68))
+    q, _ = make_query(shape, np.random.default_rng(68))
+    qc = np.array(counts, np.uint32)
     rng = np.random.default_rng(69)
     extra = torch.from_numpy(rng.standard_normal((5, shape.n_head_q * shape.head_dim)).astype(np.float32)).cuda()
     rows = kvm.rows_of(extra, shape.n_head_q, shape.head_dim)
