@@ -108,3 +108,34 @@ def test_device_query_many_layers_takes_the_copy_path(kvm_lib, oracle):
     s.set_query(torch.from_numpy(q).cuda().data_ptr(), qc)
     s.score()
     assert np.array_equal(s.scores(), om.score(q, qc))
+
+
+def test_device_query_heads_not_a_multiple_of_kv_heads(kvm_lib, oracle):
+    """n_head_q = 5 over 2 KV heads: the group size is 2 and head 4 is not
+    summed, but it is part of the kept copy that kvm_query_add adds to."""
+    torch = _torch()
+    import kvm
+    shape = Shape(n_layer=2, n_blocks=24, block_tokens=32, n_head_kv=2, n_head_q=5, budget_blocks=6,
+                  gen_blocks=2)
+    rig = make_rig(shape, seed=72)
+    om = OracleModel(rig)
+    q, qc = make_query(shape, np.random.default_rng(73))
+    s = rig.sess
+    host = _scores_host(s, q, qc)
+    s.set_query(torch.from_numpy(q).cuda().data_ptr(), qc)
+    s.score()
+    dev = s.scores()
+    assert np.array_equal(dev, host)
+    assert np.array_equal(dev, om.score(q, qc))
+    # the kept copies of both paths, head 4 included, are the same
+    rng = np.random.default_rng(74)
+    extra = torch.from_numpy(rng.standard_normal((3, shape.n_head_q * shape.head_dim)).astype(np.float32)).cuda()
+    rows = kvm.rows_of(extra, shape.n_head_q, shape.head_dim)
+    s.set_query(q, qc)
+    s.query_add(0, 3, rows)
+    s.score()
+    host2 = s.scores()
+    s.set_query(torch.from_numpy(q).cuda().data_ptr(), qc)
+    s.query_add(0, 3, rows)
+    s.score()
+    assert np.array_equal(s.scores(), host2)
