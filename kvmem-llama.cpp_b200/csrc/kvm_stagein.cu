@@ -14,8 +14,10 @@
 // elected thread writes the tile's quantized rows (contiguous in the window)
 // back with one cp.async.bulk shared->global store.  An input buffer is
 // refilled as soon as its tile is consumed; its output buffer is handed back
-// to the consumers separately (ofree barrier) once the store has read it, so
-// the loads run NSTAGE-1 tiles ahead of the quantizers.  Every wait is bounded.
+// to the consumers separately (ofree barrier) as soon as the store has read
+// it, so the loads run NSTAGE-1 tiles ahead of the quantizers.  The RoPE
+// transform kernel has no output buffers: its consumers store the window
+// from registers.  Every wait is bounded.
 
 #include "kvm_internal.cuh"
 #include "kvm_quant.cuh"
