@@ -11,15 +11,16 @@ namespace kvm {
 
 constexpr int kStageinConsumerWarps = 8;
 constexpr int kStageinStages = 3;
-// Transform mode.  attn_rot alone: 7 consumer warps + the producer, three
-// CTAs an SM (80 registers a thread), three stages and three output tiles
-// (four stages with two output tiles measured no faster); with RoPE: 8 + 1
-// warps, two CTAs an SM (its sin/cos want the registers), four stages of
-// input only.
+// Transform mode.  attn_rot alone: 7 consumer warps + the producer, four
+// CTAs an SM (64 registers a thread, 32 warps an SM), two stages and two
+// output tiles -- measured faster than three CTAs with three and three (80
+// registers) once output tiles are released as soon as their store has read
+// them; with RoPE: 8 + 1 warps, two CTAs an SM (its sin/cos want the
+// registers), four stages of input only.
 constexpr int kXfConsumerWarps = 7;
-constexpr int kXfMinBlocks = 3;
-constexpr int kXfStages = 3;
-constexpr int kXfOutStages = 3;
+constexpr int kXfMinBlocks = 4;
+constexpr int kXfStages = 2;
+constexpr int kXfOutStages = 2;
 constexpr int kXfRopeWarps = 8;
 constexpr int kXfRopeMinBlocks = 2;
 constexpr int kXfRopeStages = 4;

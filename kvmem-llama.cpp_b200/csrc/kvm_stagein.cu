@@ -167,8 +167,8 @@ __host__ __device__ inline uint32_t rope_tab_warp_bytes(const StageinArgs &a) {
     return (a.xform && a.rope_n_rot) ? ((rope_tab_rows(a) * rope_tab_stride(a) * 8u + 127u) & ~127u) : 0u;
 }
 
-// Pipeline depth (measured at config 2): attn_rot at three CTAs an SM fits
-// three stages; the RoPE kernel's stages hold no output tile.
+// Pipeline depth (measured at config 2): attn_rot at four CTAs an SM fits
+// two stages; the RoPE kernel's stages hold no output tile.
 __host__ __device__ inline int stagein_stages(const StageinArgs &a) {
     return !a.xform ? kStageinStages : (a.rope_n_rot ? kXfRopeStages : kXfStages);
 }
@@ -505,9 +505,9 @@ __device__ __forceinline__ void transform_tile(const StageinArgs &a, const TileS
 
 // CW consumer warps + the producer.  Resident CTAs per SM: three for the
 // plain kernel (its shared memory allows three; at most 72 registers a
-// thread) and for attn_rot (7 consumer warps, at most 80 registers a thread:
-// 24 warps an SM measured faster than 16 at 128 registers), two with RoPE (8
-// consumer warps, 96 registers).
+// thread), four for attn_rot (7 consumer warps, at most 64 registers a
+// thread: 32 warps an SM measured faster than 24 at 80 registers and 16 at
+// 128), two with RoPE (8 consumer warps, 96 registers).
 template <int NS, bool XF, int CW, bool ROPE = false>
 __global__ void __launch_bounds__(CW * 32 + 32, XF ? (ROPE ? kXfRopeMinBlocks : kXfMinBlocks) : 3) stagein_kernel(StageinArgs a) {
     // RoPE tiles are bound by the angle table and the rotation, not by their stores: that kernel's
