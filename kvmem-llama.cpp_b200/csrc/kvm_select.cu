@@ -10,13 +10,15 @@
 //
 // One CTA of 1024 threads per session.  The sink/mandatory/recent pins are a
 // short sequential walk (thread 0, exactly the reference's order).  The fill
-// is a radix select: 8 passes of 8-bit digits over an order-preserving 64-bit
-// key of the f64 score find the need-th best score T; every candidate above T
-// is taken, and among candidates equal to T the ones with the highest block
-// ids are taken -- the reference's strict total order (score, id), so the
-// selected set is identical to its nth_element.  -0.0 and +0.0 compare equal
-// as in the reference; NaN scores (undefined behaviour in the reference's
-// comparator) rank below every number.
+// is a radix select over an order-preserving 64-bit key of the f64 score: a
+// one-bit first digit (the key's sign half, counted with the bits the half's
+// keys share), then 8-bit digits below those bits, find the need-th best
+// score T; every candidate above T is taken, and among candidates equal to T
+// the ones with the highest block ids are taken -- the reference's strict
+// total order (score, id), so the selected set is identical to its
+// nth_element.  -0.0 and +0.0 compare equal as in the reference; NaN scores
+// (undefined behaviour in the reference's comparator) rank below every
+// number.
 #include "kvm_diff.cuh"
 #include "kvm_internal.cuh"
 #include "kvm_kernels.h"
@@ -51,10 +53,11 @@ __device__ uint32_t compact_flags(const uint8_t *flags, uint32_t n, uint32_t *ou
 // and a.selected (ascending); returns the selected count to every thread.
 // Called by every thread of a kSelectThreads CTA.
 //
-// The radix select starts at the highest bit in which the smallest and the
-// largest candidate key differ (the bits above it are common to every
-// candidate), then resolves 8 bits a pass.  Histogram counts are aggregated
-// per warp (__match_any_sync: early passes put most keys in one bin), and
+// The radix select first picks the key half (top bit) that holds the
+// threshold, then starts at the highest bit in which two keys of that half
+// differ (the bits above it are common to all of them) and resolves 8 bits a
+// pass.  Histogram counts are aggregated per warp (__match_any_sync: early
+// passes put most keys in one bin), and
 // the histogram is double-buffered so a pass needs two barriers.  The taken
 // candidates and the ascending compaction come out of one block scan: the
 // candidates equal to the threshold key that are taken are the `rem` with the
@@ -62,8 +65,7 @@ __device__ uint32_t compact_flags(const uint8_t *flags, uint32_t n, uint32_t *ou
 static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
     __shared__ uint4 scratch4[kSelectThreads / 32 + 1];
     __shared__ uint32_t hist[2][256];
-    __shared__ uint64_t s_wmin[kSelectThreads / 32];
-    __shared__ uint64_t s_wmax[kSelectThreads / 32];
+    __shared__ uint32_t s_red[9][kSelectThreads / 32];
     __shared__ uint32_t s_kc;
     __shared__ uint32_t s_remaining;
     __shared__ uint64_t s_prefix;
@@ -146,44 +148,67 @@ static __device__ uint32_t select_core(const SelectArgs &a, uint8_t *kept) {
     uint64_t thr = 0ull, msk = 0ull;
     uint32_t rem = 0;
     if (radix) {
-        // smallest and largest candidate key: their common leading bits are
-        // every candidate's
-        uint64_t kmin = ~0ull, kmax = 0ull;
+        // The candidates split by the key's top bit (scores >= 0 above the
+        // negative ones and NaN): the count of the upper half says which half
+        // holds the threshold -- a one-bit first digit -- and the AND and OR
+        // of that half's keys give the leading bits all of its keys share, so
+        // the passes start at the highest bit in which two of them differ.
+        // Word r of a thread: AND / OR (low, high) of the upper half, the same
+        // of the lower half, the upper count.
+        uint64_t and1 = ~0ull, or1 = 0ull, and0 = ~0ull, or0 = 0ull;
+        uint32_t c1 = 0;
         for_keys([&](uint32_t, bool lv, uint64_t k) {
             if (!lv) return;
-            kmin = k < kmin ? k : kmin;
-            kmax = k > kmax ? k : kmax;
+            if (k >> 63) {
+                and1 &= k;
+                or1 |= k;
+                ++c1;
+            } else {
+                and0 &= k;
+                or0 |= k;
+            }
         });
+        uint32_t r[9] = {static_cast<uint32_t>(and1), static_cast<uint32_t>(and1 >> 32),
+                         static_cast<uint32_t>(or1),  static_cast<uint32_t>(or1 >> 32),
+                         static_cast<uint32_t>(and0), static_cast<uint32_t>(and0 >> 32),
+                         static_cast<uint32_t>(or0),  static_cast<uint32_t>(or0 >> 32), c1};
+        auto warp_reduce = [&]() {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const uint64_t a1 = __shfl_xor_sync(0xffffffffu, kmin, o);
-            const uint64_t b1 = __shfl_xor_sync(0xffffffffu, kmax, o);
-            kmin = a1 < kmin ? a1 : kmin;
-            kmax = b1 > kmax ? b1 : kmax;
-        }
+            for (int w = 0; w < 8; w += 4) {
+                r[w] = __reduce_and_sync(0xffffffffu, r[w]);
+                r[w + 1] = __reduce_and_sync(0xffffffffu, r[w + 1]);
+                r[w + 2] = __reduce_or_sync(0xffffffffu, r[w + 2]);
+                r[w + 3] = __reduce_or_sync(0xffffffffu, r[w + 3]);
+            }
+            r[8] = __reduce_add_sync(0xffffffffu, r[8]);
+        };
+        warp_reduce();
         if (lane == 0) {
-            s_wmin[tid >> 5] = kmin;
-            s_wmax[tid >> 5] = kmax;
+#pragma unroll
+            for (int w = 0; w < 9; ++w) s_red[w][tid >> 5] = r[w];
         }
         __syncthreads();
         if (tid < 32) {
-            uint64_t m0 = lane < kSelectThreads / 32 ? s_wmin[lane] : ~0ull;
-            uint64_t m1 = lane < kSelectThreads / 32 ? s_wmax[lane] : 0ull;
+            const bool in = lane < kSelectThreads / 32;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const uint64_t a1 = __shfl_xor_sync(0xffffffffu, m0, o);
-                const uint64_t b1 = __shfl_xor_sync(0xffffffffu, m1, o);
-                m0 = a1 < m0 ? a1 : m0;
-                m1 = b1 > m1 ? b1 : m1;
+            for (int w = 0; w < 9; ++w) {
+                const uint32_t neutral = (w < 8 && (w & 2) == 0) ? ~0u : 0u;   // AND words: all ones
+                r[w] = in ? s_red[w][lane] : neutral;
             }
+            warp_reduce();
             if (lane == 0) {
-                const uint64_t x = m0 ^ m1;
+                const bool upper = r[8] >= need;
+                const int w0 = upper ? 0 : 4;
+                const uint64_t A = (static_cast<uint64_t>(r[w0 + 1]) << 32) | r[w0];
+                const uint64_t O = (static_cast<uint64_t>(r[w0 + 3]) << 32) | r[w0 + 2];
+                const uint64_t x = A ^ O;   // never bit 63: it is the half's own
                 const int hb = x ? 63 - __clzll(static_cast<long long>(x)) : -1;
-                const uint64_t common = hb < 0 ? ~0ull : (hb == 63 ? 0ull : ~((2ull << hb) - 1ull));
-                s_prefix = m0 & common;
+                const uint64_t common = hb < 0 ? ~0ull : ~((2ull << hb) - 1ull);
+                s_prefix = A & common;
                 s_mask = common;
                 s_hi = hb;
-                s_remaining = need;
+                // the lower half: every upper candidate is above the threshold
+                s_remaining = upper ? need : need - r[8];
             }
         }
         __syncthreads();
