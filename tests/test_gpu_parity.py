@@ -209,6 +209,58 @@ def test_select_matches_oracle(kvm_lib, oracle, seed):
         assert np.array_equal(got, want), (trial, n, budget)
 
 
+def _select_vs_oracle(kvm_lib, oracle, n, budget, scores_list, sink=0, recent=0, mand=()):
+    cfg = kvm_lib.default_config(block_tokens=128, select_budget=budget * 128,
+                                 gen_reserve=128, sink_blocks=sink, recent_blocks=recent,
+                                 max_blocks=max(n, 256))
+    s = kvm_lib.Session(cfg, 0)
+    try:
+        s.register_append(n * 128)
+        ocfg = oracle.make_cfg(128, budget, sink, recent)
+        for i, scores in enumerate(scores_list):
+            s.set_scores(scores)
+            s.select(np.asarray(mand, np.uint32))
+            got = s.plan()["selected"]
+            want = oracle.pick_topk(ocfg, scores, np.asarray(mand, np.uint32))
+            assert np.array_equal(got, want), (n, budget, i)
+    finally:
+        s.close()
+
+
+def test_select_around_the_sign_halves(kvm_lib, oracle):
+    """The selection's first digit is the key's sign half: scores >= 0 (+0 and
+    -0 alike) above the negative ones.  The count of non-negative candidates
+    is set to none, need - 1, need, need + 1 and all, so the threshold falls on
+    each side of the split and on its edge, with zeros at the boundary."""
+    rng = np.random.default_rng(31)
+    n, budget = 1500, 200
+    need = budget                                       # no pins: every slot is filled by score
+    cases = []
+    for c1 in (0, need - 1, need, need + 1, n):
+        mag = np.abs(rng.standard_normal(n)) + 1e-3
+        sign = np.full(n, -1.0)
+        sign[rng.permutation(n)[:c1]] = 1.0
+        scores = sign * mag
+        cases.append(scores)
+        z = scores.copy()                               # the smallest non-negative are zeros
+        pos = np.flatnonzero(z >= 0)
+        if pos.size:
+            z[pos[: max(1, pos.size // 4)]] = np.where(rng.random(max(1, pos.size // 4)) < 0.5, 0.0, -0.0)
+        cases.append(z)
+        cases.append(np.round(scores * 2) / 2)          # ties across both halves
+    _select_vs_oracle(kvm_lib, oracle, n, budget, cases)
+
+
+@pytest.mark.parametrize("n", [8193, 20000])
+def test_select_more_blocks_than_cached_keys(kvm_lib, oracle, n):
+    """Above 8192 blocks a thread owns more than its 8 register-cached keys and
+    reads them again on every pass."""
+    rng = np.random.default_rng(n)
+    s0 = rng.standard_normal(n)
+    cases = [s0, np.round(s0 * 4) / 4, np.abs(s0) * 1e-300, -np.abs(s0)]
+    _select_vs_oracle(kvm_lib, oracle, n, 300, cases, sink=1, recent=0, mand=[n - 1, 5])
+
+
 def test_select_empty_and_all_fit(kvm_lib, oracle):
     cfg = kvm_lib.default_config(block_tokens=128, select_budget=128 * 100, max_blocks=256)
     s = kvm_lib.Session(cfg, 0)
