@@ -279,10 +279,21 @@ def test_select_empty_and_all_fit(kvm_lib, oracle):
 
 @pytest.mark.parametrize("imm,osi", [(False, True), (True, True), (False, False)])
 def test_diff_sequence_matches_oracle(kvm_lib, oracle, imm, osi):
-    rng = np.random.default_rng(7 + imm + 2 * osi)
-    n, budget, bt = 200, 40, 32
+    _diff_sequence(kvm_lib, oracle, imm, osi, 200, 40, 7 + imm + 2 * osi)
+
+
+@pytest.mark.parametrize("imm,osi", [(False, True), (True, True)])
+def test_diff_sequence_many_blocks(kvm_lib, oracle, imm, osi):
+    """9000 blocks: each thread of the one-CTA select + diff owns 9 ids, more
+    than the selection's 8 register-cached keys."""
+    _diff_sequence(kvm_lib, oracle, imm, osi, 9000, 300, 17 + imm)
+
+
+def _diff_sequence(kvm_lib, oracle, imm, osi, n, budget, seed):
+    rng = np.random.default_rng(seed)
+    bt = 32
     cfg = kvm_lib.default_config(block_tokens=bt, select_budget=budget * bt, gen_reserve=8 * bt,
-                                 sink_blocks=1, recent_blocks=1, max_blocks=256,
+                                 sink_blocks=1, recent_blocks=1, max_blocks=max(256, n),
                                  immutable_source_k=int(imm), optimize_stage_in=int(osi),
                                  immutable_refresh_remaps=2, immutable_refresh_abs_delta_tokens=bt * 30)
     s = kvm_lib.Session(cfg, 0)
