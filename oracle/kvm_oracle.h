@@ -14,11 +14,13 @@
  *   - mean-K (sum * 1/n): pinned against the compiled RawKvStore.
  *   - quantizers q8_0/q4_0/q5_0: pinned against gguf-py 0.19.0 (which states
  *     bit-exactness with ggml-quants.c) through tests/golden fixtures.
- *   - scorer: "parity unpinned" by any reference test -- the reference scorer
- *     lives in the llama.cpp adapter, which cannot be compiled without the
- *     (absent) llama.cpp submodule, and no reference test pins scores.  The
- *     restatement follows src/adapter/llama-memory-kvmem.cpp:2869-2916 line by
- *     line, compiled with -ffp-contract=off like the reference's x86-64
+ *   - scorer: pinned against the reference's own score_retrieval
+ *     (src/adapter/llama-memory-kvmem.cpp:2869-2916).  The adapter as a whole
+ *     needs the absent llama.cpp submodule, so oracle/Makefile compiles that
+ *     one function, cut from the reference file at build time, inside
+ *     ref_score.cpp against the compiled libkvmem; tests compare live and
+ *     through tests/golden/score_golden.npz.  The restatement follows it line
+ *     by line, compiled with -ffp-contract=off like the reference's x86-64
  *     baseline build (no FMA contraction).
  */
 #ifndef KVM_ORACLE_H

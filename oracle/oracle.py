@@ -3,14 +3,17 @@
 Loads ``oracle/liboracle.so`` (the C restatement of the reference path, built
 from ``oracle/kvm_oracle.c``) and, when present, ``oracle/_ref/libkvmem_ref.so``
 (the reference's own ``kvmem/`` library compiled from its sources plus
-``ref_shim.cpp``).  Only tests, ``__graft_entry__.smoke()`` and ``bench.py``'s
+``ref_shim.cpp``, and the adapter's own ``score_retrieval`` compiled by
+``ref_score.cpp``).  Only tests, ``__graft_entry__.smoke()`` and ``bench.py``'s
 CPU-baseline / ``--impl reference`` legs may import this module; the product
 library never does.
 
 Parity status: selection, diff and mean-K are pinned against the compiled
-reference; quantizers against gguf-py 0.19.0 fixtures; the scorer is a
-line-by-line restatement of src/adapter/llama-memory-kvmem.cpp:2869-2916 that
-no reference test pins ("parity unpinned" for scores).
+reference; quantizers against gguf-py 0.19.0 fixtures; the scorer's
+restatement of src/adapter/llama-memory-kvmem.cpp:2869-2916 against that
+function itself, compiled from the reference file (``ref_score``), and
+through the committed fixture tests/golden/score_golden.npz on machines
+without the reference tree.
 """
 from __future__ import annotations
 
@@ -192,6 +195,8 @@ def ref():
                                     C.c_uint32, C.c_int32, _f32p]
         R.ref_raw_has_block.restype = C.c_int
         R.ref_raw_has_block.argtypes = [C.c_void_p, C.c_uint32]
+        R.ref_score_retrieval.restype = C.c_int
+        R.ref_score_retrieval.argtypes = [C.c_void_p, _f32p, _u32p, _f32p, _u32p, _f64p]
         _ref = R
     return _ref
 
@@ -597,6 +602,32 @@ class RefRaw:
 
     def has_block(self, block_id):
         return bool(ref().ref_raw_has_block(self.h, block_id))
+
+
+class _RefScoreShape(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_blocks", "block_tokens", "n_layer", "n_head_kv", "n_head",
+                                          "head_dim")]
+
+
+def ref_score(sums, mean_tok, q_sum, q_count, n_head_kv, n_head_q, head_dim, block_tokens=128):
+    """Scores [B] (f64) from the reference adapter's own score_retrieval
+    (llama-memory-kvmem.cpp:2869-2916, compiled by ref_score.cpp) over the same
+    inputs as ``score``: sums [L, B, E] f32 block sums of K, mean_tok [L, B]
+    tokens summed (0 = none, at most block_tokens), q_sum [L, Hq*D], q_count [L].
+    A block without statistics in any layer is absent (has_block false)."""
+    sums = np.ascontiguousarray(sums, dtype=np.float32)
+    L_, B = sums.shape[0], sums.shape[1]
+    mt = np.ascontiguousarray(mean_tok, dtype=np.uint32)
+    if mt.size and int(mt.max()) > block_tokens:
+        raise ValueError("mean_tok above block_tokens")
+    shape = _RefScoreShape(B, block_tokens, L_, n_head_kv, n_head_q, head_dim)
+    out = np.zeros(B, dtype=np.float64)
+    rc = ref().ref_score_retrieval(C.byref(shape), sums, mt,
+                                   np.ascontiguousarray(q_sum, dtype=np.float32),
+                                   np.ascontiguousarray(q_count, dtype=np.uint32), out)
+    if rc != 0:
+        raise RuntimeError("reference score_retrieval threw")
+    return out
 
 
 def ref_rope_neox(k: np.ndarray, n_head: int, head_dim: int, n_rot: int, pos0: int,

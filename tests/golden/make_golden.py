@@ -19,6 +19,11 @@ Outputs (all small, committed):
                      kvmem::KvMemStore for seeded random spans, scores, pins
   rope_golden.npz    F32 rows rotated by the reference's own kvmem::rope_neox_apply
                      (full and partial rotary dims, small and 256K-range positions)
+  score_golden.npz   block scores from the reference adapter's own
+                     llama_memory_kvmem::score_retrieval (oracle/ref_score.cpp) for
+                     seeded summaries and queries: GQA 6:1, query heads not a multiple
+                     of the KV heads, layers without query or statistics, partial
+                     blocks, zero and large sums
 
 `python tests/golden/make_golden.py meank_seq` regenerates only the named fixtures.
 """
@@ -229,6 +234,42 @@ def make_groups(rng):
                        cases=cases), f, separators=(",", ":"))
 
 
+SCORE_CASES = (   # n_layer, n_blocks, n_head_kv, n_head_q, head_dim, block_tokens, q_count
+    (3, 40, 4, 24, 64, 128, (1, 2, 0)),
+    (2, 33, 2, 5, 80, 32, (1, 3)),
+    (1, 20, 1, 1, 256, 16, (1,)),
+)
+
+
+def score_case(rng, L, B, Hkv, Hq, D, T, qc):
+    """Summaries, counts and query sums of one scorer case."""
+    E = Hkv * D
+    # K sums as F16 values (what a block sum of F16 rows looks like in scale)
+    sums = (rng.standard_normal((L, B, E)) * 40).astype(np.float16).astype(np.float32)
+    cnt = rng.integers(1, T + 1, (L, B)).astype(np.uint32)
+    cnt[:, 0] = T
+    cnt[:, 1] = 0                    # a block without statistics in any layer
+    cnt[0, 2] = 0                    # statistics missing in one layer only
+    sums[cnt == 0] = 0.0
+    sums[:, 3] = 0.0                 # statistics present, all-zero sums
+    sums[0, 4] *= 1000.0             # large sums
+    q = rng.standard_normal((L, Hq * D)).astype(np.float16).astype(np.float32)
+    return sums, cnt, q, np.array(qc, np.uint32)
+
+
+def make_score(rng):
+    arrays = {}
+    for i, (L, B, Hkv, Hq, D, T, qc) in enumerate(SCORE_CASES):
+        sums, cnt, q, qcount = score_case(rng, L, B, Hkv, Hq, D, T, qc)
+        arrays[f"sums{i}"] = sums
+        arrays[f"cnt{i}"] = cnt
+        arrays[f"q{i}"] = q
+        arrays[f"qc{i}"] = qcount
+        arrays[f"shape{i}"] = np.array([L, B, Hkv, Hq, D, T], np.uint32)
+        arrays[f"scores{i}"] = O.ref_score(sums, cnt, q, qcount, Hkv, Hq, D, T)
+    np.savez_compressed(os.path.join(HERE, "score_golden.npz"), n_cases=len(SCORE_CASES), **arrays)
+
+
 if __name__ == "__main__":
     O.build(ref=True)
     if not O.have_ref():
@@ -245,4 +286,6 @@ if __name__ == "__main__":
         make_rope(np.random.default_rng(20261203))
     if not only or "groups" in only:
         make_groups(np.random.default_rng(20261204))
+    if not only or "score" in only:
+        make_score(np.random.default_rng(20261205))
     print("golden fixtures written to", HERE)

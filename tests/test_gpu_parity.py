@@ -5,6 +5,8 @@ fields, slot layout.  Scores: the device restates the reference arithmetic
 operation for operation, so they are compared bit for bit as well (the
 north-star tolerance of 1e-4 relative is asserted separately as the floor).
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -164,6 +166,29 @@ def test_score_bitexact_uploaded_summaries(kvm_lib, oracle, Hkv, D, Hq):
     assert got.tobytes() == want.tobytes()
     rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
     assert rel.max() <= 1e-4
+
+
+def test_score_matches_reference_golden(kvm_lib):
+    """Device scores equal, bit for bit, the scores that the reference
+    adapter's own score_retrieval (llama-memory-kvmem.cpp:2869-2916, compiled
+    from its file by oracle/Makefile) produced for the same summaries and
+    query sums (tests/golden/score_golden.npz)."""
+    torch = _cuda()
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "score_golden.npz"))
+    for i in range(int(g["n_cases"])):
+        L, B, Hkv, Hq, D, T = (int(x) for x in g[f"shape{i}"])
+        sums, cnt = g[f"sums{i}"], g[f"cnt{i}"]
+        cfg = kvm_lib.default_config(n_layer=L, n_head_kv=Hkv, head_dim=D, n_head_q=Hq,
+                                     max_blocks=128, block_tokens=T, select_budget=T * 8,
+                                     gen_reserve=T * 4)
+        s = kvm_lib.Session(cfg, 0)
+        s.register_append(B * T)
+        for l in range(L):
+            s.upload_summaries(l, 0, sums[l], cnt[l])
+        s.set_query(torch.from_numpy(g[f"q{i}"]).cuda(), g[f"qc{i}"])
+        s.score()
+        assert s.scores().tobytes() == g[f"scores{i}"].tobytes(), i
+        s.close()
 
 
 def test_score_from_summarize_kernel(kvm_lib, oracle):

@@ -6,7 +6,10 @@
     compiled reference when oracle/_ref is present
   * mean-K vs the reference's own RawKvStore (memcmp-exact)
   * the reference's inline store expectations (kvmem/tests/kvmem_store_test.cpp)
-  * the scorer vs an independent numpy restatement (float32 sequential sums)
+  * the scorer vs the reference adapter's own score_retrieval, compiled from
+    its file by oracle/Makefile (live when oracle/_ref is present, and through
+    tests/golden/score_golden.npz everywhere), and vs an independent numpy
+    restatement (float32 sequential sums)
 """
 import json
 import os
@@ -485,3 +488,46 @@ def test_scorer_matches_independent_restatement(oracle):
     assert got[7] == 0.0 and np.all(terms[1] == 0.0)
     mt = oracle.score(sums, cnt, has, q, qc, Hkv, Hq, D, n_threads=4)
     assert mt.tobytes() == got.tobytes()
+
+
+def test_scorer_matches_reference_golden(oracle):
+    """Scores of the reference's own score_retrieval, recorded by
+    tests/golden/make_golden.py, equal the oracle's bit for bit."""
+    g = np.load(os.path.join(GOLD, "score_golden.npz"))
+    for i in range(int(g["n_cases"])):
+        L, B, Hkv, Hq, D, T = (int(x) for x in g[f"shape{i}"])
+        sums, cnt = g[f"sums{i}"], g[f"cnt{i}"]
+        has = (cnt > 0).any(axis=0).astype(np.uint8)
+        got = oracle.score(sums, cnt, has, g[f"q{i}"], g[f"qc{i}"], Hkv, Hq, D)
+        assert got.tobytes() == g[f"scores{i}"].tobytes(), i
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(HERE), "oracle", "_ref",
+                                                    "libkvmem_ref.so")),
+                    reason="reference library not built here")
+def test_scorer_live_vs_reference_function(oracle):
+    """The oracle's scorer against llama_memory_kvmem::score_retrieval itself
+    (llama-memory-kvmem.cpp:2869-2916) on seeded shapes: GQA groups with and
+    without a remainder, head sizes 32-256, partial and missing statistics,
+    layers without query, every layer without query."""
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import score_case
+    rng = np.random.default_rng(31)
+    for it in range(40):
+        L = int(rng.integers(1, 5))
+        B = int(rng.integers(5, 90))
+        Hkv = int(rng.choice([1, 2, 4, 8]))
+        Hq = Hkv * int(rng.integers(1, 7)) + (int(rng.integers(0, Hkv)) if it % 3 == 0 else 0)
+        D = int(rng.choice([32, 64, 80, 128, 256]))
+        T = int(rng.choice([16, 32, 128]))
+        qc = rng.integers(0, 4, L)
+        if it == 7:
+            qc[:] = 0
+        sums, cnt, q, qcount = score_case(rng, L, B, Hkv, Hq, D, T, qc)
+        has = (cnt > 0).any(axis=0).astype(np.uint8)
+        want = oracle.ref_score(sums, cnt, q, qcount, Hkv, Hq, D, T)
+        got = oracle.score(sums, cnt, has, q, qcount, Hkv, Hq, D)
+        assert got.tobytes() == want.tobytes(), (it, L, B, Hkv, Hq, D, T)
+        if it == 7:
+            assert not want.any()
