@@ -501,20 +501,25 @@ def host_cores():
 
 
 def cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref_store=None, blocks=None,
-             sample_blocks=None, q_threads=None):
-    """The reference's CPU reselection on host cores: score_retrieval restated
-    (`threads` threads), pick_topk + set_selection (the reference's own
-    libkvmem when given; single-threaded as in the reference), then the
-    gather of the staged blocks' F16 rows of every layer and their
-    quantization in one call per K/V (`q_threads` threads, default
-    `threads`), on the first `sample_blocks` staged blocks when given and
-    scaled to all.  Returns per-stage seconds."""
+             sample_blocks=None, q_threads=None, ref_scorer=None):
+    """The reference's CPU reselection on host cores: score_retrieval (the
+    reference's own function on one thread when `ref_scorer` is given, as
+    the reference runs it; else the restatement on `threads` threads),
+    pick_topk + set_selection (the reference's own libkvmem when given;
+    single-threaded as in the reference), then the gather of the staged
+    blocks' F16 rows of every layer and their quantization in one call per
+    K/V (`q_threads` threads, default `threads`), on the first
+    `sample_blocks` staged blocks when given and scaled to all.  Returns
+    per-stage seconds."""
     T = c["block_tokens"]
     E = c["n_head_kv"] * c["head_dim"]
     q_threads = threads if q_threads is None else q_threads
     t0 = time.perf_counter()
-    scores = O.score(sums, cnt, has, q, qc, c["n_head_kv"], c["n_head_q"], c["head_dim"],
-                     n_threads=threads)
+    if ref_scorer is not None:
+        scores = ref_scorer.run(q, qc)
+    else:
+        scores = O.score(sums, cnt, has, q, qc, c["n_head_kv"], c["n_head_q"], c["head_dim"],
+                         n_threads=threads)
     t1 = time.perf_counter()
     budget = c["budget_tokens"] // T
     if ref_store is not None:
@@ -562,12 +567,13 @@ def _gather_bufs(pool, n, rb_k, rb_v):
     return _GATHER["bufs"]
 
 
-def cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks, sample_blocks=8):
+def cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks, sample_blocks=8,
+                      ref_scorer=None):
     """The same step on one host thread (the reference runs score_retrieval
     and the quantizer on one thread): full score and select + diff, gather +
     quantize of `sample_blocks` staged blocks scaled to all."""
     r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, 1, ref, blocks,
-                 sample_blocks=sample_blocks, q_threads=1)
+                 sample_blocks=sample_blocks, q_threads=1, ref_scorer=ref_scorer)
     return {"cores": 1, "ms_per_step": round((r["score"] + r["plan"] + r["stagein"]) * 1e3, 2),
             "stage_ms": {k: round(r[k] * 1e3, 2) for k in ("score", "plan", "stagein")},
             "sample": f"score of every block, select+diff, gather+quantize of {r['n_sampled']} of "
@@ -631,11 +637,12 @@ def cpu_baseline(torch, c, hk, hv, qs, qc, sess, n_staged):
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU path (score_retrieval restated,
-    libkvmem select+diff compiled from the reference, CPU quantize of every
-    staged block) on all host cores, same config/metric/unit and the
-    driver's --steps / --warmup; a one-thread step is timed beside it.  Rank
-    0 only."""
+    """--impl reference: the reference's CPU path -- its own score_retrieval
+    (one thread, as the reference runs it) and libkvmem select+diff, both
+    compiled from the reference, then a CPU quantize of every staged block on
+    all host cores -- with the same config/metric/unit and the driver's
+    --steps / --warmup; a one-thread step is timed beside it.  Without the
+    compiled reference the restated scorer runs on all cores.  Rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -647,6 +654,7 @@ def run_reference(args):
     sums, cnt, has, pool_k, pool_v = cpu_inputs(O, c, args.seed)
     threads = host_cores()
     ref = _ref_store(O, c)
+    scorer = O.RefScorer(sums, cnt, c["n_head_kv"], c["n_head_q"], c["head_dim"], T) if ref else None
     blocks = O.Blocks.appended(B * T, T, tier=O.TIER_CPU)
     rng = np.random.default_rng(args.seed + 3)
     qc = np.ones(L, np.uint32)
@@ -654,11 +662,11 @@ def run_reference(args):
     q = None
     for i in range(args.warmup + args.steps):
         q = O.synth_f16(rng, (L, c["n_head_q"] * c["head_dim"]), c["head_dim"]).astype(np.float32)
-        r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref, blocks)
+        r = cpu_step(O, c, sums, cnt, has, q, qc, pool_k, pool_v, threads, ref, blocks, ref_scorer=scorer)
         if i >= args.warmup:
             times.append(r["score"] + r["plan"] + r["stagein"])
             stages.append(r)
-    one = cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks)
+    one = cpu_single_thread(O, c, sums, cnt, has, q, qc, pool_k, pool_v, ref, blocks, ref_scorer=scorer)
     step_s = statistics.mean(times)
     score_b, stage_b, _ = algo_bytes(c, stages[0]["n_staged"])
     v = round((score_b + stage_b) / step_s / 1e9, 3)
@@ -672,11 +680,14 @@ def run_reference(args):
                      for k in ("score", "plan", "stagein")},
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads,
                          "kind": "reference" if ref else "port",
-                         "sample": ("full config-2 steps: restated score_retrieval on "
-                                    f"{threads} threads, the reference's own libkvmem "
-                                    "pick_topk+set_selection (1 thread), gather + CPU q8_0 "
-                                    f"quantization of all 256 staged blocks on {threads} threads; "
-                                    "F16 rows from a 64-block host pool per layer"),
+                         "sample": ("full config-2 steps: "
+                                    + ("the reference's own score_retrieval (1 thread, as the "
+                                       "reference runs it)" if scorer else
+                                       f"restated score_retrieval on {threads} threads")
+                                    + ", the reference's own libkvmem pick_topk+set_selection "
+                                    "(1 thread), gather + CPU q8_0 quantization of all 256 staged "
+                                    f"blocks on {threads} threads; F16 rows from a 64-block host "
+                                    "pool per layer"),
                          "single_thread": one},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)

@@ -197,6 +197,11 @@ def ref():
         R.ref_raw_has_block.argtypes = [C.c_void_p, C.c_uint32]
         R.ref_score_retrieval.restype = C.c_int
         R.ref_score_retrieval.argtypes = [C.c_void_p, _f32p, _u32p, _f32p, _u32p, _f64p]
+        R.ref_scorer_new.restype = C.c_void_p
+        R.ref_scorer_new.argtypes = [C.c_void_p, _f32p, _u32p]
+        R.ref_scorer_free.argtypes = [C.c_void_p]
+        R.ref_scorer_run.restype = C.c_int
+        R.ref_scorer_run.argtypes = [C.c_void_p, _f32p, _u32p, _f64p]
         _ref = R
     return _ref
 
@@ -628,6 +633,36 @@ def ref_score(sums, mean_tok, q_sum, q_count, n_head_kv, n_head_q, head_dim, blo
     if rc != 0:
         raise RuntimeError("reference score_retrieval threw")
     return out
+
+
+class RefScorer:
+    """The reference adapter's own score_retrieval over fixed summaries (the
+    inputs of ``ref_score`` without the query): the summaries are installed
+    once, each ``run`` scores one query on one thread, as the reference does."""
+
+    def __init__(self, sums, mean_tok, n_head_kv, n_head_q, head_dim, block_tokens=128):
+        sums = np.ascontiguousarray(sums, dtype=np.float32)
+        mt = np.ascontiguousarray(mean_tok, dtype=np.uint32)
+        if mt.size and int(mt.max()) > block_tokens:
+            raise ValueError("mean_tok above block_tokens")
+        self.n_layer, self.n_blocks = sums.shape[0], sums.shape[1]
+        shape = _RefScoreShape(self.n_blocks, block_tokens, self.n_layer, n_head_kv, n_head_q, head_dim)
+        self.h = ref().ref_scorer_new(C.byref(shape), sums, mt)
+        if not self.h:
+            raise RuntimeError("reference scorer set-up threw")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().ref_scorer_free(self.h)
+            self.h = None
+
+    def run(self, q_sum, q_count, out=None):
+        out = np.zeros(self.n_blocks, np.float64) if out is None else out
+        rc = ref().ref_scorer_run(self.h, np.ascontiguousarray(q_sum, dtype=np.float32),
+                                  np.ascontiguousarray(q_count, dtype=np.uint32), out)
+        if rc != 0:
+            raise RuntimeError("reference score_retrieval threw")
+        return out
 
 
 def ref_rope_neox(k: np.ndarray, n_head: int, head_dim: int, n_rot: int, pos0: int,
