@@ -13,7 +13,12 @@
  *     inline expectations of kvmem/tests/kvmem_store_test.cpp.
  *   - mean-K (sum * 1/n): pinned against the compiled RawKvStore.
  *   - quantizers q8_0/q4_0/q5_0: pinned against gguf-py 0.19.0 (which states
- *     bit-exactness with ggml-quants.c) through tests/golden fixtures.
+ *     bit-exactness with ggml-quants.c) through tests/golden fixtures; q8_0
+ *     also against the reference's own CUDA quant_q8_0 (bit-exact), q4_0
+ *     against its quant_q4_0, which differs only where nvcc fuses x*id + 8.5f
+ *     (oracle/ref_stagein.cu, tests/test_gpu_ref_kernels.py).
+ *   - Walsh-Hadamard: bit-exact with the reference's own CUDA fwht_kernel<N>
+ *     for N = 64, 128, 256, 512 (same files).
  *   - scorer: pinned against the reference's own score_retrieval
  *     (src/adapter/llama-memory-kvmem.cpp:2869-2916).  The adapter as a whole
  *     needs the absent llama.cpp submodule, so oracle/Makefile compiles that

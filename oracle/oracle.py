@@ -13,7 +13,9 @@ reference; quantizers against gguf-py 0.19.0 fixtures; the scorer's
 restatement of src/adapter/llama-memory-kvmem.cpp:2869-2916 against that
 function itself, compiled from the reference file (``ref_score``), and
 through the committed fixture tests/golden/score_golden.npz on machines
-without the reference tree.
+without the reference tree.  The Walsh-Hadamard transform and q8_0 / q4_0
+against the reference's own CUDA kernels (oracle/_ref/libstagein_ref.so,
+tests/test_gpu_ref_kernels.py).
 """
 from __future__ import annotations
 
