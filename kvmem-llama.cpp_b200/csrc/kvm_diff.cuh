@@ -208,8 +208,11 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
     }
     __syncthreads();   // every entry was read above; now install the layout
 
-    // ---- C: the layout and the header
-    for (uint32_t i = lo; i < hi; ++i) {
+    // ---- C: the layout and the header.  Nothing here depends on order, and
+    // the two loops write disjoint entries (unselected, then selected blocks),
+    // so the threads take them strided: consecutive threads, consecutive
+    // entries, coalesced stores.
+    for (uint32_t i = tid; i < n; i += kDiffThreads) {
         if (now[i]) continue;
         // unselected GPU blocks are staged out (or dropped by the reset)
         const bool gpu = bt.tier[i] == KVM_TIER_GPU;
@@ -217,7 +220,7 @@ static __device__ void diff_core(const DiffArgs &a, uint32_t k, uint8_t *now, ui
         if (gpu) bt.tier[i] = KVM_TIER_CPU;
         bt.gpu_slot[i] = -1;
     }
-    for (uint32_t s = slo; s < shi; ++s) {
+    for (uint32_t s = tid; s < k; s += kDiffThreads) {
         const uint32_t id = sel[s];
         bt.tier[id] = KVM_TIER_GPU;
         bt.gpu_slot[id] = static_cast<int32_t>(s);
